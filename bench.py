@@ -1,0 +1,483 @@
+#!/usr/bin/env python3
+"""Benchmark of the B200 causal-attention engine (one JSON line on rank 0).
+
+Default workload (--config c3-bf16): causal prefill at the 343M trainer
+shape, B=8 H=16 T=1024 d=64, bf16 in/out, the configuration the north-star
+target (>= 60 % of dense tensor-core peak) is quoted on.  Other configs:
+c1 (16-layer fp32 decode), c2 (fp32 prefill d=32), c3-f32, c4-f32 / c4-int8
+(ragged decode), c5-f32 / c5-bf16 (backward).
+
+A step is one call of the path over one batch of synthetic input that is
+already resident in HBM.  Multi-GPU (torchrun, one process per GPU) is weak
+scaling: every rank runs its own full-size batch of (batch x head) units; no
+collective touches the data path.  The per-step device time comes from CUDA
+events around the call on the launching stream; the L2 is flushed between
+steps when the working set fits in it.  `e2e` times the same call through the
+C ABI with the inputs copied from pinned host memory and the output copied
+back inside the timed region.
+
+--impl reference times the reference's own CPU attention (compiled from its
+sources into oracle/_ref/) on a bounded sample of the same workload.
+"""
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "pure-c-llm_b200")
+sys.path.insert(0, PKG)
+sys.path.insert(0, ROOT)
+
+# ---------------------------------------------------------------------------
+# workloads
+# ---------------------------------------------------------------------------
+CONFIGS = {
+    "c1": dict(kind="decode", L=16, H=16, d=32, prior=512, steps=128, kv="f32",
+               workload="C1 KV-cached decode fp32, d_model 512 = 16 x 32, 16 layers, 512 prior rows, 128 steps"),
+    "c2": dict(kind="fwd", B=8, H=16, T=1024, d=32, dtype="f32",
+               workload="C2 causal prefill fp32 B8 H16 T1024 d32"),
+    "c3-f32": dict(kind="fwd", B=8, H=16, T=1024, d=64, dtype="f32",
+                   workload="C3 causal prefill fp32 B8 H16 T1024 d64 (343M shape)"),
+    "c3-bf16": dict(kind="fwd", B=8, H=16, T=1024, d=64, dtype="bf16",
+                    workload="C3 causal prefill bf16 B8 H16 T1024 d64 (343M shape)"),
+    "c4-f32": dict(kind="ragged", n_seq=64, H=16, d=64, max_len=8192, kv="f32",
+                   workload="C4 ragged decode fp32 cache, 64 seqs H16 d64 len~U[1,8192]"),
+    "c4-int8": dict(kind="ragged", n_seq=64, H=16, d=64, max_len=8192, kv="int8",
+                    workload="C4 ragged decode INT8 cache (per-token-head scale), 64 seqs H16 d64 len~U[1,8192]"),
+    "c5-f32": dict(kind="bwd", B=4, H=16, T=4096, d=64, dtype="f32",
+                   workload="C5 causal backward fp32 B4 H16 T4096 d64"),
+    "c5-bf16": dict(kind="bwd", B=4, H=16, T=4096, d=64, dtype="bf16",
+                    workload="C5 causal backward bf16 B4 H16 T4096 d64"),
+}
+L2_BYTES = 126 * 2 ** 20
+# dram__bytes_read.sum + dram__bytes_write.sum per launch of the dominant
+# kernel, from the ncu captures summarised under profiles/ (None until measured)
+TRAFFIC = {}
+
+
+def causal_flops(B, H, T, d):
+    """QK^T and PV over the causal triangle: 4 d flops per (i, j<=i) pair."""
+    return 4.0 * B * H * d * T * (T + 1) / 2
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        p = json.load(open(path))
+        return dict(hbm=p["hbm_gbs"], bf16=p["bf16_tflops"], bf16_sus=p.get("bf16_tflops_sustained"),
+                    src="measured")
+    return dict(hbm=6650.0, bf16=1590.0, bf16_sus=1400.0, src="fallback")
+
+
+# ---------------------------------------------------------------------------
+# clocks sampler (nvidia-smi during the timed region)
+# ---------------------------------------------------------------------------
+class Clocks:
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.path = f"/tmp/attn_clocks_{os.getpid()}.csv"
+
+    def __enter__(self):
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=self.f, stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            self.proc.wait()
+            self.f.close()
+
+    def summary(self):
+        if not self.proc or not os.path.exists(self.path):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
+        rows = [r.split(", ") for r in open(self.path).read().strip().splitlines() if r.count(",") >= 8]
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows]
+        mx = max(float(r[2]) for r in rows)
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].strip() == "Active"})
+        loaded = [s for s, r in zip(sm, rows) if float(r[3]) > 200] or sm
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": mx, "reasons": reasons,
+                "samples": len(rows)}
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the reference's own attention (oracle/_ref), bounded sample
+# ---------------------------------------------------------------------------
+def cpu_reference(cfg, budget_s=12.0):
+    import synth
+    from oracle import oracle as O
+    cores = os.cpu_count() or 1
+    os.environ.setdefault("OMP_NUM_THREADS", str(cores))
+    kind = cfg["kind"]
+    t_end = time.time() + budget_s
+    times = []
+    if kind in ("fwd", "bwd"):
+        B, H, T, d = 1, cfg["H"], cfg["T"], cfg["d"]
+        if kind == "bwd":
+            T = min(T, 1024)
+        q, k, v = (synth.normal(s, (B * T, H * d), 0, 0.5) for s in (1, 2, 3))
+        if kind == "bwd":
+            do = synth.normal(4, (B * T, H * d))
+            _, probs = O.ref_attention_forward(q, k, v, B, T, H, d)
+        while True:
+            t0 = time.perf_counter()
+            if kind == "fwd":
+                O.ref_attention_forward(q, k, v, B, T, H, d)
+            else:
+                O.ref_attention_backward(do, q, k, v, probs, B, T, H, d)
+            times.append(time.perf_counter() - t0)
+            if time.time() > t_end or len(times) >= 50:
+                break
+        work = causal_flops(B, H, T, d) * (2 if kind == "bwd" else 1)
+        value = work / min(times) / 1e12
+        sample = (f"reference train.c attention_{'backward' if kind == 'bwd' else 'forward'} "
+                  f"B={B} H={H} T={T} d={d} (one batch row of the workload), best of {len(times)}")
+        return dict(value=value, unit="TFLOP/s", cores=cores, kind="reference", sample=sample)
+    # decode: the reference's cached_attention, one call per (layer or sequence)
+    H, d = cfg["H"], cfg["d"]
+    if kind == "decode":
+        cap, lens = cfg["prior"] + cfg["steps"], [cfg["prior"] + cfg["steps"] // 2] * 16
+        t_max = 1024
+    else:
+        lens = list(synth.uniform_int(2024, cfg["n_seq"], 1, cfg["max_len"])[:8])
+        cap, t_max = cfg["max_len"], 8192
+    kc = synth.normal(5, (t_max, H * d))
+    vc = synth.normal(6, (t_max, H * d))
+    qv = synth.normal(7, (H * d,))
+    if cfg.get("kv") == "int8":
+        kc = O.dequantize_kv_int8(*O.quantize_kv_int8(kc, H, d), H, d)
+        vc = O.dequantize_kv_int8(*O.quantize_kv_int8(vc, H, d), H, d)
+    bpe = 1 if cfg.get("kv") == "int8" else 4
+    sbytes = 4 if cfg.get("kv") == "int8" else 0
+    while True:
+        t0 = time.perf_counter()
+        for n in lens:
+            O.ref_cached_attention(qv, kc, vc, int(n) - 1, H, d, t_max)
+        times.append(time.perf_counter() - t0)
+        if time.time() > t_end or len(times) >= 50:
+            break
+    nbytes = sum(int(n) * H * (2 * d * bpe + 2 * sbytes) for n in lens) + len(lens) * 2 * H * d * 4
+    value = nbytes / min(times) / 1e9
+    sample = (f"reference transformer.c cached_attention over {len(lens)} caches "
+              f"(H={H} d={d}{', dequantised INT8' if bpe == 1 else ''}), best of {len(times)}")
+    return dict(value=value, unit="GB/s", cores=cores, kind="reference", sample=sample)
+
+
+# ---------------------------------------------------------------------------
+# GPU workloads
+# ---------------------------------------------------------------------------
+class Workload:
+    """Sets up device-resident inputs; step() enqueues one call on `stream`."""
+
+    def __init__(self, cfg, A, torch, dev):
+        self.cfg, self.A, self.torch, self.dev = cfg, A, torch, dev
+        kind = cfg["kind"]
+        g = torch.Generator(device=dev).manual_seed(1234)
+        self.launches = 1
+        if kind in ("fwd", "bwd"):
+            B, H, T, d = cfg["B"], cfg["H"], cfg["T"], cfg["d"]
+            dt = torch.bfloat16 if cfg["dtype"] == "bf16" else torch.float32
+            self.dtype_code = A.BF16 if dt == torch.bfloat16 else A.F32
+            self.esz = 2 if dt == torch.bfloat16 else 4
+            mk = lambda s: (torch.randn((B * T, H * d), generator=g, device=dev) * s).to(dt)
+            self.q, self.k, self.v = mk(0.5), mk(0.5), mk(0.5)
+            self.o = torch.empty_like(self.q)
+            self.lse = torch.empty(B * H * T, device=dev)
+            self.shape = A.Shape(B, H, T, d, 0, 0)
+            self.work = causal_flops(B, H, T, d)
+            self.unit, self.metric = "TFLOP/s", "causal-attn prefill TFLOP/s"
+            self.in_bytes = 3 * B * T * H * d * self.esz
+            self.out_bytes = B * T * H * d * self.esz
+            if kind == "bwd":
+                self.do = mk(1.0)
+                A.fwd_ex(self.shape, self.dtype_code, self.q.data_ptr(), self.k.data_ptr(), self.v.data_ptr(),
+                         self.o.data_ptr(), self.lse.data_ptr(), 0)
+                self.dq, self.dk, self.dv = (torch.empty_like(self.q) for _ in range(3))
+                self.ws_bytes = A.bwd_workspace_bytes(self.shape, self.dtype_code)
+                self.ws = torch.empty(self.ws_bytes, dtype=torch.uint8, device=dev)
+                self.work = 2 * causal_flops(B, H, T, d)
+                self.metric = "causal-attn backward TFLOP/s"
+                self.launches = 3
+                self.in_bytes = 5 * B * T * H * d * self.esz + B * H * T * 4
+                self.out_bytes = 3 * B * T * H * d * self.esz
+            self.working_set = self.in_bytes + self.out_bytes
+        elif kind == "decode":
+            L, H, d, prior, steps = cfg["L"], cfg["H"], cfg["d"], cfg["prior"], cfg["steps"]
+            cap = prior + steps
+            self.kc = [torch.randn((cap, H * d), generator=g, device=dev) for _ in range(L)]
+            self.vc = [torch.randn((cap, H * d), generator=g, device=dev) for _ in range(L)]
+            self.kp = torch.tensor([t.data_ptr() for t in self.kc], dtype=torch.int64, device=dev)
+            self.vp = torch.tensor([t.data_ptr() for t in self.vc], dtype=torch.int64, device=dev)
+            self.qs = torch.randn((steps, L, H * d), generator=g, device=dev)
+            self.outs = torch.empty_like(self.qs)
+            self.lens = torch.tensor([[prior + s + 1] * L for s in range(steps)], dtype=torch.int32, device=dev)
+            self.shape = A.DecodeShape(L, H, d, A.F32, 0, cap, cap)
+            self.ws_bytes = A.decode_workspace_bytes(self.shape)
+            self.ws = torch.zeros(self.ws_bytes, dtype=torch.uint8, device=dev)
+            self.step_idx = 0
+            # bytes of one full 128-step run / 128: K and V rows read + q/out
+            total = sum((prior + s + 1) * L * H * d * 4 * 2 + 2 * L * H * d * 4 for s in range(steps))
+            self.work = total / steps
+            self.unit, self.metric = "GB/s", "KV-decode HBM GB/s"
+            self.in_bytes = L * H * d * 4 + L * 4
+            self.out_bytes = L * H * d * 4
+            self.working_set = self.work
+        else:  # ragged
+            import synth
+            n, H, d, max_len = cfg["n_seq"], cfg["H"], cfg["d"], cfg["max_len"]
+            lens_h = synth.uniform_int(2024, n, 1, max_len)
+            cap = int(lens_h.max())
+            kc = torch.randn((n * cap, H * d), generator=g, device=dev)
+            vc = torch.randn((n * cap, H * d), generator=g, device=dev)
+            self.int8 = cfg["kv"] == "int8"
+            if self.int8:
+                self.kc, self.ks = A.quantize_int8_t(kc, H)
+                self.vc, self.vs = A.quantize_int8_t(vc, H)
+                del kc, vc
+            else:
+                self.kc, self.vc, self.ks, self.vs = kc, vc, None, None
+            self.q = torch.randn((n, H * d), generator=g, device=dev)
+            self.o = torch.empty_like(self.q)
+            self.lens = torch.from_numpy(lens_h).to(dev)
+            self.shape = A.DecodeShape(n, H, d, A.I8 if self.int8 else A.F32, 0, cap, cap)
+            self.ws_bytes = A.decode_workspace_bytes(self.shape)
+            self.ws = torch.zeros(self.ws_bytes, dtype=torch.uint8, device=dev)
+            per_row = H * (2 * d + 2 * 4) if self.int8 else H * d * 4 * 2
+            self.work = float(lens_h.sum()) * per_row + 2 * n * H * d * 4
+            self.unit, self.metric = "GB/s", "KV-decode HBM GB/s"
+            self.in_bytes = n * H * d * 4 + n * 4
+            self.out_bytes = n * H * d * 4
+            self.working_set = self.work
+
+    def step(self, stream):
+        A, c = self.A, self.cfg
+        kind = c["kind"]
+        if kind == "fwd":
+            A.fwd_ex(self.shape, self.dtype_code, self.q.data_ptr(), self.k.data_ptr(), self.v.data_ptr(),
+                     self.o.data_ptr(), self.lse.data_ptr(), stream)
+        elif kind == "bwd":
+            A.bwd_ex(self.shape, self.dtype_code, self.do.data_ptr(), self.q.data_ptr(), self.k.data_ptr(),
+                     self.v.data_ptr(), self.o.data_ptr(), self.lse.data_ptr(), self.dq.data_ptr(),
+                     self.dk.data_ptr(), self.dv.data_ptr(), 0, self.ws.data_ptr(), self.ws_bytes, stream)
+        elif kind == "decode":
+            s = self.step_idx % c["steps"]
+            self.step_idx += 1
+            A.check(A.lib.attn_decode_ptrs_ex(ctypes.byref(self.shape), self.qs[s].data_ptr(), self.kp.data_ptr(),
+                                              self.vp.data_ptr(), None, None, self.lens[s].data_ptr(),
+                                              self.outs[s].data_ptr(), self.ws.data_ptr(), self.ws_bytes, stream))
+        else:
+            A.decode_ex(self.shape, self.q.data_ptr(), self.kc.data_ptr(), self.vc.data_ptr(),
+                        self.ks.data_ptr() if self.int8 else None, self.vs.data_ptr() if self.int8 else None,
+                        self.lens.data_ptr(), self.o.data_ptr(), self.ws.data_ptr(), self.ws_bytes, stream)
+
+    # --- end to end: host inputs -> device -> call -> host output -------------
+    def setup_e2e(self):
+        torch = self.torch
+        kind = self.cfg["kind"]
+        if kind in ("fwd", "bwd"):
+            srcs = [self.q, self.k, self.v] + ([self.do] if kind == "bwd" else [])
+            self.h_in = [t.cpu().pin_memory() for t in srcs]
+            self.d_in = srcs
+            self.h_out = [torch.empty(t.shape, dtype=t.dtype).pin_memory()
+                          for t in ([self.o] if kind == "fwd" else [self.dq, self.dk, self.dv])]
+            self.d_out = [self.o] if kind == "fwd" else [self.dq, self.dk, self.dv]
+        elif kind == "decode":
+            self.h_in = [self.qs[0].cpu().pin_memory()]
+            self.d_in = [self.qs[0]]
+            self.h_out = [torch.empty(self.outs[0].shape).pin_memory()]
+            self.d_out = [self.outs[0]]
+        else:
+            self.h_in = [self.q.cpu().pin_memory()]
+            self.d_in = [self.q]
+            self.h_out = [torch.empty(self.o.shape).pin_memory()]
+            self.d_out = [self.o]
+
+    def e2e_step(self, stream_obj):
+        for h, d in zip(self.h_in, self.d_in):
+            d.copy_(h, non_blocking=True)
+        self.step(stream_obj.cuda_stream)
+        for h, d in zip(self.h_out, self.d_out):
+            h.copy_(d, non_blocking=True)
+
+
+def run_ours(args, cfg):
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    import attn_b200 as A
+
+    wl = Workload(cfg, A, torch, dev)
+    stream = torch.cuda.Stream(device=dev)
+    flush = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device=dev) if wl.working_set < 2 * L2_BYTES \
+        else None
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            if flush is not None:
+                flush.zero_()
+            wl.step(stream.cuda_stream)
+        stream.synchronize()
+        starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        barrier()
+        torch.cuda.synchronize()
+        with Clocks(local) as clk:
+            t_wall = time.perf_counter()
+            for i in range(args.steps):
+                if flush is not None:
+                    flush.zero_()
+                starts[i].record(stream)
+                wl.step(stream.cuda_stream)
+                ends[i].record(stream)
+            stream.synchronize()
+            barrier()
+            torch.cuda.synchronize()
+            t_wall = time.perf_counter() - t_wall
+        step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+        total_ms = sum(step_ms)
+        # end to end through the C ABI with host buffers
+        wl.setup_e2e()
+        for _ in range(max(1, args.warmup // 2)):
+            wl.e2e_step(stream)
+        stream.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        e0.record(stream)
+        for _ in range(args.steps):
+            wl.e2e_step(stream)
+        e1.record(stream)
+        stream.synchronize()
+        e2e_ms = e0.elapsed_time(e1)
+
+    if world > 1:
+        t = torch.tensor([total_ms, e2e_ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms, e2e_ms = t.tolist()
+    clocks = clk.summary()
+
+    res = None
+    if rank == 0:
+        pk = peaks()
+        ms = total_ms / args.steps
+        scale = 1e12 if wl.unit == "TFLOP/s" else 1e9
+        value = world * wl.work * args.steps / (total_ms / 1e3) / scale
+        achieved = wl.work / (ms / 1e3) / scale
+        if wl.unit == "TFLOP/s":
+            peak, bound, punit = pk["bf16"], "tensor", "TFLOP/s"
+        else:
+            peak, bound, punit = pk["hbm"], "hbm", "GB/s"
+        e2e_val = world * wl.work * args.steps / (e2e_ms / 1e3) / scale
+        res = {
+            "metric": wl.metric, "value": round(value, 3), "unit": wl.unit, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": {"f32": "f32", "bf16": "bf16"}.get(cfg.get("dtype", cfg.get("kv", "f32")), "f32")
+            if cfg["kind"] in ("fwd", "bwd") else ("f32 (int8 cache)" if cfg.get("kv") == "int8" else "f32"),
+            "data": "synthetic (seeded normal inputs of the config's shape)",
+            "config": {"workload": cfg["workload"], "config_key": args.config,
+                       "parallelism": f"dp{world} over (batch x head) units, no collective",
+                       "l2": "flushed between steps" if flush is not None else "working set > L2",
+                       "wall_s_timed": round(t_wall, 4)},
+            "roofline": {"bound": bound, "achieved": round(achieved, 2), "peak": peak, "unit": punit,
+                         "frac": round(achieved / peak, 4), "traffic": TRAFFIC.get(args.config),
+                         "peak_source": f"{pk['src']} ({'bf16_tflops burst' if bound == 'tensor' else 'hbm_gbs'})",
+                         "algorithmic_work_per_launch": wl.work},
+            "e2e": {"value": round(e2e_val, 4), "unit": wl.unit,
+                    "h2d_bytes_per_step": wl.in_bytes, "d2h_bytes_per_step": wl.out_bytes},
+            "gpu_launches": wl.launches * args.steps,
+            "clocks": clocks,
+        }
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+    return res
+
+
+def run_reference(args, cfg):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return None
+    try:
+        from oracle import oracle as O
+        if not O.ref_available():
+            return {"impl": "reference", "unavailable": "oracle/_ref not built (reference sources absent at build)"}
+    except Exception as e:  # pragma: no cover
+        return {"impl": "reference", "unavailable": f"oracle import failed: {e}"}
+    budget = max(3.0, min(20.0, 60.0 / max(1, args.steps + args.warmup)))
+    vals = []
+    cb = None
+    for i in range(args.warmup + args.steps):
+        cb = cpu_reference(cfg, budget_s=budget if i >= args.warmup else 0.5)
+        if i >= args.warmup:
+            vals.append(cb["value"])
+    value = statistics.median(vals)
+    cb["value"] = value
+    return {
+        "impl": "reference", "metric": {"fwd": "causal-attn prefill TFLOP/s", "bwd": "causal-attn backward TFLOP/s"}
+        .get(cfg["kind"], "KV-decode HBM GB/s"),
+        "value": round(value, 6), "unit": cb["unit"], "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic (seeded normal inputs of the config's shape)",
+        "config": {"workload": cfg["workload"], "config_key": args.config},
+        "cpu_baseline": cb,
+        "e2e": {"value": round(value, 6), "unit": cb["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="c3-bf16")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    cfg = CONFIGS[args.config]
+    if args.impl == "reference":
+        res = run_reference(args, cfg)
+    else:
+        res = run_ours(args, cfg)
+        if res is not None and int(os.environ.get("WORLD_SIZE", "1")) == 1 and not args.no_cpu_baseline:
+            res["cpu_baseline"] = cpu_reference(cfg)
+    if res is not None:
+        print(json.dumps(res), flush=True)
+
+
+if __name__ == "__main__":
+    main()

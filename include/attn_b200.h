@@ -1,0 +1,227 @@
+/*
+ * attn_b200.h -- C ABI of the B200 causal-attention engine (libattn_b200.so).
+ *
+ * Drop-in boundary for pure-c-llm's attention:
+ *   - attn_fwd / attn_bwd keep the exact signatures, pointer meaning and
+ *     error behaviour of gpu_kernels.h:67-72 (device pointers, shapes from
+ *     compile-time-style defaults, void return, exit(1) on a CUDA error like
+ *     CUDA_CHECK at gpu_kernels.h:34-36), so train_kaggle.cu:155/199 link
+ *     unchanged.
+ *   - attn_cached_attention replaces the static cached_attention of
+ *     transformer.c:203-248 (one query token against cache rows 0..pos).
+ *   - the *_ex entry points take explicit shapes, a stream and a workspace
+ *     and return a status instead of exiting.
+ *
+ * Everything here is plain C: pointers, sizes, ints.  All tensor pointers are
+ * DEVICE pointers unless a comment says otherwise.  A stream argument of NULL
+ * means the legacy default stream, as the reference uses.
+ *
+ * Layout (transformer.h:15-18): an activation is a row-major matrix with one
+ * row per token; head h of a token occupies columns [h*d, (h+1)*d).  Rows are
+ * `row_stride` elements apart (heads*head_dim for a dense tensor, D_MODEL in
+ * the reference).  Token t of batch b is row b*T + t.
+ */
+#ifndef ATTN_B200_H
+#define ATTN_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define ATTN_API __attribute__((visibility("default")))
+#else
+#define ATTN_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st *attn_stream_t;   /* a cudaStream_t */
+
+/* status codes returned by every int-returning entry point */
+enum {
+    ATTN_OK = 0,
+    ATTN_ERR_INVALID = 1,      /* bad pointer, shape, stride or alignment      */
+    ATTN_ERR_UNSUPPORTED = 2,  /* valid request this build has no kernel for   */
+    ATTN_ERR_CUDA = 3,         /* a CUDA runtime/driver call failed            */
+    ATTN_ERR_NOMEM = 4,        /* device allocation failed                     */
+    ATTN_ERR_WORKSPACE = 5,    /* caller workspace smaller than required       */
+    ATTN_ERR_DEVICE = 6        /* a kernel reported an internal error (bounded
+                                  wait expired); see attn_device_error()       */
+};
+
+/* element types of activations / caches */
+enum {
+    ATTN_F32 = 0,    /* float32 storage, float32 arithmetic (the reference's)  */
+    ATTN_BF16 = 1,   /* bf16 storage, bf16 tensor-core products, fp32 accumulate */
+    ATTN_I8 = 2      /* int8 KV cache codes + per-(token, head) fp32 scale      */
+};
+
+/* ------------------------------------------------------------------------
+ * Errors
+ * ---------------------------------------------------------------------- */
+/* Text of the last failure on the calling host thread ("" if none). */
+ATTN_API const char *attn_last_error(void);
+/* Reads and clears the device-side error word of `device` (0 = none).  Bounded
+ * waits inside kernels record a code here instead of hanging. */
+ATTN_API int attn_device_error(int device, int *code_out);
+/* Library version, (major << 16) | minor. */
+ATTN_API int attn_version(void);
+
+/* ------------------------------------------------------------------------
+ * Training attention, drop-in (gpu_kernels.h:66-72)
+ * ---------------------------------------------------------------------- */
+/* Replaces gpu_kernels.h:67 attn_fwd.  Q,K,V,att: (B*T, H*d) fp32 device.
+ * `probs` is the caller's B*H*T*T-float buffer (train_kaggle.cu:123,128); this
+ * library stores the per-row log-sum-exp and a head-major copy of the output
+ * there, which attn_bwd reads back (needs T >= d+1, true at the reference's
+ * T=1024, d=128).  Sets att.  Exits(1) with a message on failure. */
+ATTN_API void attn_fwd(const float *Q, const float *K, const float *V, float *att, float *probs);
+
+/* Replaces gpu_kernels.h:70 attn_bwd.  SETS dQ, dK, dV (like the reference's
+ * cuBLAS path, beta = 0).  `scratch` is the caller's B*H*T*T-float workspace
+ * (train_kaggle.cu:138).  Exits(1) with a message on failure. */
+ATTN_API void attn_bwd(float *dQ, float *dK, float *dV, float *scratch,
+              const float *dAtt, const float *Q, const float *K, const float *V,
+              const float *probs);
+
+/* Shape used by attn_fwd/attn_bwd.  Defaults are gpu_kernels.h:17-31:
+ * B_SIZE 4, N_HEADS 12, T_SIZE 1024, D_HEAD 128 (DIM 1536); a build may
+ * override them with -DATTN_B_SIZE= etc.  Returns ATTN_OK or an error. */
+ATTN_API int attn_set_macro_shape(int batch, int heads, int seq_len, int head_dim);
+
+/* ------------------------------------------------------------------------
+ * Training attention, explicit shapes
+ * ---------------------------------------------------------------------- */
+typedef struct {
+    int batch;                  /* B                                          */
+    int heads;                  /* H (heads handled by this call)             */
+    int seq_len;                /* T                                          */
+    int head_dim;               /* d: 32, 64, 96 or 128                       */
+    long long in_row_stride;    /* elements between rows of Q,K,V,dO (0: H*d) */
+    long long out_row_stride;   /* elements between rows of O,dQ,dK,dV (0: H*d) */
+} attn_shape;
+
+/* Causal forward O = softmax(Q K^T / sqrt(d)) V per (b, h), rows j <= i.
+ * dtype ATTN_F32: fp32 in/out, fp32 arithmetic (train.c:339-370 semantics).
+ * dtype ATTN_BF16: bf16 in/out, tensor-core products, fp32 softmax.
+ * lse (may be NULL): B*H*T floats, [b][h][t] = max + log(sum) of the scaled
+ * scores of row t -- the statistic the backward recomputes P from. */
+ATTN_API int attn_fwd_ex(const attn_shape *s, int dtype,
+                const void *Q, const void *K, const void *V, void *O,
+                float *lse, attn_stream_t stream);
+
+/* Bytes of device workspace attn_bwd_ex needs for this shape. */
+ATTN_API size_t attn_bwd_workspace_bytes(const attn_shape *s, int dtype);
+
+/* Analytic backward (train.c:373-407): dQ, dK, dV from dO, the forward's
+ * inputs, its output O and its lse.  accumulate = 1 adds into dQ/dK/dV as
+ * train.c does; 0 overwrites them as gpu_kernels.cu's attn_bwd does. */
+ATTN_API int attn_bwd_ex(const attn_shape *s, int dtype,
+                const void *dO, const void *Q, const void *K, const void *V,
+                const void *O, const float *lse,
+                void *dQ, void *dK, void *dV, int accumulate,
+                void *workspace, size_t workspace_bytes, attn_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * KV-cached decode (transformer.c:203-248, model.h:42-45)
+ * ---------------------------------------------------------------------- */
+typedef struct {
+    int n_seq;                  /* independent sequences (or layers) per call */
+    int heads;                  /* H                                          */
+    int head_dim;               /* d: 32, 64, 96 or 128                       */
+    int kv_dtype;               /* ATTN_F32 or ATTN_I8                        */
+    long long row_stride;       /* elements between cache rows (0: H*d)      */
+    long long cap;              /* rows allocated per sequence's cache        */
+    int max_len;                /* upper bound of lens[] (<= cap)             */
+} attn_decode_shape;
+
+/* Bytes of device workspace attn_decode_ex / attn_decode_ptrs_ex need. */
+ATTN_API size_t attn_decode_workspace_bytes(const attn_decode_shape *s);
+
+/* Decode one query token per sequence against that sequence's cache rows
+ * 0..lens[s]-1 (lens[s] = pos+1 in transformer.c terms; lens is a DEVICE
+ * int array, each in [1, max_len]; NULL means every sequence attends max_len
+ * rows).
+ *   q, out: n_seq x (H*d) fp32, dense.
+ *   kcache/vcache: sequence s row r at base + (s*cap + r)*row_stride, fp32
+ *     (ATTN_F32) or int8 codes (ATTN_I8).
+ *   kscale/vscale: ATTN_I8 only, fp32 [(s*cap + r)*H + h] (NULL for fp32).
+ * workspace may be NULL: the library then uses a buffer of its own per
+ * device (allocated on first use). */
+ATTN_API int attn_decode_ex(const attn_decode_shape *s, const float *q,
+                   const void *kcache, const void *vcache,
+                   const float *kscale, const float *vscale,
+                   const int *lens, float *out,
+                   void *workspace, size_t workspace_bytes, attn_stream_t stream);
+
+/* Same, with one cache slab per sequence: kptrs/vptrs (and kscales/vscales
+ * for ATTN_I8) are DEVICE arrays of n_seq device pointers, each slab laid out
+ * as cap rows of row_stride elements -- the per-layer KVCache.k[l] slabs of
+ * model.h:42-45. */
+ATTN_API int attn_decode_ptrs_ex(const attn_decode_shape *s, const float *q,
+                        const void *const *kptrs, const void *const *vptrs,
+                        const float *const *kscales, const float *const *vscales,
+                        const int *lens, float *out,
+                        void *workspace, size_t workspace_bytes, attn_stream_t stream);
+
+/* cached_attention (transformer.c:203) with device pointers: one token of one
+ * layer, attends rows 0..pos.  Writes out (H*d).  Uses the library's own
+ * workspace.  Returns a status. */
+ATTN_API int attn_cached_attention(const float *q, const float *kcache, const float *vcache,
+                          float *out, int pos, int heads, int head_dim,
+                          long long row_stride, attn_stream_t stream);
+
+/* INT8 quantiser for caches: the reference's symmetric absmax scheme
+ * (gemm_bench.c:225-236: amax floored at 1e-8, scale = amax/127,
+ * q = lroundf(x/scale) clamped to +-127) applied per (row, head).
+ * x: rows x row_stride fp32; codes: same layout int8; scales: rows x heads. */
+ATTN_API int attn_kv_quantize_int8(const float *x, long long rows, int heads, int head_dim,
+                          long long row_stride, int8_t *codes, float *scales,
+                          attn_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Device KV cache (model.h:42-48, alloc_kv_cache at model.c:27-33 mallocs
+ * host slabs; this one owns device slabs)
+ * ---------------------------------------------------------------------- */
+#define ATTN_MAX_LAYERS 64
+typedef struct {
+    int n_layers, cap, heads, head_dim, kv_dtype;
+    void *k[ATTN_MAX_LAYERS];        /* cap x (heads*head_dim) per layer      */
+    void *v[ATTN_MAX_LAYERS];
+    float *kscale[ATTN_MAX_LAYERS];  /* cap x heads per layer (ATTN_I8 only)  */
+    float *vscale[ATTN_MAX_LAYERS];
+} attn_kv_cache;
+
+ATTN_API int attn_kv_cache_alloc(attn_kv_cache *c, int n_layers, int cap, int heads,
+                        int head_dim, int kv_dtype);
+ATTN_API int attn_kv_cache_free(attn_kv_cache *c);
+/* Writes one token's K and V rows (fp32, H*d each, device) at row `pos` of
+ * `layer`, quantising on append for an ATTN_I8 cache -- the row write of
+ * transformer.c:260-264. */
+ATTN_API int attn_kv_cache_append(attn_kv_cache *c, int layer, int pos,
+                         const float *krow, const float *vrow, attn_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Multi-GPU partitioning by (batch x head) units
+ * ---------------------------------------------------------------------- */
+/* Contiguous split of n_units over `world` ranks: rank gets [*begin, *end). */
+ATTN_API int attn_shard_range(long long n_units, int world, int rank,
+                     long long *begin, long long *end);
+/* Longest-processing-time-first assignment of (seq, head) decode units whose
+ * cost is the cache length: out_rank[s*heads + h] receives the rank,
+ * out_load[r] (may be NULL) the summed length per rank.  Host arrays. */
+ATTN_API int attn_shard_lpt(const int *lens, int n_seq, int heads, int world,
+                   int *out_rank, long long *out_load);
+/* After an all-gather of head shards, staging is [world][B][T][H/world][d];
+ * writes out as (B*T, H*d).  dtype ATTN_F32 or ATTN_BF16. */
+ATTN_API int attn_gather_permute(const void *staging, void *out, int world, int batch,
+                        int seq_len, int heads, int head_dim, int dtype,
+                        attn_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ATTN_B200_H */

@@ -1,0 +1,340 @@
+// decode.cu -- KV-cached decode attention, split over cache rows (sm_100a).
+//
+// Semantics: cached_attention, transformer.c:203-248 -- for every head, one
+// query row scores cache rows 0..len-1 with (q . k_j) / sqrt(d), softmaxes
+// them and sums the value rows.  INT8 caches hold codes plus a per-(row, head)
+// fp32 scale (the absmax scheme of gemm_bench.c:225-236); attention runs over
+// the dequantised values code * scale.
+//
+// Design (HBM-bound; ~0 flops per byte):
+//   * one CTA per (split, head, sequence); a split is a contiguous chunk of
+//     cache rows, sized on the host so the grid covers the 148 SMs several
+//     times over;
+//   * 8 lanes per cache row, each holding head_dim/8 elements, so every warp
+//     load instruction moves four full 128-byte row segments (fp32) and all
+//     bytes of a sector are used; four row batches are loaded before any is
+//     consumed to keep ~16 KB per CTA in flight;
+//   * scores live in shared memory (base-2 domain), block max / sum reduce
+//     with warp shuffles;
+//   * splits of one (sequence, head) are merged by the last CTA to finish
+//     (threadfence + atomic ticket; nobody waits on anybody), which then
+//     re-arms the ticket to zero for the next call.
+#include "common.cuh"
+
+namespace attn {
+
+struct DecodeParams {
+    const float *q;                       // n_seq x H*D
+    const void *kbase, *vbase;            // contiguous caches (kptrs == nullptr)
+    const void *const *kptrs;             // per-sequence slabs (device array)
+    const void *const *vptrs;
+    const float *ksbase, *vsbase;         // INT8 scales, contiguous layout
+    const float *const *ksptrs;           // INT8 scales, per-sequence slabs
+    const float *const *vsptrs;
+    const int *lens;                      // n_seq, device; NULL = max_len for all
+    float *out;                           // n_seq x H*D
+    float *part_o;                        // [n_seq*H][max_splits][D]
+    float *part_ml;                       // [n_seq*H][max_splits][2]
+    unsigned *tickets;                    // [n_seq*H], zero between calls
+    int *err;                             // device error word
+    long long row_stride;                 // elements between cache rows
+    long long cap;                        // rows per sequence (contiguous layout)
+    int H, max_len, max_splits, chunk;
+    float qscale;                         // log2(e) / sqrt(D)
+};
+
+constexpr int kDecThreads = 128;
+constexpr int kLanesPerRow = 8;
+constexpr int kRowsPerPass = kDecThreads / kLanesPerRow;   // 16
+constexpr int kUnroll = 4;
+
+// Per-lane slice of a row: fp32 lanes take float4 groups {sub*4 + 32*k},
+// int8 lanes take D/8 consecutive bytes starting at sub*D/8.
+template <int D, bool I8>
+struct RowSlice {
+    static constexpr int E = D / kLanesPerRow;   // elements per lane
+    float v[E];
+
+    __device__ __forceinline__ void load(const void *row, int sub) {
+        if constexpr (!I8) {
+            const float *r = static_cast<const float *>(row);
+#pragma unroll
+            for (int k = 0; k < E / 4; k++) {
+                float4 x = __ldg(reinterpret_cast<const float4 *>(r + sub * 4 + 32 * k));
+                v[4 * k + 0] = x.x; v[4 * k + 1] = x.y; v[4 * k + 2] = x.z; v[4 * k + 3] = x.w;
+            }
+        } else {
+            const int8_t *r = static_cast<const int8_t *>(row) + sub * E;
+#pragma unroll
+            for (int k = 0; k < E / 4; k++) {
+                uint32_t w = __ldg(reinterpret_cast<const unsigned int *>(r + 4 * k));
+#pragma unroll
+                for (int b = 0; b < 4; b++)
+                    v[4 * k + b] = (float)(int8_t)((w >> (8 * b)) & 0xffu);
+            }
+        }
+    }
+    // element index (within the head) of slot i for lane `sub`
+    static __device__ __forceinline__ int index(int sub, int i) {
+        if constexpr (!I8) return sub * 4 + 32 * (i / 4) + (i % 4);
+        else return sub * E + i;
+    }
+};
+
+template <int D, bool I8>
+__global__ void __launch_bounds__(kDecThreads)
+decode_split_kernel(const DecodeParams p)
+{
+    using Slice = RowSlice<D, I8>;
+    constexpr int E = Slice::E;
+    extern __shared__ float smem[];
+    float *sc = smem;                         // [chunk] scores, then weights
+    float *red = smem + p.chunk;              // [kRowsPerPass * D] partial outputs
+    __shared__ float wred[kDecThreads / 32];
+    __shared__ int last_flag;
+
+    const int split = blockIdx.x, h = blockIdx.y, e = blockIdx.z;
+    int len = p.lens ? p.lens[e] : p.max_len;
+    if (len < 1 || len > p.max_len) {
+        if (split == 0 && threadIdx.x == 0) atomicExch(p.err, 0x100 + (len < 1 ? 1 : 2));
+        len = len < 1 ? 1 : p.max_len;
+    }
+    const int nsplit = (len + p.chunk - 1) / p.chunk;
+    if (split >= nsplit) return;
+    const int r0 = split * p.chunk;
+    const int n = min(len - r0, p.chunk);
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int grp = tid / kLanesPerRow, sub = tid % kLanesPerRow;
+
+    // cache bases for this sequence (element offsets in units of the cache type)
+    const char *kb, *vb;
+    const float *ksb = nullptr, *vsb = nullptr;
+    constexpr int esz = I8 ? 1 : 4;
+    if (p.kptrs) {
+        kb = static_cast<const char *>(p.kptrs[e]);
+        vb = static_cast<const char *>(p.vptrs[e]);
+        if constexpr (I8) { ksb = p.ksptrs[e]; vsb = p.vsptrs[e]; }
+    } else {
+        const long long off = (long long)e * p.cap * p.row_stride;
+        kb = static_cast<const char *>(p.kbase) + off * esz;
+        vb = static_cast<const char *>(p.vbase) + off * esz;
+        if constexpr (I8) {
+            ksb = p.ksbase + (long long)e * p.cap * p.H;
+            vsb = p.vsbase + (long long)e * p.cap * p.H;
+        }
+    }
+    const long long rstride_b = p.row_stride * esz;
+    const long long head_off_b = (long long)h * D * esz;
+
+    // query slice in registers, pre-scaled into the base-2 domain
+    float qv[E];
+    {
+        const float *qh = p.q + (long long)e * p.H * D + h * D;
+#pragma unroll
+        for (int i = 0; i < E; i++) qv[i] = qh[Slice::index(sub, i)] * p.qscale;
+    }
+
+    // ---- pass 1: scores of rows r0 .. r0+n-1 ----------------------------------
+    for (int base = 0; base < n; base += kRowsPerPass * kUnroll) {
+        Slice ks[kUnroll];
+#pragma unroll
+        for (int u = 0; u < kUnroll; u++) {
+            const int r = base + u * kRowsPerPass + grp;
+            if (r < n) ks[u].load(kb + (r0 + r) * rstride_b + head_off_b, sub);
+        }
+#pragma unroll
+        for (int u = 0; u < kUnroll; u++) {
+            const int r = base + u * kRowsPerPass + grp;
+            float acc = 0.f;
+            if (r < n) {
+#pragma unroll
+                for (int i = 0; i < E; i++) acc = fmaf(qv[i], ks[u].v[i], acc);
+            }
+            acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+            acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+            acc += __shfl_xor_sync(0xffffffffu, acc, 4);
+            if (r < n && sub == 0) {
+                if constexpr (I8) acc *= __ldg(ksb + (long long)(r0 + r) * p.H + h);
+                sc[r] = acc;
+            }
+        }
+    }
+    __syncthreads();
+
+    // ---- softmax statistics of the chunk ---------------------------------------
+    float m = -INFINITY;
+    for (int r = tid; r < n; r += kDecThreads) m = fmaxf(m, sc[r]);
+    m = warp_max(m);
+    if (lane == 0) wred[warp] = m;
+    __syncthreads();
+    m = fmaxf(fmaxf(wred[0], wred[1]), fmaxf(wred[2], wred[3]));
+    __syncthreads();
+    float l = 0.f;
+    for (int r = tid; r < n; r += kDecThreads) {
+        const float pr = exp2f(sc[r] - m);
+        l += pr;
+        if constexpr (I8) sc[r] = pr * __ldg(vsb + (long long)(r0 + r) * p.H + h);
+        else sc[r] = pr;
+    }
+    l = warp_sum(l);
+    if (lane == 0) wred[warp] = l;
+    __syncthreads();
+    l = (wred[0] + wred[1]) + (wred[2] + wred[3]);
+
+    // ---- pass 2: weighted sum of value rows -----------------------------------
+    float o[E];
+#pragma unroll
+    for (int i = 0; i < E; i++) o[i] = 0.f;
+    for (int base = 0; base < n; base += kRowsPerPass * kUnroll) {
+        Slice vs[kUnroll];
+#pragma unroll
+        for (int u = 0; u < kUnroll; u++) {
+            const int r = base + u * kRowsPerPass + grp;
+            if (r < n) vs[u].load(vb + (r0 + r) * rstride_b + head_off_b, sub);
+        }
+#pragma unroll
+        for (int u = 0; u < kUnroll; u++) {
+            const int r = base + u * kRowsPerPass + grp;
+            if (r < n) {
+                const float w = sc[r];
+#pragma unroll
+                for (int i = 0; i < E; i++) o[i] = fmaf(w, vs[u].v[i], o[i]);
+            }
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < E; i++) red[grp * D + Slice::index(sub, i)] = o[i];
+    __syncthreads();
+
+    float *out = p.out + (long long)e * p.H * D + h * D;
+    if (nsplit == 1) {
+        const float inv = 1.f / l;
+        for (int c = tid; c < D; c += kDecThreads) {
+            float s = 0.f;
+#pragma unroll
+            for (int g = 0; g < kRowsPerPass; g++) s += red[g * D + c];
+            out[c] = s * inv;
+        }
+        return;
+    }
+
+    // ---- publish this split's partial state, last CTA merges -----------------
+    const long long eh = (long long)e * p.H + h;
+    float *po = p.part_o + (eh * p.max_splits + split) * D;
+    for (int c = tid; c < D; c += kDecThreads) {
+        float s = 0.f;
+#pragma unroll
+        for (int g = 0; g < kRowsPerPass; g++) s += red[g * D + c];
+        po[c] = s;
+    }
+    if (tid == 0) {
+        p.part_ml[(eh * p.max_splits + split) * 2 + 0] = m;
+        p.part_ml[(eh * p.max_splits + split) * 2 + 1] = l;
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+        const unsigned prev = atomicAdd(p.tickets + eh, 1u);
+        last_flag = (prev == (unsigned)(nsplit - 1));
+    }
+    __syncthreads();
+    if (!last_flag) return;
+    __threadfence();
+
+    const float *pml = p.part_ml + eh * p.max_splits * 2;
+    float M = -INFINITY;
+    for (int s = 0; s < nsplit; s++) M = fmaxf(M, __ldcg(pml + 2 * s));
+    float L = 0.f;
+    for (int s = 0; s < nsplit; s++) L += __ldcg(pml + 2 * s + 1) * exp2f(__ldcg(pml + 2 * s) - M);
+    const float invL = 1.f / L;
+    const float *pob = p.part_o + eh * p.max_splits * D;
+    for (int c = tid; c < D; c += kDecThreads) {
+        float acc = 0.f;
+        for (int s = 0; s < nsplit; s++)
+            acc += __ldcg(pob + (long long)s * D + c) * exp2f(__ldcg(pml + 2 * s) - M);
+        out[c] = acc * invL;
+    }
+    if (tid == 0) p.tickets[eh] = 0u;   // re-arm for the next call
+}
+
+}  // namespace attn
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+namespace attn_host {
+
+// Rows per split: enough CTAs to cover the SMs ~8 times, 64-row granularity.
+int decode_chunk(int max_len, long long units) {
+    long long target = 148LL * 8;
+    long long c = ((long long)max_len * units + target - 1) / target;
+    c = (c + 63) / 64 * 64;
+    if (c < 64) c = 64;
+    if (c > 1024) c = 1024;
+    return (int)c;
+}
+
+size_t decode_workspace_bytes(int n_seq, int heads, int head_dim, int max_len) {
+    const int chunk = decode_chunk(max_len, (long long)n_seq * heads);
+    const long long splits = (max_len + chunk - 1) / chunk;
+    const long long eh = (long long)n_seq * heads;
+    size_t b = 0;
+    b += (size_t)eh * splits * head_dim * sizeof(float);   // part_o
+    b += (size_t)eh * splits * 2 * sizeof(float);          // part_ml
+    b = (b + 255) / 256 * 256;
+    b += (size_t)eh * sizeof(unsigned);                    // tickets
+    return (b + 255) / 256 * 256;
+}
+
+struct DecodeLaunch {
+    int n_seq, heads, head_dim, kv_dtype, max_len;
+    long long row_stride, cap;
+    const float *q;
+    const void *kbase, *vbase;
+    const void *const *kptrs, *const *vptrs;
+    const float *ksbase, *vsbase;
+    const float *const *ksptrs, *const *vsptrs;
+    const int *lens;
+    float *out;
+    void *ws;
+    int *err;
+    cudaStream_t stream;
+};
+
+template <int D, bool I8>
+static int launch_decode_t(const DecodeLaunch &L) {
+    using namespace attn;
+    DecodeParams p;
+    const long long eh = (long long)L.n_seq * L.heads;
+    p.chunk = decode_chunk(L.max_len, eh);
+    p.max_splits = (L.max_len + p.chunk - 1) / p.chunk;
+    char *ws = static_cast<char *>(L.ws);
+    size_t o_bytes = (size_t)eh * p.max_splits * D * sizeof(float);
+    size_t ml_bytes = (size_t)eh * p.max_splits * 2 * sizeof(float);
+    p.part_o = reinterpret_cast<float *>(ws);
+    p.part_ml = reinterpret_cast<float *>(ws + o_bytes);
+    p.tickets = reinterpret_cast<unsigned *>(ws + (o_bytes + ml_bytes + 255) / 256 * 256);
+    p.q = L.q; p.kbase = L.kbase; p.vbase = L.vbase; p.kptrs = L.kptrs; p.vptrs = L.vptrs;
+    p.ksbase = L.ksbase; p.vsbase = L.vsbase; p.ksptrs = L.ksptrs; p.vsptrs = L.vsptrs;
+    p.lens = L.lens; p.out = L.out; p.err = L.err;
+    p.row_stride = L.row_stride; p.cap = L.cap; p.H = L.heads; p.max_len = L.max_len;
+    p.qscale = kLog2e / sqrtf((float)D);
+    dim3 grid(p.max_splits, L.heads, L.n_seq);
+    size_t smem = (size_t)(p.chunk + kRowsPerPass * D) * sizeof(float);
+    decode_split_kernel<D, I8><<<grid, kDecThreads, smem, L.stream>>>(p);
+    return check_launch("decode_split_kernel");
+}
+
+int launch_decode(const DecodeLaunch &L) {
+    const bool i8 = L.kv_dtype == ATTN_I8;
+    switch (L.head_dim) {
+        case 32: return i8 ? launch_decode_t<32, true>(L) : launch_decode_t<32, false>(L);
+        case 64: return i8 ? launch_decode_t<64, true>(L) : launch_decode_t<64, false>(L);
+        case 96: return i8 ? launch_decode_t<96, true>(L) : launch_decode_t<96, false>(L);
+        case 128: return i8 ? launch_decode_t<128, true>(L) : launch_decode_t<128, false>(L);
+        default: return set_error(ATTN_ERR_UNSUPPORTED, "decode: head_dim %d not in {32,64,96,128}", L.head_dim);
+    }
+}
+
+}  // namespace attn_host

@@ -1,0 +1,96 @@
+"""The C-ABI library loads here (no GPU), exports every symbol that
+include/attn_b200.h declares, and its host-only logic behaves."""
+import ctypes
+import os
+import re
+
+import numpy as np
+import pytest
+
+from conftest import ROOT
+
+import attn_b200 as A
+
+
+def declared_functions():
+    src = open(os.path.join(ROOT, "include", "attn_b200.h")).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    names = re.findall(r"^\s*ATTN_API\s+(?:const\s+)?[a-z_0-9]+\s*\*?\s*(attn_[a-z_0-9]+)\s*\(", src, flags=re.M)
+    return sorted(set(names))
+
+
+def test_header_declares_the_drop_in_surface():
+    names = declared_functions()
+    for must in ("attn_fwd", "attn_bwd", "attn_fwd_ex", "attn_bwd_ex", "attn_decode_ex",
+                 "attn_cached_attention", "attn_kv_quantize_int8"):
+        assert must in names
+
+
+def test_every_declared_symbol_is_exported_and_bound():
+    for name in declared_functions():
+        assert hasattr(A.lib, name), f"{name} missing from libattn_b200.so"
+        assert name in A.SIGNATURES, f"{name} has no ctypes signature in attn_b200.py"
+
+
+def test_version_and_error_text():
+    assert A.lib.attn_version() >= 1
+    assert isinstance(A.last_error(), str)
+
+
+def test_shard_range_partitions_exactly():
+    for n, world in [(128, 1), (128, 8), (64, 3), (5, 8), (0, 2)]:
+        spans = [A.shard_range(n, world, r) for r in range(world)]
+        assert spans[0][0] == 0 and spans[-1][1] == n
+        for (b0, e0), (b1, e1) in zip(spans, spans[1:]):
+            assert e0 == b1
+        sizes = [e - b for b, e in spans]
+        assert max(sizes) - min(sizes) <= 1
+
+
+def test_shard_range_rejects_bad_rank():
+    with pytest.raises(A.AttnError):
+        A.shard_range(10, 2, 2)
+
+
+def test_shard_lpt_balances_ragged_lengths():
+    import synth
+    lens = synth.uniform_int(7, 64, 1, 8192)
+    ranks, load = A.shard_lpt(lens, 16, 8)
+    assert ranks.shape == (64 * 16,) and set(ranks.tolist()) <= set(range(8))
+    # recompute loads from the assignment
+    per = np.zeros(8, np.int64)
+    for u, r in enumerate(ranks):
+        per[r] += lens[u // 16]
+    assert np.array_equal(per, load)
+    assert per.sum() == lens.sum() * 16
+    # LPT bound: max load <= 4/3 of optimum (>= mean)
+    assert per.max() <= per.mean() * 4 / 3 + lens.max()
+
+
+def test_argument_validation_needs_no_gpu():
+    s = A.Shape(1, 1, 8, 48, 0, 0)                       # unsupported head_dim
+    assert A.lib.attn_fwd_ex(ctypes.byref(s), A.F32, 16, 16, 16, 16, None, None) == A.ERR_UNSUPPORTED
+    assert "head_dim" in A.last_error()
+    s = A.Shape(1, 2, 8, 64, 100, 0)                     # stride < H*d
+    assert A.lib.attn_fwd_ex(ctypes.byref(s), A.F32, 16, 16, 16, 16, None, None) == A.ERR_INVALID
+    s = A.Shape(1, 2, 8, 64, 0, 0)
+    assert A.lib.attn_fwd_ex(ctypes.byref(s), 7, 16, 16, 16, 16, None, None) == A.ERR_UNSUPPORTED
+    assert A.lib.attn_set_macro_shape(4, 12, 64, 128) == A.ERR_UNSUPPORTED   # T < d+1
+    ds = A.DecodeShape(1, 16, 32, A.F32, 0, 10, 20)     # cap < max_len
+    assert A.lib.attn_decode_ex(ctypes.byref(ds), 16, 16, 16, None, None, None, 16, None, 0, None) == A.ERR_INVALID
+    ds = A.DecodeShape(1, 16, 32, A.I8, 0, 64, 64)      # int8 without scales
+    assert A.lib.attn_decode_ex(ctypes.byref(ds), 16, 16, 16, None, None, None, 16, None, 0, None) == A.ERR_INVALID
+
+
+def test_workspace_sizes():
+    s = A.Shape(4, 16, 4096, 64, 0, 0)
+    assert A.bwd_workspace_bytes(s, A.F32) >= 2 * 4 * 16 * 4096 * 4
+    ds = A.DecodeShape(64, 16, 64, A.F32, 0, 8192, 8192)
+    assert A.decode_workspace_bytes(ds) > 64 * 16 * 4
+
+
+def test_drop_in_probs_buffer_is_large_enough_at_reference_shape():
+    # gpu_kernels.h: B=4, H=12, T=1024, d=128; probs holds lse + a copy of att
+    B, H, T, d = 4, 12, 1024, 128
+    assert B * H * T * T >= B * H * T + B * T * H * d
+    assert A.lib.attn_set_macro_shape(B, H, T, d) == A.OK

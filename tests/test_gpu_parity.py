@@ -1,0 +1,396 @@
+"""CUDA path vs the oracle and the reference-generated fixtures, through the
+C ABI.  Tolerances (max|out-ref| / max|ref|): 1e-5 for fp32 arithmetic and
+for attention over a dequantised INT8 cache; 2e-2 (forward) and 3e-2
+(backward) for bf16 tensor-core products against fp32 over the same
+bf16-rounded inputs; bit-exact for the INT8 quantiser."""
+import ctypes
+
+import numpy as np
+import pytest
+
+from conftest import golden, rel_err
+from oracle import oracle as O
+import synth
+
+pytestmark = pytest.mark.gpu
+
+F32_TOL = 1e-5
+BF16_FWD_TOL = 2e-2
+BF16_BWD_TOL = 3e-2
+
+
+@pytest.fixture(scope="module")
+def A(cuda):
+    import attn_b200
+    return attn_b200
+
+
+def dev(x, dtype=None):
+    import torch
+    t = torch.from_numpy(np.ascontiguousarray(x)).cuda()
+    return t.to(dtype) if dtype is not None else t
+
+
+def host(t):
+    import torch
+    return t.float().cpu().numpy() if t.dtype == torch.bfloat16 else t.cpu().numpy()
+
+
+def bf16_round(x):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(x)).to(torch.bfloat16).float().numpy()
+
+
+def qkv(seed, B, T, H, d, std=0.5):
+    return (synth.normal(seed, (B * T, H * d), 0, std), synth.normal(seed + 1, (B * T, H * d), 0, std),
+            synth.normal(seed + 2, (B * T, H * d), 0, std))
+
+
+# ---------------------------------------------------------------------------
+# forward
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("name", ["fwd_h4_d32", "fwd_h2_d64", "fwd_h2_d128", "fwd_h2_d96", "fwd_t1"])
+def test_forward_f32_golden(A, name):
+    z = golden(name)
+    B, T, H, d = (int(x) for x in z["shape"])
+    out, lse = A.forward_t(dev(z["q"]), dev(z["k"]), dev(z["v"]), H, B)
+    assert rel_err(host(out), z["att"]) < F32_TOL
+    probs = O.lse_to_probs(z["q"], z["k"], host(lse).reshape(B, H, T), B, T, H, d)
+    assert rel_err(probs, z["probs"]) < F32_TOL
+
+
+@pytest.mark.parametrize("B,T,H,d", [(2, 130, 3, 32), (1, 200, 2, 64), (1, 77, 2, 96), (1, 129, 2, 128),
+                                     (1, 64, 1, 64), (3, 1, 2, 32), (1, 256, 4, 64)])
+def test_forward_f32_vs_oracle(A, B, T, H, d):
+    q, k, v = qkv(11 * T + d, B, T, H, d)
+    ref, _, rlse = O.attn_forward(q, k, v, B, T, H, d)
+    out, lse = A.forward_t(dev(q), dev(k), dev(v), H, B)
+    assert rel_err(host(out), ref) < F32_TOL
+    assert rel_err(host(lse), rlse.reshape(-1)) < F32_TOL
+
+
+@pytest.mark.parametrize("B,T,H,d", [(2, 130, 3, 32), (1, 300, 2, 64), (1, 129, 2, 128), (2, 1024, 2, 64),
+                                     (1, 77, 2, 96), (1, 5, 1, 64)])
+def test_forward_bf16_vs_fp32_oracle(A, B, T, H, d):
+    import torch
+    q, k, v = (bf16_round(x) for x in qkv(7 * T + d, B, T, H, d))
+    ref, _, rlse = O.attn_forward(q, k, v, B, T, H, d)
+    out, lse = A.forward_t(dev(q, torch.bfloat16), dev(k, torch.bfloat16), dev(v, torch.bfloat16), H, B)
+    assert out.dtype == torch.bfloat16
+    assert rel_err(host(out), ref) < BF16_FWD_TOL
+    assert np.abs(host(lse) - rlse.reshape(-1)).max() < 0.05
+
+
+def test_forward_strided_heads_subset(A):
+    """A call may cover a head slice of wider rows (the per-rank shard of a
+    multi-GPU split): in/out strides larger than H*d."""
+    import torch
+    B, T, H, d = 2, 96, 4, 64
+    q, k, v = qkv(5, B, T, H, d)
+    ref, _, _ = O.attn_forward(q, k, v, B, T, H, d)
+    qd, kd, vd = dev(q), dev(k), dev(v)
+    h0, hn = 1, 2
+    out = torch.zeros((B * T, hn * d), device="cuda")
+    shape = A.Shape(B, hn, T, d, H * d, hn * d)
+    A.fwd_ex(shape, A.F32, qd[:, h0 * d:].data_ptr(), kd[:, h0 * d:].data_ptr(), vd[:, h0 * d:].data_ptr(),
+             out.data_ptr(), None)
+    torch.cuda.synchronize()
+    assert rel_err(host(out), ref[:, h0 * d:(h0 + hn) * d]) < F32_TOL
+
+
+def test_forward_deterministic(A):
+    q, k, v = qkv(3, 2, 300, 2, 64)
+    a, _ = A.forward_t(dev(q), dev(k), dev(v), 2, 2)
+    b, _ = A.forward_t(dev(q), dev(k), dev(v), 2, 2)
+    assert np.array_equal(host(a), host(b))
+
+
+# ---------------------------------------------------------------------------
+# backward
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("name", ["bwd_h2_d64", "bwd_h4_d32"])
+def test_backward_f32_golden(A, name):
+    z = golden(name)
+    B, T, H, d = (int(x) for x in z["shape"])
+    q, k, v, do = dev(z["q"]), dev(z["k"]), dev(z["v"]), dev(z["do"])
+    o, lse = A.forward_t(q, k, v, H, B)
+    dq, dk, dv = A.backward_t(do, q, k, v, o, lse, H, B)
+    assert rel_err(host(dq), z["dq"]) < F32_TOL
+    assert rel_err(host(dk), z["dk"]) < F32_TOL
+    assert rel_err(host(dv), z["dv"]) < F32_TOL
+
+
+def test_backward_accumulate_flag(A):
+    """accumulate=1 adds into the gradients like train.c:372; 0 sets them
+    like gpu_kernels.cu's attn_bwd (beta = 0)."""
+    z = golden("bwd_h4_d32")
+    B, T, H, d = (int(x) for x in z["shape"])
+    q, k, v, do = dev(z["q"]), dev(z["k"]), dev(z["v"]), dev(z["do"])
+    o, lse = A.forward_t(q, k, v, H, B)
+    base = synth.normal(77, z["q"].shape)
+    dq, dk, dv = dev(base), dev(base), dev(base)
+    A.backward_t(do, q, k, v, o, lse, H, B, dq, dk, dv, accumulate=True)
+    assert rel_err(host(dq), base + z["dq"]) < F32_TOL
+    assert rel_err(host(dv), base + z["dv"]) < F32_TOL
+    A.backward_t(do, q, k, v, o, lse, H, B, dq, dk, dv, accumulate=False)
+    assert rel_err(host(dk), z["dk"]) < F32_TOL
+
+
+@pytest.mark.parametrize("B,T,H,d", [(1, 200, 2, 64), (2, 70, 2, 32), (1, 129, 1, 128), (1, 100, 2, 96),
+                                     (1, 1, 2, 64)])
+def test_backward_f32_vs_oracle(A, B, T, H, d):
+    q, k, v = qkv(13 * T + d, B, T, H, d)
+    do = synth.normal(99 + T, (B * T, H * d))
+    _, probs, _ = O.attn_forward(q, k, v, B, T, H, d, want_probs=True)
+    rq, rk, rv = O.attn_backward(do, q, k, v, probs, B, T, H, d)
+    qd, kd, vd, gd = dev(q), dev(k), dev(v), dev(do)
+    o, lse = A.forward_t(qd, kd, vd, H, B)
+    dq, dk, dv = A.backward_t(gd, qd, kd, vd, o, lse, H, B)
+    assert rel_err(host(dq), rq) < F32_TOL
+    assert rel_err(host(dk), rk) < F32_TOL
+    assert rel_err(host(dv), rv) < F32_TOL
+
+
+@pytest.mark.parametrize("B,T,H,d", [(1, 200, 2, 64), (2, 130, 2, 32), (1, 256, 1, 128)])
+def test_backward_bf16_vs_fp32_oracle(A, B, T, H, d):
+    import torch
+    q, k, v = (bf16_round(x) for x in qkv(17 * T + d, B, T, H, d))
+    do = bf16_round(synth.normal(5 + T, (B * T, H * d)))
+    _, probs, _ = O.attn_forward(q, k, v, B, T, H, d, want_probs=True)
+    rq, rk, rv = O.attn_backward(do, q, k, v, probs, B, T, H, d)
+    bf = torch.bfloat16
+    qd, kd, vd, gd = dev(q, bf), dev(k, bf), dev(v, bf), dev(do, bf)
+    o, lse = A.forward_t(qd, kd, vd, H, B)
+    dq, dk, dv = A.backward_t(gd, qd, kd, vd, o, lse, H, B)
+    assert rel_err(host(dq), rq) < BF16_BWD_TOL
+    assert rel_err(host(dk), rk) < BF16_BWD_TOL
+    assert rel_err(host(dv), rv) < BF16_BWD_TOL
+
+
+def test_backward_deterministic_and_workspace_check(A):
+    import torch
+    q, k, v = qkv(8, 1, 150, 2, 64)
+    do = synth.normal(9, q.shape)
+    qd, kd, vd, gd = dev(q), dev(k), dev(v), dev(do)
+    o, lse = A.forward_t(qd, kd, vd, 2, 1)
+    r1 = A.backward_t(gd, qd, kd, vd, o, lse, 2, 1)
+    r2 = A.backward_t(gd, qd, kd, vd, o, lse, 2, 1)
+    for a, b in zip(r1, r2):
+        assert np.array_equal(host(a), host(b))
+    shape = A.Shape(1, 2, 150, 64, 0, 0)
+    small = torch.empty(64, dtype=torch.uint8, device="cuda")
+    st = A.lib.attn_bwd_ex(ctypes.byref(shape), A.F32, gd.data_ptr(), qd.data_ptr(), kd.data_ptr(), vd.data_ptr(),
+                           o.data_ptr(), lse.data_ptr(), r1[0].data_ptr(), r1[1].data_ptr(), r1[2].data_ptr(), 0,
+                           small.data_ptr(), 64, None)
+    assert st == A.ERR_WORKSPACE
+
+
+# ---------------------------------------------------------------------------
+# drop-in attn_fwd / attn_bwd (gpu_kernels.h:67-72)
+# ---------------------------------------------------------------------------
+def test_drop_in_fwd_bwd(A):
+    import torch
+    B, T, H, d = 2, 130, 2, 64
+    A.check(A.lib.attn_set_macro_shape(B, H, T, d))
+    try:
+        q, k, v = qkv(21, B, T, H, d)
+        do = synth.normal(22, q.shape)
+        ref, probs, _ = O.attn_forward(q, k, v, B, T, H, d, want_probs=True)
+        rq, rk, rv = O.attn_backward(do, q, k, v, probs, B, T, H, d)
+        qd, kd, vd, gd = dev(q), dev(k), dev(v), dev(do)
+        att = torch.empty_like(qd)
+        probs_buf = torch.empty(B * H * T * T, device="cuda")
+        scratch = torch.empty(B * H * T * T, device="cuda")
+        dq, dk, dv = (torch.full_like(qd, 7.0) for _ in range(3))   # SET, not accumulated
+        torch.cuda.synchronize()
+        A.lib.attn_fwd(qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), att.data_ptr(), probs_buf.data_ptr())
+        A.lib.attn_bwd(dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), scratch.data_ptr(), gd.data_ptr(),
+                       qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), probs_buf.data_ptr())
+        torch.cuda.synchronize()
+        assert rel_err(host(att), ref) < F32_TOL
+        assert rel_err(host(dq), rq) < F32_TOL
+        assert rel_err(host(dk), rk) < F32_TOL
+        assert rel_err(host(dv), rv) < F32_TOL
+    finally:
+        A.lib.attn_set_macro_shape(4, 12, 1024, 128)
+
+
+# ---------------------------------------------------------------------------
+# decode
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("name", ["decode_h4_d32", "decode_h2_d64"])
+def test_cached_attention_golden(A, name):
+    import torch
+    z = golden(name)
+    H, d, _ = (int(x) for x in z["shape"])
+    kc, vc = dev(z["kcache"]), dev(z["vcache"])
+    for i, pos in enumerate(z["positions"]):
+        q = dev(z["q"][i])
+        out = torch.empty_like(q)
+        A.check(A.lib.attn_cached_attention(q.data_ptr(), kc.data_ptr(), vc.data_ptr(), out.data_ptr(), int(pos),
+                                            H, d, H * d, None))
+        torch.cuda.synchronize()
+        assert rel_err(host(out), z["out"][i]) < F32_TOL
+
+
+@pytest.mark.parametrize("H,d,n_seq,max_len", [(16, 64, 8, 3000), (16, 32, 5, 700), (4, 128, 3, 1500),
+                                               (2, 96, 4, 257), (16, 64, 2, 1)])
+def test_ragged_decode_f32_vs_oracle(A, H, d, n_seq, max_len):
+    import torch
+    lens = synth.uniform_int(H * d + n_seq, n_seq, 1, max_len)
+    lens[0] = max_len
+    cap = max_len
+    kc = synth.normal(31, (n_seq * cap, H * d))
+    vc = synth.normal(32, (n_seq * cap, H * d))
+    q = synth.normal(33, (n_seq, H * d))
+    out = A.decode_t(dev(q), dev(kc), dev(vc), dev(lens), H, cap, max_len)
+    torch.cuda.synchronize()
+    for s in range(n_seq):
+        ref = O.cached_attention(q[s], kc[s * cap:(s + 1) * cap], vc[s * cap:(s + 1) * cap], int(lens[s]) - 1, H, d)
+        assert rel_err(host(out)[s], ref) < F32_TOL, s
+
+
+def test_decode_pointer_array_layers(A):
+    """attn_decode_ptrs_ex over per-layer slabs (KVCache.k[l], model.h:43)."""
+    import torch
+    L, H, d, cap, pos = 4, 16, 32, 640, 600
+    ks = [synth.normal(40 + l, (cap, H * d)) for l in range(L)]
+    vs = [synth.normal(50 + l, (cap, H * d)) for l in range(L)]
+    q = synth.normal(60, (L, H * d))
+    kd = [dev(x) for x in ks]
+    vd = [dev(x) for x in vs]
+    kp = torch.tensor([t.data_ptr() for t in kd], dtype=torch.int64, device="cuda")
+    vp = torch.tensor([t.data_ptr() for t in vd], dtype=torch.int64, device="cuda")
+    lens = torch.full((L,), pos + 1, dtype=torch.int32, device="cuda")
+    qd = dev(q)
+    out = torch.empty_like(qd)
+    shape = A.DecodeShape(L, H, d, A.F32, 0, cap, cap)
+    A.check(A.lib.attn_decode_ptrs_ex(ctypes.byref(shape), qd.data_ptr(), kp.data_ptr(), vp.data_ptr(), None, None,
+                                      lens.data_ptr(), out.data_ptr(), None, 0, None))
+    torch.cuda.synchronize()
+    for l in range(L):
+        ref = O.ref_cached_attention(q[l], ks[l], vs[l], pos, H, d, 1024) if O.ref_available() else \
+            O.cached_attention(q[l], ks[l], vs[l], pos, H, d)
+        assert rel_err(host(out)[l], ref) < F32_TOL
+
+
+def test_quantiser_bit_exact(A):
+    import torch
+    z = golden("quant_h4_d32")
+    H, d = (int(x) for x in z["shape"])
+    codes, scales = A.quantize_int8_t(dev(z["x"]), H)
+    torch.cuda.synchronize()
+    assert np.array_equal(host(codes), z["codes"])
+    assert np.array_equal(host(scales).view(np.uint32), z["scales"].view(np.uint32))
+    x = synth.normal(5, (333, 16 * 64), 0, 3.0)
+    c2, s2 = A.quantize_int8_t(dev(x), 16)
+    rc, rs = O.quantize_kv_int8(x, 16, 64)
+    assert np.array_equal(host(c2), rc) and np.array_equal(host(s2).view(np.uint32), rs.view(np.uint32))
+
+
+def test_int8_decode_golden(A):
+    import torch
+    z = golden("int8_decode_h2_d64")
+    H, d, _ = (int(x) for x in z["shape"])
+    pos = int(z["pos"])
+    lens = torch.tensor([pos + 1], dtype=torch.int32, device="cuda")
+    out = A.decode_t(dev(z["q"][None, :]), dev(z["kcodes"]), dev(z["vcodes"]), lens, H, pos + 1, pos + 1,
+                     kscale=dev(z["kscale"]), vscale=dev(z["vscale"]))
+    torch.cuda.synchronize()
+    assert rel_err(host(out)[0], z["out"]) < F32_TOL
+
+
+@pytest.mark.parametrize("H,d,n_seq,max_len", [(16, 64, 6, 4000), (16, 32, 3, 900), (2, 128, 3, 333)])
+def test_ragged_decode_int8_vs_dequantised_oracle(A, H, d, n_seq, max_len):
+    import torch
+    lens = synth.uniform_int(3 * H + d, n_seq, 1, max_len)
+    cap = max_len
+    kc = synth.normal(71, (n_seq * cap, H * d))
+    vc = synth.normal(72, (n_seq * cap, H * d))
+    q = synth.normal(73, (n_seq, H * d))
+    kq, ksc = A.quantize_int8_t(dev(kc), H)
+    vq, vsc = A.quantize_int8_t(dev(vc), H)
+    out = A.decode_t(dev(q), kq, vq, dev(lens), H, cap, max_len, kscale=ksc, vscale=vsc)
+    torch.cuda.synchronize()
+    kd = O.dequantize_kv_int8(host(kq), host(ksc), H, d)
+    vd = O.dequantize_kv_int8(host(vq), host(vsc), H, d)
+    for s in range(n_seq):
+        ref = O.cached_attention(q[s], kd[s * cap:(s + 1) * cap], vd[s * cap:(s + 1) * cap], int(lens[s]) - 1, H, d)
+        assert rel_err(host(out)[s], ref) < F32_TOL
+        # informational bound against the un-quantised cache
+        ref32 = O.cached_attention(q[s], kc[s * cap:(s + 1) * cap], vc[s * cap:(s + 1) * cap], int(lens[s]) - 1, H, d)
+        assert rel_err(host(out)[s], ref32) < 5e-2
+
+
+def test_decode_caller_workspace_and_reuse(A):
+    import torch
+    H, d, n_seq, max_len = 16, 64, 4, 2048
+    lens = synth.uniform_int(9, n_seq, 1000, max_len)
+    kc = synth.normal(81, (n_seq * max_len, H * d))
+    vc = synth.normal(82, (n_seq * max_len, H * d))
+    q = synth.normal(83, (n_seq, H * d))
+    shape = A.DecodeShape(n_seq, H, d, A.F32, 0, max_len, max_len)
+    ws = torch.zeros(A.decode_workspace_bytes(shape), dtype=torch.uint8, device="cuda")
+    outs = [host(A.decode_t(dev(q), dev(kc), dev(vc), dev(lens), H, max_len, max_len, workspace=ws))
+            for _ in range(3)]
+    assert np.array_equal(outs[0], outs[1]) and np.array_equal(outs[1], outs[2])
+    ref = O.cached_attention(q[1], kc[max_len:2 * max_len], vc[max_len:2 * max_len], int(lens[1]) - 1, H, d)
+    assert rel_err(outs[0][1], ref) < F32_TOL
+
+
+def test_decode_bad_length_sets_device_error_word(A):
+    """Failure detection without a fault: an out-of-range length is clamped,
+    recorded in the device error word, and the context stays usable."""
+    import torch
+    H, d, cap = 2, 64, 100
+    kc, vc = dev(synth.normal(1, (cap, H * d))), dev(synth.normal(2, (cap, H * d)))
+    q = dev(synth.normal(3, (1, H * d)))
+    code = ctypes.c_int()
+    A.check(A.lib.attn_device_error(0, ctypes.byref(code)))       # clear
+    out = A.decode_t(q, kc, vc, dev(np.array([cap + 50], np.int32)), H, cap, cap)
+    torch.cuda.synchronize()
+    A.check(A.lib.attn_device_error(0, ctypes.byref(code)))
+    assert code.value != 0
+    assert np.isfinite(host(out)).all()
+    A.check(A.lib.attn_device_error(0, ctypes.byref(code)))
+    assert code.value == 0
+
+
+def test_kv_cache_alloc_append_decode(A):
+    import torch
+    for kv in (A.F32, A.I8):
+        c = A.KVCache()
+        L, cap, H, d = 3, 64, 4, 32
+        A.check(A.lib.attn_kv_cache_alloc(ctypes.byref(c), L, cap, H, d, kv))
+        try:
+            rows_k = synth.normal(10 + kv, (cap, H * d))
+            rows_v = synth.normal(20 + kv, (cap, H * d))
+            kd, vd = dev(rows_k), dev(rows_v)
+            for pos in range(40):
+                A.check(A.lib.attn_kv_cache_append(ctypes.byref(c), 1, pos, kd[pos].data_ptr(), vd[pos].data_ptr(),
+                                                   None))
+            q = dev(synth.normal(30, (1, H * d)))
+            out = torch.empty_like(q)
+            lens = torch.tensor([40], dtype=torch.int32, device="cuda")
+            shape = A.DecodeShape(1, H, d, kv, 0, cap, cap)
+            A.check(A.lib.attn_decode_ex(ctypes.byref(shape), q.data_ptr(), c.k[1], c.v[1], c.kscale[1], c.vscale[1],
+                                         lens.data_ptr(), out.data_ptr(), None, 0, None))
+            torch.cuda.synchronize()
+            kr, vr = rows_k[:40], rows_v[:40]
+            if kv == A.I8:
+                kr = O.dequantize_kv_int8(*O.quantize_kv_int8(kr, H, d), H, d)
+                vr = O.dequantize_kv_int8(*O.quantize_kv_int8(vr, H, d), H, d)
+            ref = O.cached_attention(host(q)[0], kr, vr, 39, H, d)
+            assert rel_err(host(out)[0], ref) < F32_TOL
+        finally:
+            A.check(A.lib.attn_kv_cache_free(ctypes.byref(c)))
+
+
+def test_gather_permute(A):
+    import torch
+    G, B, T, H, d = 4, 2, 33, 8, 32
+    staging = synth.normal(5, (G, B, T, H // G, d))
+    out = A.gather_permute_t(dev(staging).reshape(-1, d), G, B, T, H, d)
+    torch.cuda.synchronize()
+    ref = staging.transpose(1, 2, 0, 3, 4).reshape(B * T, H * d)
+    assert np.array_equal(host(out), ref)
