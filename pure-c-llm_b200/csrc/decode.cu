@@ -10,15 +10,16 @@
 //   * one CTA per (split, head, sequence); a split is a contiguous chunk of
 //     cache rows, sized on the host so the grid covers the 148 SMs several
 //     times over;
-//   * 8 lanes per cache row, each holding head_dim/8 elements, so every warp
-//     load instruction moves four full 128-byte row segments (fp32) and all
-//     bytes of a sector are used; four row batches are loaded before any is
-//     consumed to keep ~16 KB per CTA in flight;
+//   * fp32 rows: 8 lanes per cache row, each holding head_dim/8 elements, so
+//     every warp load instruction moves four full 128-byte row segments and
+//     all bytes of a sector are used; int8 rows: 4 lanes per row with 16-byte
+//     loads at d = 64; several row batches are loaded before any is consumed
+//     to keep 8-16 KB per CTA in flight;
 //   * scores live in shared memory (base-2 domain), block max / sum reduce
 //     with warp shuffles;
 //   * splits of one (sequence, head) are merged by the last CTA to finish
-//     (threadfence + atomic ticket; nobody waits on anybody), which then
-//     re-arms the ticket to zero for the next call.
+//     (threadfence + atomic ticket; nobody waits on anybody).  The tickets
+//     are cleared on the stream before each launch.
 #include "common.cuh"
 
 namespace attn {
@@ -44,40 +45,57 @@ struct DecodeParams {
 };
 
 constexpr int kDecThreads = 128;
-constexpr int kLanesPerRow = 8;
-constexpr int kRowsPerPass = kDecThreads / kLanesPerRow;   // 16
-constexpr int kUnroll = 4;
 
-// Per-lane slice of a row: fp32 lanes take float4 groups {sub*4 + 32*k},
-// int8 lanes take D/8 consecutive bytes starting at sub*D/8.
+// Lane geometry.  fp32 rows: 8 lanes per row, lane `sub` holds the float4
+// groups {sub*4 + 32k} (every warp load moves four 128-byte row segments).
+// int8 rows: 4 lanes per row, lane `sub` holds D/4 consecutive bytes (16-byte
+// loads at d = 64), raw words kept packed until use.
 template <int D, bool I8>
 struct RowSlice {
-    static constexpr int E = D / kLanesPerRow;   // elements per lane
-    float v[E];
+    static constexpr int LPR = I8 ? 4 : 8;                 // lanes per row
+    static constexpr int ROWS = kDecThreads / LPR;         // rows per CTA pass
+    static constexpr int E = D / LPR;                      // elements per lane
+    static constexpr int W = I8 ? E / 4 : E;               // registers per lane
+    static constexpr int UNROLL = I8 ? 8 : 4;              // row batches in flight
+    uint32_t w[W];
 
-    __device__ __forceinline__ void load(const void *row, int sub) {
+    __device__ __forceinline__ void load(const char *row, int sub) {
         if constexpr (!I8) {
-            const float *r = static_cast<const float *>(row);
+            const float *r = reinterpret_cast<const float *>(row);
 #pragma unroll
             for (int k = 0; k < E / 4; k++) {
-                float4 x = __ldg(reinterpret_cast<const float4 *>(r + sub * 4 + 32 * k));
-                v[4 * k + 0] = x.x; v[4 * k + 1] = x.y; v[4 * k + 2] = x.z; v[4 * k + 3] = x.w;
+                const uint4 x = __ldg(reinterpret_cast<const uint4 *>(r + sub * 4 + 32 * k));
+                w[4 * k + 0] = x.x; w[4 * k + 1] = x.y; w[4 * k + 2] = x.z; w[4 * k + 3] = x.w;
+            }
+        } else if constexpr (E % 16 == 0) {
+            const uint4 *r = reinterpret_cast<const uint4 *>(row + sub * E);
+#pragma unroll
+            for (int k = 0; k < E / 16; k++) {
+                const uint4 x = __ldg(r + k);
+                w[4 * k + 0] = x.x; w[4 * k + 1] = x.y; w[4 * k + 2] = x.z; w[4 * k + 3] = x.w;
             }
         } else {
-            const int8_t *r = static_cast<const int8_t *>(row) + sub * E;
+            const uint2 *r = reinterpret_cast<const uint2 *>(row + sub * E);
 #pragma unroll
-            for (int k = 0; k < E / 4; k++) {
-                uint32_t w = __ldg(reinterpret_cast<const unsigned int *>(r + 4 * k));
-#pragma unroll
-                for (int b = 0; b < 4; b++)
-                    v[4 * k + b] = (float)(int8_t)((w >> (8 * b)) & 0xffu);
+            for (int k = 0; k < E / 8; k++) {
+                const uint2 x = __ldg(r + k);
+                w[2 * k + 0] = x.x; w[2 * k + 1] = x.y;
             }
         }
+    }
+    __device__ __forceinline__ float get(int i) const {
+        if constexpr (!I8) return __uint_as_float(w[i]);
+        else return (float)(int8_t)((w[i / 4] >> (8 * (i % 4))) & 0xffu);
     }
     // element index (within the head) of slot i for lane `sub`
     static __device__ __forceinline__ int index(int sub, int i) {
         if constexpr (!I8) return sub * 4 + 32 * (i / 4) + (i % 4);
         else return sub * E + i;
+    }
+    static __device__ __forceinline__ float row_sum(float v) {
+#pragma unroll
+        for (int o = LPR / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        return v;
     }
 };
 
@@ -87,9 +105,11 @@ decode_split_kernel(const DecodeParams p)
 {
     using Slice = RowSlice<D, I8>;
     constexpr int E = Slice::E;
+    constexpr int ROWS = Slice::ROWS;
+    constexpr int UNROLL = Slice::UNROLL;
     extern __shared__ float smem[];
     float *sc = smem;                         // [chunk] scores, then weights
-    float *red = smem + p.chunk;              // [kRowsPerPass * D] partial outputs
+    float *red = smem + p.chunk;              // [ROWS * D] partial outputs
     __shared__ float wred[kDecThreads / 32];
     __shared__ int last_flag;
 
@@ -105,7 +125,7 @@ decode_split_kernel(const DecodeParams p)
     const int n = min(len - r0, p.chunk);
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int grp = tid / kLanesPerRow, sub = tid % kLanesPerRow;
+    const int grp = tid / Slice::LPR, sub = tid % Slice::LPR;
 
     // cache bases for this sequence (element offsets in units of the cache type)
     const char *kb, *vb;
@@ -136,24 +156,22 @@ decode_split_kernel(const DecodeParams p)
     }
 
     // ---- pass 1: scores of rows r0 .. r0+n-1 ----------------------------------
-    for (int base = 0; base < n; base += kRowsPerPass * kUnroll) {
-        Slice ks[kUnroll];
+    for (int base = 0; base < n; base += ROWS * UNROLL) {
+        Slice ks[UNROLL];
 #pragma unroll
-        for (int u = 0; u < kUnroll; u++) {
-            const int r = base + u * kRowsPerPass + grp;
+        for (int u = 0; u < UNROLL; u++) {
+            const int r = base + u * ROWS + grp;
             if (r < n) ks[u].load(kb + (r0 + r) * rstride_b + head_off_b, sub);
         }
 #pragma unroll
-        for (int u = 0; u < kUnroll; u++) {
-            const int r = base + u * kRowsPerPass + grp;
+        for (int u = 0; u < UNROLL; u++) {
+            const int r = base + u * ROWS + grp;
             float acc = 0.f;
             if (r < n) {
 #pragma unroll
-                for (int i = 0; i < E; i++) acc = fmaf(qv[i], ks[u].v[i], acc);
+                for (int i = 0; i < E; i++) acc = fmaf(qv[i], ks[u].get(i), acc);
             }
-            acc += __shfl_xor_sync(0xffffffffu, acc, 1);
-            acc += __shfl_xor_sync(0xffffffffu, acc, 2);
-            acc += __shfl_xor_sync(0xffffffffu, acc, 4);
+            acc = Slice::row_sum(acc);
             if (r < n && sub == 0) {
                 if constexpr (I8) acc *= __ldg(ksb + (long long)(r0 + r) * p.H + h);
                 sc[r] = acc;
@@ -186,20 +204,20 @@ decode_split_kernel(const DecodeParams p)
     float o[E];
 #pragma unroll
     for (int i = 0; i < E; i++) o[i] = 0.f;
-    for (int base = 0; base < n; base += kRowsPerPass * kUnroll) {
-        Slice vs[kUnroll];
+    for (int base = 0; base < n; base += ROWS * UNROLL) {
+        Slice vs[UNROLL];
 #pragma unroll
-        for (int u = 0; u < kUnroll; u++) {
-            const int r = base + u * kRowsPerPass + grp;
+        for (int u = 0; u < UNROLL; u++) {
+            const int r = base + u * ROWS + grp;
             if (r < n) vs[u].load(vb + (r0 + r) * rstride_b + head_off_b, sub);
         }
 #pragma unroll
-        for (int u = 0; u < kUnroll; u++) {
-            const int r = base + u * kRowsPerPass + grp;
+        for (int u = 0; u < UNROLL; u++) {
+            const int r = base + u * ROWS + grp;
             if (r < n) {
                 const float w = sc[r];
 #pragma unroll
-                for (int i = 0; i < E; i++) o[i] = fmaf(w, vs[u].v[i], o[i]);
+                for (int i = 0; i < E; i++) o[i] = fmaf(w, vs[u].get(i), o[i]);
             }
         }
     }
@@ -213,7 +231,7 @@ decode_split_kernel(const DecodeParams p)
         for (int c = tid; c < D; c += kDecThreads) {
             float s = 0.f;
 #pragma unroll
-            for (int g = 0; g < kRowsPerPass; g++) s += red[g * D + c];
+            for (int g = 0; g < ROWS; g++) s += red[g * D + c];
             out[c] = s * inv;
         }
         return;
@@ -225,7 +243,7 @@ decode_split_kernel(const DecodeParams p)
     for (int c = tid; c < D; c += kDecThreads) {
         float s = 0.f;
 #pragma unroll
-        for (int g = 0; g < kRowsPerPass; g++) s += red[g * D + c];
+        for (int g = 0; g < ROWS; g++) s += red[g * D + c];
         po[c] = s;
     }
     if (tid == 0) {
@@ -279,11 +297,11 @@ size_t decode_workspace_bytes(int n_seq, int heads, int head_dim, int max_len) {
     const int chunk = decode_chunk(max_len, (long long)n_seq * heads);
     const long long splits = (max_len + chunk - 1) / chunk;
     const long long eh = (long long)n_seq * heads;
-    size_t b = 0;
-    b += (size_t)eh * splits * head_dim * sizeof(float);   // part_o
+    size_t b = (size_t)eh * sizeof(unsigned);              // tickets
+    b = (b + 255) / 256 * 256;
     b += (size_t)eh * splits * 2 * sizeof(float);          // part_ml
     b = (b + 255) / 256 * 256;
-    b += (size_t)eh * sizeof(unsigned);                    // tickets
+    b += (size_t)eh * splits * head_dim * sizeof(float);   // part_o
     return (b + 255) / 256 * 256;
 }
 
@@ -309,19 +327,26 @@ static int launch_decode_t(const DecodeLaunch &L) {
     const long long eh = (long long)L.n_seq * L.heads;
     p.chunk = decode_chunk(L.max_len, eh);
     p.max_splits = (L.max_len + p.chunk - 1) / p.chunk;
+    // workspace: [tickets | part_ml | part_o], each 256-byte aligned.  The
+    // tickets are cleared on the stream before every launch, so a workspace
+    // may be shared by calls of any shape (ordered on one stream).
     char *ws = static_cast<char *>(L.ws);
-    size_t o_bytes = (size_t)eh * p.max_splits * D * sizeof(float);
-    size_t ml_bytes = (size_t)eh * p.max_splits * 2 * sizeof(float);
-    p.part_o = reinterpret_cast<float *>(ws);
-    p.part_ml = reinterpret_cast<float *>(ws + o_bytes);
-    p.tickets = reinterpret_cast<unsigned *>(ws + (o_bytes + ml_bytes + 255) / 256 * 256);
+    const size_t t_bytes = ((size_t)eh * sizeof(unsigned) + 255) / 256 * 256;
+    const size_t ml_bytes = ((size_t)eh * p.max_splits * 2 * sizeof(float) + 255) / 256 * 256;
+    p.tickets = reinterpret_cast<unsigned *>(ws);
+    p.part_ml = reinterpret_cast<float *>(ws + t_bytes);
+    p.part_o = reinterpret_cast<float *>(ws + t_bytes + ml_bytes);
+    if (p.max_splits > 1) {
+        cudaError_t e = cudaMemsetAsync(p.tickets, 0, (size_t)eh * sizeof(unsigned), L.stream);
+        if (e != cudaSuccess) return set_error(ATTN_ERR_CUDA, "decode: ticket clear: %s", cudaGetErrorString(e));
+    }
     p.q = L.q; p.kbase = L.kbase; p.vbase = L.vbase; p.kptrs = L.kptrs; p.vptrs = L.vptrs;
     p.ksbase = L.ksbase; p.vsbase = L.vsbase; p.ksptrs = L.ksptrs; p.vsptrs = L.vsptrs;
     p.lens = L.lens; p.out = L.out; p.err = L.err;
     p.row_stride = L.row_stride; p.cap = L.cap; p.H = L.heads; p.max_len = L.max_len;
     p.qscale = kLog2e / sqrtf((float)D);
     dim3 grid(p.max_splits, L.heads, L.n_seq);
-    size_t smem = (size_t)(p.chunk + kRowsPerPass * D) * sizeof(float);
+    size_t smem = (size_t)(p.chunk + RowSlice<D, I8>::ROWS * D) * sizeof(float);
     decode_split_kernel<D, I8><<<grid, kDecThreads, smem, L.stream>>>(p);
     return check_launch("decode_split_kernel");
 }
