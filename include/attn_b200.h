@@ -166,6 +166,23 @@ ATTN_API int attn_decode_ptrs_ex(const attn_decode_shape *s, const float *q,
                         const int *lens, float *out,
                         void *workspace, size_t workspace_bytes, attn_stream_t stream);
 
+/* No counterpart in the reference.  Same as attn_decode_ex, but it allocates
+ * nothing and takes no workspace: the scratch is a fixed array of
+ * ATTN_DECODE_STATIC_SCRATCH_BYTES inside the library's device image, reserved
+ * on every GPU that loads the library until the process exits.  It is for
+ * callers that cannot allocate device memory (memory owned by another
+ * allocator, or a loop that must not let cudaMalloc synchronise the device).
+ * Shapes whose scratch need (attn_decode_workspace_bytes) exceeds the array
+ * are rejected with ATTN_ERR_WORKSPACE.  The first call on a device looks up
+ * the array's device address (cudaGetSymbolAddress); make that first call
+ * before any stream capture.  All calls share the array: calls whose kernels
+ * overlap on the GPU race. */
+#define ATTN_DECODE_STATIC_SCRATCH_BYTES (4u << 20)
+ATTN_API int attn_decode_static_ex(const attn_decode_shape *s, const float *q,
+                                   const void *kcache, const void *vcache,
+                                   const float *kscale, const float *vscale,
+                                   const int *lens, float *out, attn_stream_t stream);
+
 /* cached_attention (transformer.c:203) with device pointers: one token of one
  * layer, attends rows 0..pos.  Writes out (H*d).  Uses the library's own
  * workspace.  Returns a status. */

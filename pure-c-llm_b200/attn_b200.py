@@ -16,6 +16,7 @@ LIB_PATH = os.path.join(_HERE, "libattn_b200.so")
 OK, ERR_INVALID, ERR_UNSUPPORTED, ERR_CUDA, ERR_NOMEM, ERR_WORKSPACE, ERR_DEVICE = range(7)
 F32, BF16, I8 = 0, 1, 2
 MAX_LAYERS = 64
+STATIC_SCRATCH_BYTES = 4 << 20      # ATTN_DECODE_STATIC_SCRATCH_BYTES
 
 
 class AttnError(RuntimeError):
@@ -67,6 +68,7 @@ SIGNATURES = {
     "attn_decode_workspace_bytes": (SZ, [ctypes.POINTER(DecodeShape)]),
     "attn_decode_ex": (I, [ctypes.POINTER(DecodeShape), P, P, P, P, P, P, P, P, SZ, P]),
     "attn_decode_ptrs_ex": (I, [ctypes.POINTER(DecodeShape), P, P, P, P, P, P, P, P, SZ, P]),
+    "attn_decode_static_ex": (I, [ctypes.POINTER(DecodeShape), P, P, P, P, P, P, P, P]),
     "attn_cached_attention": (I, [P, P, P, P, I, I, I, LL, P]),
     "attn_kv_quantize_int8": (I, [P, LL, I, I, LL, P, P, P]),
     "attn_kv_cache_alloc": (I, [ctypes.POINTER(KVCache), I, I, I, I, I]),
