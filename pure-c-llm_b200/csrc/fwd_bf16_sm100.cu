@@ -222,15 +222,24 @@ fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
             tc_fence_before();
             mbar_arrive(BAR(B_SE + wg));             // S buffer may be overwritten now
 
-            const bool diag = (j == n - 1);
-            float mx = -INFINITY;
+            // row max as 8 independent partial chains (a single 128-long chain of
+            // dependent max operations would serialise on instruction latency)
+            float mp[8];
 #pragma unroll
-            for (int c = 0; c < 128; c++) {
-                float v = __uint_as_float(s[c]);
-                if (diag && c > row) v = -INFINITY;
-                s[c] = __float_as_uint(v);
-                mx = fmaxf(mx, v);
+            for (int i = 0; i < 8; i++) mp[i] = -INFINITY;
+            if (j == n - 1) {                        // diagonal tile: keys past the query row are masked
+#pragma unroll
+                for (int c = 0; c < 128; c++) {
+                    const float v = c > row ? -INFINITY : __uint_as_float(s[c]);
+                    s[c] = __float_as_uint(v);
+                    mp[c & 7] = fmaxf(mp[c & 7], v);
+                }
+            } else {
+#pragma unroll
+                for (int c = 0; c < 128; c++) mp[c & 7] = fmaxf(mp[c & 7], __uint_as_float(s[c]));
             }
+            float mx = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])),
+                             fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
             mx *= p.scale_log2;
             float alpha = 1.f;
             const bool grow = mx > m_run + 8.f;      // also true on the first tile
@@ -240,14 +249,16 @@ fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
                 l_run *= alpha;
             }
             const float neg_m = -m_run;
-            float ls = 0.f;
+            float lp[8];
+#pragma unroll
+            for (int i = 0; i < 8; i++) lp[i] = 0.f;
 #pragma unroll
             for (int c = 0; c < 128; c++) {
                 const float e = ex2(fmaf(__uint_as_float(s[c]), p.scale_log2, neg_m));
                 s[c] = __float_as_uint(e);
-                ls += e;
+                lp[c & 7] += e;
             }
-            l_run += ls;
+            l_run += ((lp[0] + lp[1]) + (lp[2] + lp[3])) + ((lp[4] + lp[5]) + (lp[6] + lp[7]));
             // P buffer and O are in use by the previous PV until it completes
             if (j > 0) ok = mbar_wait(BAR(B_OD + wg), (j - 1) & 1, abort_flag, p.err, 0x222);
             if (!(ok = __all_sync(0xffffffffu, ok))) break;
