@@ -4,21 +4,25 @@
 // scores, softmax statistics and accumulators (the tolerance of this path is
 // stated against fp32 attention over the same bf16 inputs).
 //
-// One CTA per (pair of 128-row query tiles, head, batch), 10 warps:
-//   warp 0      TMA producer: Q tiles once, then K_j/V_j into a 3-stage ring
-//   warp 1      MMA issuer (one thread): S_i = Q_i K_j^T and O_i += P_i V_j
-//               with tcgen05.mma kind::f16, accumulators in TMEM
-//   warps 2-5   softmax for query tile 0; warps 6-9 for query tile 1.  A
+// One CTA per (pair of 128-row query tiles, head, batch), 12 warps:
+//   warp 0      TMA producer: Q tiles once, then K_j/V_j into a 4-stage ring
+//   warp 1      MMA issuer (one thread): S_i = Q_i K_j^T (both operands in
+//               shared memory) and O_i += P_i V_j (P from TMEM, V from shared
+//               memory) with tcgen05.mma kind::f16, accumulators in TMEM
+//   warps 4-7   softmax for query tile 0; warps 8-11 for query tile 1.  A
 //               thread owns one query row (= one TMEM lane): it reads its S
 //               row with tcgen05.ld, keeps the running max/sum, writes its
-//               row of P (bf16) into 128-byte-swizzled shared memory for the
-//               next MMA, and rescales its O row in TMEM when the max grew by
-//               more than 2^8 (otherwise the stale max is kept; the final
-//               normalisation uses the same max for O and the sum).
+//               row of P (bf16 pairs) back into TMEM with tcgen05.st, and
+//               rescales its O row in TMEM when the max grew by more than 2^8
+//               (otherwise the stale max is kept; the final normalisation uses
+//               the same max for O and the sum).
 // The two query tiles ping-pong: while one warpgroup runs softmax, the
-// tensor core works on the other tile's products.
+// tensor core works on the other tile's products.  Keeping P in TMEM halves
+// the shared-memory traffic of the PV product (which would otherwise read
+// 6 KB per 32 tensor cycles, above the ~128 B/clk shared-memory bandwidth).
 //
-// TMEM: S0 cols [0,128), S1 [128,256), O0 [256,256+D), O1 [256+D, 256+2D).
+// TMEM: S0 cols [0,128), S1 [128,256), O0 [256,256+D), O1 [256+D, 256+2D),
+// P0 and P1 64 columns each after the O tiles.
 // Every mbarrier wait is bounded; a timeout records a code in the device
 // error word, raises a CTA-wide abort flag, and all roles fall through to the
 // common teardown, which frees TMEM.
@@ -34,22 +38,24 @@ using namespace sm100;
 
 constexpr int BM = 128;           // query rows per tile (TMEM lanes)
 constexpr int BN = 128;           // keys per tile
-constexpr int kStages = 3;
-constexpr int kThreads = 320;
+constexpr int kStages = 4;
+constexpr int kThreads = 384;
 
 template <int D>
 struct Cfg {
     static constexpr int Q_BYTES = BM * D * 2;
     static constexpr int KV_BYTES = BN * D * 2;
-    static constexpr int P_BYTES = BM * BN * 2;
     static constexpr int OFF_Q = 0;
-    static constexpr int OFF_P = 2 * Q_BYTES;
-    static constexpr int OFF_KV = OFF_P + 2 * P_BYTES;
+    static constexpr int OFF_KV = 2 * Q_BYTES;
     static constexpr int STAGE_BYTES = 2 * KV_BYTES;
     static constexpr int OFF_BAR = OFF_KV + kStages * STAGE_BYTES;
     static constexpr int SMEM = OFF_BAR + 256 + 1024;
+    // TMEM columns: S (fp32, 128 keys) and O (fp32, D) per query tile, and P
+    // (bf16 pairs, 64 columns for 128 keys) per query tile
     static constexpr int TM_S0 = 0, TM_S1 = 128, TM_O0 = 256, TM_O1 = 256 + D;
+    static constexpr int TM_P0 = 256 + 2 * D, TM_P1 = 256 + 2 * D + BN / 2;
     static constexpr int TM_COLS = 512;
+    static_assert(TM_P1 + BN / 2 <= TM_COLS, "TMEM budget");
 };
 
 // barrier slots
@@ -76,15 +82,17 @@ fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
     uint8_t *sb = smem_raw + (base - raw);
-    const uint32_t sQ = base + C::OFF_Q, sP = base + C::OFF_P, sKV = base + C::OFF_KV;
+    const uint32_t sQ = base + C::OFF_Q, sKV = base + C::OFF_KV;
     const uint32_t bar0 = base + C::OFF_BAR;
 #define BAR(i) (bar0 + 8u * (uint32_t)(i))
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sb + C::OFF_BAR + 128);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(sb + C::OFF_BAR + 132);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int pair = p.n_pairs - 1 - (int)blockIdx.x;      // heaviest pairs first
-    const int h = blockIdx.y, b = blockIdx.z;
+    // the pair index is the slowest grid dimension, so every CTA of the
+    // heaviest pairs (most key tiles) is issued before any lighter one
+    const int pair = p.n_pairs - 1 - (int)blockIdx.z;
+    const int h = blockIdx.x, b = blockIdx.y;
     const int q0 = pair * 2 * BM;
     const bool has_q1 = (q0 + BM) < p.T;
     const int n0 = q0 / BN + 1;                  // key tiles of query tile 0 (last is diagonal)
@@ -112,6 +120,11 @@ fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
+    // registers: 384 x 168 at launch; warpgroup 0 (TMA, MMA, 2 spare warps)
+    // gives back down to 72 so the two softmax warpgroups can hold 216 each
+    // (128 x 72 + 256 x 216 = 384 x 168).  Each setmaxnreg sits inside its
+    // role's branch so that it dominates the code that uses the new budget.
+    if (warp < 4) regs_dec<72>();
     if (warp == 0) {
         // ------------------------------------------------------------ producer
         if (lane == 0) {
@@ -149,12 +162,12 @@ fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
             };
             auto issue_PV = [&](int i, int j) {
                 const uint32_t va = sKV + (j % kStages) * C::STAGE_BYTES + C::KV_BYTES;
-                const uint32_t pa = sP + i * C::P_BYTES;
+                const uint32_t pt = tmem + (i ? C::TM_P1 : C::TM_P0);
                 const uint32_t d_t = tmem + (i ? C::TM_O1 : C::TM_O0);
 #pragma unroll
-                for (int kk = 0; kk < BN / 16; kk++)
-                    mma_bf16_ss(d_t, sw128_desc(pa + (kk >> 2) * (BM * 128) + (kk & 3) * 32, 16, 1024),
-                                sw128_desc(va + kk * 16 * 128, 16384, 1024), idO, (j > 0 || kk > 0));
+                for (int kk = 0; kk < BN / 16; kk++)      // 16 keys = 8 packed TMEM columns per step
+                    mma_bf16_ts(d_t, pt + kk * 8, sw128_desc(va + kk * 16 * 128, 16384, 1024), idO,
+                                (j > 0 || kk > 0));
                 mma_commit(BAR(B_OD + i));
             };
             bool ok = mbar_wait(BAR(B_Q), 0, abort_flag, p.err, 0x211) &&
@@ -164,20 +177,31 @@ fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
                 issue_S(0, 0);
                 if (has_q1) issue_S(1, 0);
             }
+            // Per key tile j: the scores of tile j+1 are issued as soon as each
+            // warpgroup has drained its S buffer (it does so right after loading
+            // S_j, before its softmax), so S_{j+1} is ready by the time P_j is;
+            // the PV products of tile j follow when P_j arrives.  A warpgroup
+            // therefore never waits for its own MMAs between tiles.
             for (int j = 0; ok && j < n_kv; j++) {
                 const int nx = j + 1, nst = nx % kStages;
-                bool next_ready = false;
+                const bool s0_next = nx < n0, s1_next = has_q1 && nx < n1;
+                if (s0_next || s1_next) {
+                    if (!(ok = mbar_wait(BAR(B_KVF + nst), (nx / kStages) & 1, abort_flag, p.err, 0x214))) break;
+                }
+                if (s0_next) {
+                    if (!(ok = mbar_wait(BAR(B_SE + 0), j & 1, abort_flag, p.err, 0x215))) break;
+                    tc_fence_after();
+                    issue_S(0, nx);
+                }
+                if (s1_next) {
+                    if (!(ok = mbar_wait(BAR(B_SE + 1), j & 1, abort_flag, p.err, 0x218))) break;
+                    tc_fence_after();
+                    issue_S(1, nx);
+                }
                 if (j < n0) {
                     if (!(ok = mbar_wait(BAR(B_PF + 0), j & 1, abort_flag, p.err, 0x213))) break;
                     tc_fence_after();
                     issue_PV(0, j);
-                }
-                if (nx < n0) {
-                    if (!(ok = mbar_wait(BAR(B_KVF + nst), (nx / kStages) & 1, abort_flag, p.err, 0x214))) break;
-                    next_ready = true;
-                    if (!(ok = mbar_wait(BAR(B_SE + 0), j & 1, abort_flag, p.err, 0x215))) break;
-                    tc_fence_after();
-                    issue_S(0, nx);
                 }
                 if (has_q1) {
                     if (!(ok = mbar_wait(BAR(B_PF + 1), j & 1, abort_flag, p.err, 0x216))) break;
@@ -185,19 +209,12 @@ fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
                     issue_PV(1, j);
                 }
                 mma_commit(BAR(B_KVE + j % kStages));      // stage j free once these MMAs finish
-                if (has_q1 && nx < n1) {
-                    if (!next_ready &&
-                        !(ok = mbar_wait(BAR(B_KVF + nst), (nx / kStages) & 1, abort_flag, p.err, 0x217)))
-                        break;
-                    if (!(ok = mbar_wait(BAR(B_SE + 1), j & 1, abort_flag, p.err, 0x218))) break;
-                    tc_fence_after();
-                    issue_S(1, nx);
-                }
             }
         }
-    } else {
+    } else if (warp >= 4) {
         // ------------------------------------------------------------ softmax
-        const int wg = (warp - 2) >> 2;
+        regs_inc<216>();
+        const int wg = (warp - 4) >> 2;
         const int quad = warp & 3;                   // TMEM lane quadrant of this warp
         const int row = quad * 32 + lane;            // query row within the tile
         const int n = wg ? n1 : n0;
@@ -205,8 +222,7 @@ fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
         const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
         const uint32_t tS = tmem + lane_base + (wg ? C::TM_S1 : C::TM_S0);
         const uint32_t tO = tmem + lane_base + (wg ? C::TM_O1 : C::TM_O0);
-        uint8_t *prow = sb + C::OFF_P + wg * C::P_BYTES + row * 128;
-        const int sw = row & 7;
+        const uint32_t tP = tmem + lane_base + (wg ? C::TM_P1 : C::TM_P0);
         float m_run = -INFINITY, l_run = 0.f;
         bool ok = true;
         for (int j = 0; j < n; j++) {
@@ -214,10 +230,13 @@ fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
             if (!(ok = __all_sync(0xffffffffu, ok))) break;   // tcgen05.ld below is warp-collective
             tc_fence_after();
             uint32_t s[128];
-            tmem_ld32(tS + 0, *reinterpret_cast<uint32_t(*)[32]>(&s[0]));
-            tmem_ld32(tS + 32, *reinterpret_cast<uint32_t(*)[32]>(&s[32]));
-            tmem_ld32(tS + 64, *reinterpret_cast<uint32_t(*)[32]>(&s[64]));
-            tmem_ld32(tS + 96, *reinterpret_cast<uint32_t(*)[32]>(&s[96]));
+#pragma unroll
+            for (int q4 = 0; q4 < 4; q4++) {         // (copies keep `s` in registers)
+                uint32_t t[32];
+                tmem_ld32(tS + 32 * q4, t);
+#pragma unroll
+                for (int c = 0; c < 32; c++) s[32 * q4 + c] = t[c];
+            }
             tmem_wait_ld();
             tc_fence_before();
             mbar_arrive(BAR(B_SE + wg));             // S buffer may be overwritten now
@@ -263,15 +282,15 @@ fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
             if (j > 0) ok = mbar_wait(BAR(B_OD + wg), (j - 1) & 1, abort_flag, p.err, 0x222);
             if (!(ok = __all_sync(0xffffffffu, ok))) break;
             tc_fence_after();
+            // P row -> TMEM as bf16 pairs (keys 2c, 2c+1 in column c): the A
+            // operand of the next PV product
 #pragma unroll
-            for (int c16 = 0; c16 < 16; c16++) {
-                uint4 v;
-                v.x = pack_bf16(__uint_as_float(s[8 * c16 + 0]), __uint_as_float(s[8 * c16 + 1]));
-                v.y = pack_bf16(__uint_as_float(s[8 * c16 + 2]), __uint_as_float(s[8 * c16 + 3]));
-                v.z = pack_bf16(__uint_as_float(s[8 * c16 + 4]), __uint_as_float(s[8 * c16 + 5]));
-                v.w = pack_bf16(__uint_as_float(s[8 * c16 + 6]), __uint_as_float(s[8 * c16 + 7]));
-                const int kb = c16 >> 3, c = c16 & 7;
-                *reinterpret_cast<uint4 *>(prow + kb * (BM * 128) + ((c ^ sw) << 4)) = v;
+            for (int half = 0; half < 2; half++) {
+                uint32_t t[32];
+#pragma unroll
+                for (int c = 0; c < 32; c++)
+                    t[c] = pack_bf16(__uint_as_float(s[64 * half + 2 * c]), __uint_as_float(s[64 * half + 2 * c + 1]));
+                tmem_st32(tP + 32 * half, t);
             }
             // rows whose max did not grow keep alpha = 1; the TMEM round trip is
             // warp-collective, so a warp rescales if any of its rows needs it
@@ -285,9 +304,8 @@ fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
                     for (int c = 0; c < 32; c++) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
                     tmem_st32(tO + c0, o);
                 }
-                tmem_wait_st();
             }
-            fence_async_smem();
+            tmem_wait_st();                          // P (and O) stores complete before the MMA reads them
             tc_fence_before();
             mbar_arrive(BAR(B_PF + wg));
         }
@@ -397,7 +415,7 @@ int launch_fwd_bf16_sm100(int D, const void *q, const void *k, const void *v, vo
     const size_t smem = Cfg<64>::SMEM;
     if (!ensure_smem_attr((const void *)fwd_kernel<64>, smem))
         return set_error(ATTN_ERR_CUDA, "tcgen05 forward: cannot set shared-memory size");
-    dim3 grid(p.n_pairs, H, B);
+    dim3 grid(H, B, p.n_pairs);
     fwd_kernel<64><<<grid, kThreads, smem, s>>>(tq, tk, tv, p);
     return check_launch("tcgen05 forward kernel");
 }
