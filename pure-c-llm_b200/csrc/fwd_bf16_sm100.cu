@@ -4,22 +4,29 @@
 // scores, softmax statistics and accumulators (the tolerance of this path is
 // stated against fp32 attention over the same bf16 inputs).
 //
-// One CTA per (pair of 128-row query tiles, head, batch), 12 warps:
-//   warp 0      TMA producer: Q tiles once, then K_j/V_j into a 4-stage ring
+// Persistent kernel: one CTA per SM walks a list of work items; an item is a
+// pair of consecutive 128-row query tiles of one (batch, head).  The host
+// orders the items longest-first and deals them to CTAs greedily (LPT), so
+// the causal triangle's uneven item costs balance across SMs.  12 warps:
+//   warp 0      TMA producer: Q tiles into a double buffer (the next item's Q
+//               loads while the current item runs), K_j/V_j into a 4-stage
+//               ring that runs across item boundaries
 //   warp 1      MMA issuer (one thread): S_i = Q_i K_j^T (both operands in
 //               shared memory) and O_i += P_i V_j (P from TMEM, V from shared
-//               memory) with tcgen05.mma kind::f16, accumulators in TMEM
-//   warps 4-7   softmax for query tile 0; warps 8-11 for query tile 1.  A
-//               thread owns one query row (= one TMEM lane): it reads its S
-//               row with tcgen05.ld, keeps the running max/sum, writes its
-//               row of P (bf16 pairs) back into TMEM with tcgen05.st, and
-//               rescales its O row in TMEM when the max grew by more than 2^8
+//               memory), tcgen05.mma kind::f16, fp32 accumulators in TMEM
+//   warps 2-3   spare (they only give their registers to the softmax warps)
+//   warps 4-7   softmax for query tile 0 of each item; warps 8-11 for tile 1.
+//               A thread owns one query row (= one TMEM lane): it reads its S
+//               row with tcgen05.ld, keeps the running max/sum, writes its row
+//               of P (bf16 pairs) back into TMEM with tcgen05.st, and rescales
+//               its O row in TMEM when the max grew by more than 2^8
 //               (otherwise the stale max is kept; the final normalisation uses
 //               the same max for O and the sum).
-// The two query tiles ping-pong: while one warpgroup runs softmax, the
-// tensor core works on the other tile's products.  Keeping P in TMEM halves
-// the shared-memory traffic of the PV product (which would otherwise read
-// 6 KB per 32 tensor cycles, above the ~128 B/clk shared-memory bandwidth).
+// The two query tiles ping-pong on the tensor core, and the MMA warp issues
+// S_{j+1} as soon as a warpgroup has drained S_j, so a warpgroup never waits
+// for its own products between tiles.  The first S of the next item is issued
+// while the warpgroups still finish the current one; its first PV waits until
+// the warpgroup has read out the previous O.
 //
 // TMEM: S0 cols [0,128), S1 [128,256), O0 [256,256+D), O1 [256+D, 256+2D),
 // P0 and P1 64 columns each after the O tiles.
@@ -29,7 +36,9 @@
 #include "common.cuh"
 #include "sm100.cuh"
 
+#include <algorithm>
 #include <cudaTypedefs.h>
+#include <vector>
 
 namespace attn {
 namespace fa {
@@ -40,18 +49,18 @@ constexpr int BM = 128;           // query rows per tile (TMEM lanes)
 constexpr int BN = 128;           // keys per tile
 constexpr int kStages = 4;
 constexpr int kThreads = 384;
+constexpr int kMaxCtas = 160;     // >= SM count of a B200 (148)
+constexpr int kMaxItems = 6144;   // schedule carried in the kernel parameters
 
 template <int D>
 struct Cfg {
-    static constexpr int Q_BYTES = BM * D * 2;
+    static constexpr int Q_BYTES = BM * D * 2;      // one query tile
     static constexpr int KV_BYTES = BN * D * 2;
-    static constexpr int OFF_Q = 0;
-    static constexpr int OFF_KV = 2 * Q_BYTES;
+    static constexpr int OFF_Q = 0;                 // 2 buffers x 2 query tiles
+    static constexpr int OFF_KV = 4 * Q_BYTES;
     static constexpr int STAGE_BYTES = 2 * KV_BYTES;
     static constexpr int OFF_BAR = OFF_KV + kStages * STAGE_BYTES;
     static constexpr int SMEM = OFF_BAR + 256 + 1024;
-    // TMEM columns: S (fp32, 128 keys) and O (fp32, D) per query tile, and P
-    // (bf16 pairs, 64 columns for 128 keys) per query tile
     static constexpr int TM_S0 = 0, TM_S1 = 128, TM_O0 = 256, TM_O1 = 256 + D;
     static constexpr int TM_P0 = 256 + 2 * D, TM_P1 = 256 + 2 * D + BN / 2;
     static constexpr int TM_COLS = 512;
@@ -59,22 +68,66 @@ struct Cfg {
 };
 
 // barrier slots
-enum { B_Q = 0, B_KVF = 1, B_KVE = 1 + kStages, B_SF = 1 + 2 * kStages, B_SE = B_SF + 2, B_PF = B_SE + 2,
-       B_OD = B_PF + 2, B_COUNT = B_OD + 2 };
+enum {
+    B_QF = 0,                    // 2: query buffer loaded
+    B_QE = 2,                    // 2: query buffer free (its last S finished)
+    B_KVF = 4,                   // kStages: key/value stage loaded
+    B_KVE = 4 + kStages,         // kStages: key/value stage free
+    B_SF = 4 + 2 * kStages,      // 2: S ready (per warpgroup)
+    B_SE = B_SF + 2,             // 2: S drained into registers
+    B_PF = B_SE + 2,             // 2: P written (and O rescaled)
+    B_OD = B_PF + 2,             // 2: PV finished
+    B_OF = B_OD + 2,             // 2: O read out by the epilogue
+    B_COUNT = B_OF + 2
+};
 
 struct Params {
     __nv_bfloat16 *o;
     float *lse;
     long long out_stride;
-    int T, H, n_pairs;
-    float scale_log2;     // log2(e) / sqrt(d)
+    int T, H, B, n_pairs, n_items;
+    float scale_log2;            // log2(e) / sqrt(d)
     int *err;
+    int use_list;                // 1: per-CTA lists below; 0: round-robin over items
+    unsigned short list_off[kMaxCtas + 1];
+    unsigned short list[kMaxItems];
 };
+
+struct Item {
+    int h, b, q0, n0, n1, n_kv;
+    bool has_q1;
+};
+
+// item i in longest-first order: pairs from the last (most key tiles) down
+__device__ __forceinline__ Item decode_item(const Params &p, int i) {
+    Item it;
+    const int hb = p.H * p.B;
+    const int pair = p.n_pairs - 1 - i / hb;
+    const int r = i % hb;
+    it.h = r % p.H;
+    it.b = r / p.H;
+    it.q0 = pair * 2 * BM;
+    it.has_q1 = (it.q0 + BM) < p.T;
+    it.n0 = it.q0 / BN + 1;
+    it.n1 = it.has_q1 ? it.n0 + 1 : 0;
+    it.n_kv = it.has_q1 ? it.n1 : it.n0;
+    return it;
+}
+
+// the k-th item of this CTA, or -1
+__device__ __forceinline__ int item_of(const Params &p, int k) {
+    if (p.use_list) {
+        const int idx = p.list_off[blockIdx.x] + k;
+        return idx < p.list_off[blockIdx.x + 1] ? (int)p.list[idx] : -1;
+    }
+    const int i = (int)blockIdx.x + k * (int)gridDim.x;
+    return i < p.n_items ? i : -1;
+}
 
 template <int D>
 __global__ void __launch_bounds__(kThreads, 1)
 fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
-           const __grid_constant__ CUtensorMap tv, const Params p)
+           const __grid_constant__ CUtensorMap tv, const __grid_constant__ Params p)
 {
     using C = Cfg<D>;
     static_assert(D == 64, "this kernel instance covers head_dim 64");
@@ -85,29 +138,22 @@ fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
     const uint32_t sQ = base + C::OFF_Q, sKV = base + C::OFF_KV;
     const uint32_t bar0 = base + C::OFF_BAR;
 #define BAR(i) (bar0 + 8u * (uint32_t)(i))
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sb + C::OFF_BAR + 128);
-    volatile int *abort_flag = reinterpret_cast<volatile int *>(sb + C::OFF_BAR + 132);
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sb + C::OFF_BAR + 192);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(sb + C::OFF_BAR + 196);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    // the pair index is the slowest grid dimension, so every CTA of the
-    // heaviest pairs (most key tiles) is issued before any lighter one
-    const int pair = p.n_pairs - 1 - (int)blockIdx.z;
-    const int h = blockIdx.x, b = blockIdx.y;
-    const int q0 = pair * 2 * BM;
-    const bool has_q1 = (q0 + BM) < p.T;
-    const int n0 = q0 / BN + 1;                  // key tiles of query tile 0 (last is diagonal)
-    const int n1 = has_q1 ? n0 + 1 : 0;          // key tiles of query tile 1
-    const int n_kv = has_q1 ? n1 : n0;           // key tiles streamed by this CTA
 
     if (threadIdx.x == 0) {
-        mbar_init(BAR(B_Q), 1);
-        for (int s = 0; s < kStages; s++) { mbar_init(BAR(B_KVF + s), 1); mbar_init(BAR(B_KVE + s), 1); }
         for (int i = 0; i < 2; i++) {
+            mbar_init(BAR(B_QF + i), 1);
+            mbar_init(BAR(B_QE + i), 1);
             mbar_init(BAR(B_SF + i), 1);
             mbar_init(BAR(B_SE + i), 128);
             mbar_init(BAR(B_PF + i), 128);
             mbar_init(BAR(B_OD + i), 1);
+            mbar_init(BAR(B_OF + i), 128);
         }
+        for (int s = 0; s < kStages; s++) { mbar_init(BAR(B_KVF + s), 1); mbar_init(BAR(B_KVE + s), 1); }
         *abort_flag = 0;
         fence_mbar_init();
     }
@@ -131,28 +177,43 @@ fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
             prefetch_tmap(&tq);
             prefetch_tmap(&tk);
             prefetch_tmap(&tv);
-            mbar_arrive_expect_tx(BAR(B_Q), (has_q1 ? 2 : 1) * C::Q_BYTES);
-            tma_load_3d(sQ, &tq, BAR(B_Q), h * D, q0, b);
-            if (has_q1) tma_load_3d(sQ + C::Q_BYTES, &tq, BAR(B_Q), h * D, q0 + BM, b);
-            for (int j = 0; j < n_kv; j++) {
-                const int st = j % kStages;
-                if (j >= kStages &&
-                    !mbar_wait(BAR(B_KVE + st), ((j / kStages) + 1) & 1, abort_flag, p.err, 0x201))
+            int g = 0;                                  // key/value tiles issued so far
+            bool ok = true;
+            for (int k = 0; ok; k++) {
+                const int id = item_of(p, k);
+                if (id < 0) break;
+                const Item it = decode_item(p, id);
+                const int qb = k & 1;
+                if (k >= 2 && !(ok = mbar_wait(BAR(B_QE + qb), ((k >> 1) + 1) & 1, abort_flag, p.err, 0x201)))
                     break;
-                mbar_arrive_expect_tx(BAR(B_KVF + st), 2 * C::KV_BYTES);
-                const uint32_t dst = sKV + st * C::STAGE_BYTES;
-                tma_load_3d(dst, &tk, BAR(B_KVF + st), h * D, j * BN, b);
-                tma_load_3d(dst + C::KV_BYTES, &tv, BAR(B_KVF + st), h * D, j * BN, b);
+                const uint32_t qdst = sQ + qb * 2 * C::Q_BYTES;
+                mbar_arrive_expect_tx(BAR(B_QF + qb), (it.has_q1 ? 2 : 1) * C::Q_BYTES);
+                tma_load_3d(qdst, &tq, BAR(B_QF + qb), it.h * D, it.q0, it.b);
+                if (it.has_q1) tma_load_3d(qdst + C::Q_BYTES, &tq, BAR(B_QF + qb), it.h * D, it.q0 + BM, it.b);
+                for (int j = 0; j < it.n_kv; j++, g++) {
+                    const int st = g % kStages;
+                    if (g >= kStages &&
+                        !(ok = mbar_wait(BAR(B_KVE + st), ((g / kStages) + 1) & 1, abort_flag, p.err, 0x202)))
+                        break;
+                    mbar_arrive_expect_tx(BAR(B_KVF + st), 2 * C::KV_BYTES);
+                    const uint32_t dst = sKV + st * C::STAGE_BYTES;
+                    tma_load_3d(dst, &tk, BAR(B_KVF + st), it.h * D, j * BN, it.b);
+                    tma_load_3d(dst + C::KV_BYTES, &tv, BAR(B_KVF + st), it.h * D, j * BN, it.b);
+                }
             }
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
         if (lane == 0) {
             constexpr uint32_t idS = idesc_bf16(BM, BN, 0, 0);   // Q, K both K-major
-            constexpr uint32_t idO = idesc_bf16(BM, D, 0, 1);    // P K-major, V MN-major
-            auto issue_S = [&](int i, int j) {
-                const uint32_t ka = sKV + (j % kStages) * C::STAGE_BYTES;
-                const uint32_t qa = sQ + i * C::Q_BYTES;
+            constexpr uint32_t idO = idesc_bf16(BM, D, 0, 1);    // P K-major (TMEM), V MN-major
+            int g = 0;                 // key/value tiles consumed
+            int t[2] = {0, 0};         // tiles processed per warpgroup (S/P/O barrier phases)
+            int kw[2] = {0, 0};        // items processed per warpgroup (O-free phases)
+            bool ok = true;
+            auto issue_S = [&](int i, int qb, int stage) {
+                const uint32_t ka = sKV + stage * C::STAGE_BYTES;
+                const uint32_t qa = sQ + (qb * 2 + i) * C::Q_BYTES;
                 const uint32_t d_t = tmem + (i ? C::TM_S1 : C::TM_S0);
 #pragma unroll
                 for (int kk = 0; kk < D / 16; kk++)
@@ -160,55 +221,66 @@ fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
                                 kk > 0);
                 mma_commit(BAR(B_SF + i));
             };
-            auto issue_PV = [&](int i, int j) {
-                const uint32_t va = sKV + (j % kStages) * C::STAGE_BYTES + C::KV_BYTES;
+            auto issue_PV = [&](int i, int stage, bool first) {
+                const uint32_t va = sKV + stage * C::STAGE_BYTES + C::KV_BYTES;
                 const uint32_t pt = tmem + (i ? C::TM_P1 : C::TM_P0);
                 const uint32_t d_t = tmem + (i ? C::TM_O1 : C::TM_O0);
 #pragma unroll
                 for (int kk = 0; kk < BN / 16; kk++)      // 16 keys = 8 packed TMEM columns per step
                     mma_bf16_ts(d_t, pt + kk * 8, sw128_desc(va + kk * 16 * 128, 16384, 1024), idO,
-                                (j > 0 || kk > 0));
+                                (!first || kk > 0));
                 mma_commit(BAR(B_OD + i));
             };
-            bool ok = mbar_wait(BAR(B_Q), 0, abort_flag, p.err, 0x211) &&
-                      mbar_wait(BAR(B_KVF + 0), 0, abort_flag, p.err, 0x212);
-            if (ok) {
+            // S of warpgroup i for its global tile index ti, key stage of tile g+j
+            auto s_step = [&](int i, int qb, int ti, int gj) -> bool {
+                if (ti > 0 && !mbar_wait(BAR(B_SE + i), (ti - 1) & 1, abort_flag, p.err, 0x211 + i)) return false;
                 tc_fence_after();
-                issue_S(0, 0);
-                if (has_q1) issue_S(1, 0);
-            }
-            // Per key tile j: the scores of tile j+1 are issued as soon as each
-            // warpgroup has drained its S buffer (it does so right after loading
-            // S_j, before its softmax), so S_{j+1} is ready by the time P_j is;
-            // the PV products of tile j follow when P_j arrives.  A warpgroup
-            // therefore never waits for its own MMAs between tiles.
-            for (int j = 0; ok && j < n_kv; j++) {
-                const int nx = j + 1, nst = nx % kStages;
-                const bool s0_next = nx < n0, s1_next = has_q1 && nx < n1;
-                if (s0_next || s1_next) {
-                    if (!(ok = mbar_wait(BAR(B_KVF + nst), (nx / kStages) & 1, abort_flag, p.err, 0x214))) break;
+                issue_S(i, qb, gj % kStages);
+                return true;
+            };
+            for (int k = 0; ok; k++) {
+                const int id = item_of(p, k);
+                if (id < 0) break;
+                const Item it = decode_item(p, id);
+                const int qb = k & 1;
+                if (!(ok = mbar_wait(BAR(B_QF + qb), (k >> 1) & 1, abort_flag, p.err, 0x213))) break;
+                if (!(ok = mbar_wait(BAR(B_KVF + g % kStages), (g / kStages) & 1, abort_flag, p.err, 0x214))) break;
+                const int b0 = t[0], b1 = t[1];
+                if (!(ok = s_step(0, qb, b0, g))) break;
+                if (it.has_q1 && !(ok = s_step(1, qb, b1, g))) break;
+                for (int j = 0; ok && j < it.n_kv; j++) {
+                    const int nx = j + 1;
+                    const bool s0_next = nx < it.n0, s1_next = it.has_q1 && nx < it.n1;
+                    if (s0_next || s1_next) {
+                        if (!(ok = mbar_wait(BAR(B_KVF + (g + nx) % kStages), ((g + nx) / kStages) & 1, abort_flag,
+                                             p.err, 0x215)))
+                            break;
+                    }
+                    if (s0_next && !(ok = s_step(0, qb, b0 + nx, g + nx))) break;
+                    if (s1_next && !(ok = s_step(1, qb, b1 + nx, g + nx))) break;
+                    if (nx == it.n_kv) mma_commit(BAR(B_QE + qb));   // this item's last S issued
+                    if (j < it.n0) {
+                        if (j == 0 && kw[0] > 0 &&
+                            !(ok = mbar_wait(BAR(B_OF + 0), (kw[0] - 1) & 1, abort_flag, p.err, 0x216)))
+                            break;
+                        if (!(ok = mbar_wait(BAR(B_PF + 0), (b0 + j) & 1, abort_flag, p.err, 0x217))) break;
+                        tc_fence_after();
+                        issue_PV(0, (g + j) % kStages, j == 0);
+                    }
+                    if (it.has_q1) {
+                        if (j == 0 && kw[1] > 0 &&
+                            !(ok = mbar_wait(BAR(B_OF + 1), (kw[1] - 1) & 1, abort_flag, p.err, 0x218)))
+                            break;
+                        if (!(ok = mbar_wait(BAR(B_PF + 1), (b1 + j) & 1, abort_flag, p.err, 0x219))) break;
+                        tc_fence_after();
+                        issue_PV(1, (g + j) % kStages, j == 0);
+                    }
+                    mma_commit(BAR(B_KVE + (g + j) % kStages));   // stage free once these MMAs finish
                 }
-                if (s0_next) {
-                    if (!(ok = mbar_wait(BAR(B_SE + 0), j & 1, abort_flag, p.err, 0x215))) break;
-                    tc_fence_after();
-                    issue_S(0, nx);
-                }
-                if (s1_next) {
-                    if (!(ok = mbar_wait(BAR(B_SE + 1), j & 1, abort_flag, p.err, 0x218))) break;
-                    tc_fence_after();
-                    issue_S(1, nx);
-                }
-                if (j < n0) {
-                    if (!(ok = mbar_wait(BAR(B_PF + 0), j & 1, abort_flag, p.err, 0x213))) break;
-                    tc_fence_after();
-                    issue_PV(0, j);
-                }
-                if (has_q1) {
-                    if (!(ok = mbar_wait(BAR(B_PF + 1), j & 1, abort_flag, p.err, 0x216))) break;
-                    tc_fence_after();
-                    issue_PV(1, j);
-                }
-                mma_commit(BAR(B_KVE + j % kStages));      // stage j free once these MMAs finish
+                g += it.n_kv;
+                t[0] += it.n0;
+                kw[0] += 1;
+                if (it.has_q1) { t[1] += it.n1; kw[1] += 1; }
             }
         }
     } else if (warp >= 4) {
@@ -217,123 +289,135 @@ fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
         const int wg = (warp - 4) >> 2;
         const int quad = warp & 3;                   // TMEM lane quadrant of this warp
         const int row = quad * 32 + lane;            // query row within the tile
-        const int n = wg ? n1 : n0;
-        const int qs = q0 + wg * BM;
         const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
         const uint32_t tS = tmem + lane_base + (wg ? C::TM_S1 : C::TM_S0);
         const uint32_t tO = tmem + lane_base + (wg ? C::TM_O1 : C::TM_O0);
         const uint32_t tP = tmem + lane_base + (wg ? C::TM_P1 : C::TM_P0);
-        float m_run = -INFINITY, l_run = 0.f;
+        int t = 0;                                   // global tile index of this warpgroup
         bool ok = true;
-        for (int j = 0; j < n; j++) {
-            ok = mbar_wait(BAR(B_SF + wg), j & 1, abort_flag, p.err, 0x221);
-            if (!(ok = __all_sync(0xffffffffu, ok))) break;   // tcgen05.ld below is warp-collective
+        for (int k = 0; ok; k++) {
+            const int id = item_of(p, k);
+            if (id < 0) break;
+            const Item it = decode_item(p, id);
+            const int n = wg ? it.n1 : it.n0;
+            if (n == 0) continue;                    // no second query tile in this item
+            const int qs = it.q0 + wg * BM;
+            float m_run = -INFINITY, l_run = 0.f;
+            for (int j = 0; j < n; j++, t++) {
+                ok = mbar_wait(BAR(B_SF + wg), t & 1, abort_flag, p.err, 0x221);
+                if (!(ok = __all_sync(0xffffffffu, ok))) break;   // tcgen05.ld below is warp-collective
+                tc_fence_after();
+                uint32_t s[128];
+#pragma unroll
+                for (int q4 = 0; q4 < 4; q4++) {     // (copies keep `s` in registers)
+                    uint32_t tt[32];
+                    tmem_ld32(tS + 32 * q4, tt);
+#pragma unroll
+                    for (int c = 0; c < 32; c++) s[32 * q4 + c] = tt[c];
+                }
+                tmem_wait_ld();
+                tc_fence_before();
+                mbar_arrive(BAR(B_SE + wg));         // S buffer may be overwritten now
+
+                // row max as 8 independent partial chains
+                float mp[8];
+#pragma unroll
+                for (int i = 0; i < 8; i++) mp[i] = -INFINITY;
+                if (j == n - 1) {                    // diagonal tile: keys past the query row are masked
+#pragma unroll
+                    for (int c = 0; c < 128; c++) {
+                        const float v = c > row ? -INFINITY : __uint_as_float(s[c]);
+                        s[c] = __float_as_uint(v);
+                        mp[c & 7] = fmaxf(mp[c & 7], v);
+                    }
+                } else {
+#pragma unroll
+                    for (int c = 0; c < 128; c++) mp[c & 7] = fmaxf(mp[c & 7], __uint_as_float(s[c]));
+                }
+                float mx = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])),
+                                 fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
+                mx *= p.scale_log2;
+                float alpha = 1.f;
+                const bool grow = mx > m_run + 8.f;  // also true on the first tile
+                if (grow) {
+                    alpha = ex2(m_run - mx);
+                    m_run = mx;
+                    l_run *= alpha;
+                }
+                const float neg_m = -m_run;
+                float lp[8];
+#pragma unroll
+                for (int i = 0; i < 8; i++) lp[i] = 0.f;
+#pragma unroll
+                for (int c = 0; c < 128; c++) {
+                    const float e = ex2(fmaf(__uint_as_float(s[c]), p.scale_log2, neg_m));
+                    s[c] = __float_as_uint(e);
+                    lp[c & 7] += e;
+                }
+                l_run += ((lp[0] + lp[1]) + (lp[2] + lp[3])) + ((lp[4] + lp[5]) + (lp[6] + lp[7]));
+                // P and O belong to the previous PV (maybe of the previous item) until it completes
+                if (t > 0) ok = mbar_wait(BAR(B_OD + wg), (t - 1) & 1, abort_flag, p.err, 0x222);
+                if (!(ok = __all_sync(0xffffffffu, ok))) break;
+                tc_fence_after();
+                // P row -> TMEM as bf16 pairs (keys 2c, 2c+1 in column c): the A
+                // operand of the next PV product
+#pragma unroll
+                for (int half = 0; half < 2; half++) {
+                    uint32_t tt[32];
+#pragma unroll
+                    for (int c = 0; c < 32; c++)
+                        tt[c] = pack_bf16(__uint_as_float(s[64 * half + 2 * c]),
+                                          __uint_as_float(s[64 * half + 2 * c + 1]));
+                    tmem_st32(tP + 32 * half, tt);
+                }
+                // rows whose max did not grow keep alpha = 1; the TMEM round trip is
+                // warp-collective, so a warp rescales if any of its rows needs it
+                if (__any_sync(0xffffffffu, j > 0 && grow)) {
+                    uint32_t o[32];
+#pragma unroll
+                    for (int c0 = 0; c0 < D; c0 += 32) {
+                        tmem_ld32(tO + c0, o);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int c = 0; c < 32; c++) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
+                        tmem_st32(tO + c0, o);
+                    }
+                }
+                tmem_wait_st();                      // P (and O) stores complete before the MMA reads them
+                tc_fence_before();
+                mbar_arrive(BAR(B_PF + wg));
+            }
+            if (!ok) break;
+            // epilogue: O of this item, then release the O accumulator
+            ok = mbar_wait(BAR(B_OD + wg), (t - 1) & 1, abort_flag, p.err, 0x223);
+            if (!(ok = __all_sync(0xffffffffu, ok))) break;
             tc_fence_after();
-            uint32_t s[128];
+            uint32_t o[D];
 #pragma unroll
-            for (int q4 = 0; q4 < 4; q4++) {         // (copies keep `s` in registers)
-                uint32_t t[32];
-                tmem_ld32(tS + 32 * q4, t);
+            for (int c0 = 0; c0 < D; c0 += 32) {
+                uint32_t tt[32];
+                tmem_ld32(tO + c0, tt);
 #pragma unroll
-                for (int c = 0; c < 32; c++) s[32 * q4 + c] = t[c];
+                for (int c = 0; c < 32; c++) o[c0 + c] = tt[c];
             }
             tmem_wait_ld();
             tc_fence_before();
-            mbar_arrive(BAR(B_SE + wg));             // S buffer may be overwritten now
-
-            // row max as 8 independent partial chains (a single 128-long chain of
-            // dependent max operations would serialise on instruction latency)
-            float mp[8];
-#pragma unroll
-            for (int i = 0; i < 8; i++) mp[i] = -INFINITY;
-            if (j == n - 1) {                        // diagonal tile: keys past the query row are masked
-#pragma unroll
-                for (int c = 0; c < 128; c++) {
-                    const float v = c > row ? -INFINITY : __uint_as_float(s[c]);
-                    s[c] = __float_as_uint(v);
-                    mp[c & 7] = fmaxf(mp[c & 7], v);
-                }
-            } else {
-#pragma unroll
-                for (int c = 0; c < 128; c++) mp[c & 7] = fmaxf(mp[c & 7], __uint_as_float(s[c]));
-            }
-            float mx = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])),
-                             fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
-            mx *= p.scale_log2;
-            float alpha = 1.f;
-            const bool grow = mx > m_run + 8.f;      // also true on the first tile
-            if (grow) {
-                alpha = ex2(m_run - mx);
-                m_run = mx;
-                l_run *= alpha;
-            }
-            const float neg_m = -m_run;
-            float lp[8];
-#pragma unroll
-            for (int i = 0; i < 8; i++) lp[i] = 0.f;
-#pragma unroll
-            for (int c = 0; c < 128; c++) {
-                const float e = ex2(fmaf(__uint_as_float(s[c]), p.scale_log2, neg_m));
-                s[c] = __float_as_uint(e);
-                lp[c & 7] += e;
-            }
-            l_run += ((lp[0] + lp[1]) + (lp[2] + lp[3])) + ((lp[4] + lp[5]) + (lp[6] + lp[7]));
-            // P buffer and O are in use by the previous PV until it completes
-            if (j > 0) ok = mbar_wait(BAR(B_OD + wg), (j - 1) & 1, abort_flag, p.err, 0x222);
-            if (!(ok = __all_sync(0xffffffffu, ok))) break;
-            tc_fence_after();
-            // P row -> TMEM as bf16 pairs (keys 2c, 2c+1 in column c): the A
-            // operand of the next PV product
-#pragma unroll
-            for (int half = 0; half < 2; half++) {
-                uint32_t t[32];
-#pragma unroll
-                for (int c = 0; c < 32; c++)
-                    t[c] = pack_bf16(__uint_as_float(s[64 * half + 2 * c]), __uint_as_float(s[64 * half + 2 * c + 1]));
-                tmem_st32(tP + 32 * half, t);
-            }
-            // rows whose max did not grow keep alpha = 1; the TMEM round trip is
-            // warp-collective, so a warp rescales if any of its rows needs it
-            if (__any_sync(0xffffffffu, j > 0 && grow)) {
-                uint32_t o[32];
-#pragma unroll
-                for (int c0 = 0; c0 < D; c0 += 32) {
-                    tmem_ld32(tO + c0, o);
-                    tmem_wait_ld();
-#pragma unroll
-                    for (int c = 0; c < 32; c++) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
-                    tmem_st32(tO + c0, o);
-                }
-            }
-            tmem_wait_st();                          // P (and O) stores complete before the MMA reads them
-            tc_fence_before();
-            mbar_arrive(BAR(B_PF + wg));
-        }
-        if (ok && n > 0) ok = mbar_wait(BAR(B_OD + wg), (n - 1) & 1, abort_flag, p.err, 0x223);
-        if (__all_sync(0xffffffffu, ok && n > 0)) {
-            tc_fence_after();
+            mbar_arrive(BAR(B_OF + wg));             // the next item's first PV may overwrite O
             const int qrow = qs + row;
-            const float inv = 1.f / l_run;
-            uint32_t o[32];
+            if (qrow < p.T) {
+                const float inv = 1.f / l_run;
+                __nv_bfloat16 *dst = p.o + ((long long)it.b * p.T + qrow) * p.out_stride + (long long)it.h * D;
 #pragma unroll
-            for (int c0 = 0; c0 < D; c0 += 32) {
-                tmem_ld32(tO + c0, o);
-                tmem_wait_ld();
-                if (qrow < p.T) {
-                    __nv_bfloat16 *dst = p.o + ((long long)b * p.T + qrow) * p.out_stride + (long long)h * D + c0;
-#pragma unroll
-                    for (int c = 0; c < 32; c += 8) {
-                        uint4 v;
-                        v.x = pack_bf16(__uint_as_float(o[c + 0]) * inv, __uint_as_float(o[c + 1]) * inv);
-                        v.y = pack_bf16(__uint_as_float(o[c + 2]) * inv, __uint_as_float(o[c + 3]) * inv);
-                        v.z = pack_bf16(__uint_as_float(o[c + 4]) * inv, __uint_as_float(o[c + 5]) * inv);
-                        v.w = pack_bf16(__uint_as_float(o[c + 6]) * inv, __uint_as_float(o[c + 7]) * inv);
-                        *reinterpret_cast<uint4 *>(dst + c) = v;
-                    }
+                for (int c = 0; c < D; c += 8) {
+                    uint4 v;
+                    v.x = pack_bf16(__uint_as_float(o[c + 0]) * inv, __uint_as_float(o[c + 1]) * inv);
+                    v.y = pack_bf16(__uint_as_float(o[c + 2]) * inv, __uint_as_float(o[c + 3]) * inv);
+                    v.z = pack_bf16(__uint_as_float(o[c + 4]) * inv, __uint_as_float(o[c + 5]) * inv);
+                    v.w = pack_bf16(__uint_as_float(o[c + 6]) * inv, __uint_as_float(o[c + 7]) * inv);
+                    *reinterpret_cast<uint4 *>(dst + c) = v;
                 }
+                if (p.lse) p.lse[((long long)it.b * p.H + it.h) * p.T + qrow] = (m_run + __log2f(l_run)) * kLn2;
             }
-            if (p.lse && qrow < p.T)
-                p.lse[((long long)b * p.H + h) * p.T + qrow] = (m_run + __log2f(l_run)) * kLn2;
         }
     }
 
@@ -392,6 +476,32 @@ bool fwd_bf16_sm100_supported(int D, long long in_stride, long long out_stride) 
     return D == 64 && in_stride % 8 == 0 && out_stride % 8 == 0 && encode_fn() != nullptr;
 }
 
+// Longest-processing-time-first deal of the items (already in descending
+// cost order) to `ctas` CTAs; item cost = key tiles of both query tiles plus
+// a fixed per-item overhead.
+static void lpt_schedule(attn::fa::Params &p, int ctas) {
+    using namespace attn::fa;
+    std::vector<std::vector<unsigned short>> lists(ctas);
+    std::vector<long long> load(ctas, 0);
+    const int hb = p.H * p.B;
+    for (int i = 0; i < p.n_items; i++) {
+        const int pair = p.n_pairs - 1 - i / hb;
+        const int q0 = pair * 2 * BM;
+        const bool has_q1 = (q0 + BM) < p.T;
+        const int n0 = q0 / BN + 1;
+        const long long cost = n0 + (has_q1 ? n0 + 1 : 0) + 2;
+        const int c = (int)(std::min_element(load.begin(), load.end()) - load.begin());
+        lists[c].push_back((unsigned short)i);
+        load[c] += cost;
+    }
+    int off = 0;
+    for (int c = 0; c < ctas; c++) {
+        p.list_off[c] = (unsigned short)off;
+        for (unsigned short v : lists[c]) p.list[off++] = v;
+    }
+    p.list_off[ctas] = (unsigned short)off;
+}
+
 int launch_fwd_bf16_sm100(int D, const void *q, const void *k, const void *v, void *o, float *lse,
                           long long in_stride, long long out_stride, int B, int H, int T, int *err,
                           cudaStream_t s) {
@@ -403,20 +513,27 @@ int launch_fwd_bf16_sm100(int D, const void *q, const void *k, const void *v, vo
     if (!make_map(&tq, q, H * D, T, B, in_stride) || !make_map(&tk, k, H * D, T, B, in_stride) ||
         !make_map(&tv, v, H * D, T, B, in_stride))
         return set_error(ATTN_ERR_CUDA, "tcgen05 forward: cuTensorMapEncodeTiled failed");
-    Params p;
+    static thread_local Params p;   // large (schedule inside); copied into the launch
     p.o = static_cast<__nv_bfloat16 *>(o);
     p.lse = lse;
     p.out_stride = out_stride;
     p.T = T;
     p.H = H;
+    p.B = B;
     p.n_pairs = (T + 2 * BM - 1) / (2 * BM);
+    p.n_items = p.n_pairs * H * B;
     p.scale_log2 = attn::kLog2e / sqrtf((float)D);
     p.err = err;
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int ctas = std::max(1, std::min(std::min(sms, kMaxCtas), p.n_items));
+    p.use_list = p.n_items <= kMaxItems;
+    if (p.use_list) lpt_schedule(p, ctas);
     const size_t smem = Cfg<64>::SMEM;
     if (!ensure_smem_attr((const void *)fwd_kernel<64>, smem))
         return set_error(ATTN_ERR_CUDA, "tcgen05 forward: cannot set shared-memory size");
-    dim3 grid(H, B, p.n_pairs);
-    fwd_kernel<64><<<grid, kThreads, smem, s>>>(tq, tk, tv, p);
+    fwd_kernel<64><<<ctas, kThreads, smem, s>>>(tq, tk, tv, p);
     return check_launch("tcgen05 forward kernel");
 }
 
