@@ -88,9 +88,8 @@ struct Params {
     int T, H, B, n_pairs, n_items;
     float scale_log2;            // log2(e) / sqrt(d)
     int *err;
-    int use_list;                // 1: per-CTA lists below; 0: round-robin over items
-    unsigned short list_off[kMaxCtas + 1];
-    unsigned short list[kMaxItems];
+    int use_list;                // 1: per-CTA lists in `sched`; 0: round-robin over items
+    const unsigned short *sched; // [kMaxCtas + 1] list offsets, then the item lists
 };
 
 struct Item {
@@ -117,8 +116,8 @@ __device__ __forceinline__ Item decode_item(const Params &p, int i) {
 // the k-th item of this CTA, or -1
 __device__ __forceinline__ int item_of(const Params &p, int k) {
     if (p.use_list) {
-        const int idx = p.list_off[blockIdx.x] + k;
-        return idx < p.list_off[blockIdx.x + 1] ? (int)p.list[idx] : -1;
+        const int idx = (int)__ldg(p.sched + blockIdx.x) + k;
+        return idx < (int)__ldg(p.sched + blockIdx.x + 1) ? (int)__ldg(p.sched + kMaxCtas + 1 + idx) : -1;
     }
     const int i = (int)blockIdx.x + k * (int)gridDim.x;
     return i < p.n_items ? i : -1;
@@ -211,24 +210,26 @@ fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
             int t[2] = {0, 0};         // tiles processed per warpgroup (S/P/O barrier phases)
             int kw[2] = {0, 0};        // items processed per warpgroup (O-free phases)
             bool ok = true;
+            // Descriptors of consecutive K-steps differ only in the start-address
+            // field (bits 0-13, 16-byte units), so each step adds a constant to a
+            // base descriptor: the issuing thread shares its SMSP with two busy
+            // softmax warps, and rebuilding descriptors per MMA starved it.
             auto issue_S = [&](int i, int qb, int stage) {
-                const uint32_t ka = sKV + stage * C::STAGE_BYTES;
-                const uint32_t qa = sQ + (qb * 2 + i) * C::Q_BYTES;
+                const uint64_t kd = sw128_desc(sKV + stage * C::STAGE_BYTES, 16, 1024);
+                const uint64_t qd = sw128_desc(sQ + (qb * 2 + i) * C::Q_BYTES, 16, 1024);
                 const uint32_t d_t = tmem + (i ? C::TM_S1 : C::TM_S0);
 #pragma unroll
-                for (int kk = 0; kk < D / 16; kk++)
-                    mma_bf16_ss(d_t, sw128_desc(qa + kk * 32, 16, 1024), sw128_desc(ka + kk * 32, 16, 1024), idS,
-                                kk > 0);
+                for (int kk = 0; kk < D / 16; kk++)          // +32 bytes along K per step
+                    mma_bf16_ss(d_t, qd + 2 * kk, kd + 2 * kk, idS, kk > 0);
                 mma_commit(BAR(B_SF + i));
             };
             auto issue_PV = [&](int i, int stage, bool first) {
-                const uint32_t va = sKV + stage * C::STAGE_BYTES + C::KV_BYTES;
+                const uint64_t vd = sw128_desc(sKV + stage * C::STAGE_BYTES + C::KV_BYTES, 16384, 1024);
                 const uint32_t pt = tmem + (i ? C::TM_P1 : C::TM_P0);
                 const uint32_t d_t = tmem + (i ? C::TM_O1 : C::TM_O0);
 #pragma unroll
-                for (int kk = 0; kk < BN / 16; kk++)      // 16 keys = 8 packed TMEM columns per step
-                    mma_bf16_ts(d_t, pt + kk * 8, sw128_desc(va + kk * 16 * 128, 16384, 1024), idO,
-                                (!first || kk > 0));
+                for (int kk = 0; kk < BN / 16; kk++)      // 16 keys per step: 8 packed TMEM columns of P,
+                    mma_bf16_ts(d_t, pt + kk * 8, vd + 128 * kk, idO, (!first || kk > 0));   // 2 KB of V
                 mma_commit(BAR(B_OD + i));
             };
             // S of warpgroup i for its global tile index ti, key stage of tile g+j
@@ -319,23 +320,19 @@ fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
                 tc_fence_before();
                 mbar_arrive(BAR(B_SE + wg));         // S buffer may be overwritten now
 
-                // row max as 8 independent partial chains
+                // row max: 8 independent chains of 3-input max
                 float mp[8];
 #pragma unroll
                 for (int i = 0; i < 8; i++) mp[i] = -INFINITY;
                 if (j == n - 1) {                    // diagonal tile: keys past the query row are masked
 #pragma unroll
-                    for (int c = 0; c < 128; c++) {
-                        const float v = c > row ? -INFINITY : __uint_as_float(s[c]);
-                        s[c] = __float_as_uint(v);
-                        mp[c & 7] = fmaxf(mp[c & 7], v);
-                    }
-                } else {
-#pragma unroll
-                    for (int c = 0; c < 128; c++) mp[c & 7] = fmaxf(mp[c & 7], __uint_as_float(s[c]));
+                    for (int c = 0; c < 128; c++)
+                        if (c > row) s[c] = __float_as_uint(-INFINITY);
                 }
-                float mx = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])),
-                                 fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
+#pragma unroll
+                for (int c = 0; c < 128; c += 2)
+                    mp[(c >> 1) & 7] = max3(mp[(c >> 1) & 7], __uint_as_float(s[c]), __uint_as_float(s[c + 1]));
+                float mx = max3(max3(mp[0], mp[1], mp[2]), max3(mp[3], mp[4], mp[5]), fmaxf(mp[6], mp[7]));
                 mx *= p.scale_log2;
                 float alpha = 1.f;
                 const bool grow = mx > m_run + 8.f;  // also true on the first tile
@@ -344,17 +341,33 @@ fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
                     m_run = mx;
                     l_run *= alpha;
                 }
-                const float neg_m = -m_run;
-                float lp[8];
+                // p = 2^(s*scale - m), pairwise: packed argument and sums (two
+                // lanes of work per issue slot: the softmax warps share their
+                // SMSPs with the MMA-issuing thread), exp2 on MUFU; bf16 pairs
+                // packed on the fly for the TMEM store
+                const uint64_t scale2 = f2(p.scale_log2, p.scale_log2);
+                const uint64_t negm2 = f2(-m_run, -m_run);
+                uint64_t lp2[4];
 #pragma unroll
-                for (int i = 0; i < 8; i++) lp[i] = 0.f;
+                for (int i = 0; i < 4; i++) lp2[i] = 0ull;
+                uint32_t pk[64];
 #pragma unroll
-                for (int c = 0; c < 128; c++) {
-                    const float e = ex2(fmaf(__uint_as_float(s[c]), p.scale_log2, neg_m));
-                    s[c] = __float_as_uint(e);
-                    lp[c & 7] += e;
+                for (int c2 = 0; c2 < 64; c2++) {
+                    const uint64_t x2 = fma2(f2(__uint_as_float(s[2 * c2]), __uint_as_float(s[2 * c2 + 1])), scale2, negm2);
+                    float xl, xh;
+                    f2_split(x2, xl, xh);
+                    const uint64_t e2 = f2(ex2(xl), ex2(xh));
+                    lp2[c2 & 3] = add2(lp2[c2 & 3], e2);
+                    float el, eh;
+                    f2_split(e2, el, eh);
+                    pk[c2] = pack_bf16(el, eh);
                 }
-                l_run += ((lp[0] + lp[1]) + (lp[2] + lp[3])) + ((lp[4] + lp[5]) + (lp[6] + lp[7]));
+                {
+                    const uint64_t l2 = add2(add2(lp2[0], lp2[1]), add2(lp2[2], lp2[3]));
+                    float ll, lh;
+                    f2_split(l2, ll, lh);
+                    l_run += ll + lh;
+                }
                 // P and O belong to the previous PV (maybe of the previous item) until it completes
                 if (t > 0) ok = mbar_wait(BAR(B_OD + wg), (t - 1) & 1, abort_flag, p.err, 0x222);
                 if (!(ok = __all_sync(0xffffffffu, ok))) break;
@@ -365,9 +378,7 @@ fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
                 for (int half = 0; half < 2; half++) {
                     uint32_t tt[32];
 #pragma unroll
-                    for (int c = 0; c < 32; c++)
-                        tt[c] = pack_bf16(__uint_as_float(s[64 * half + 2 * c]),
-                                          __uint_as_float(s[64 * half + 2 * c + 1]));
+                    for (int c = 0; c < 32; c++) tt[c] = pk[32 * half + c];
                     tmem_st32(tP + 32 * half, tt);
                 }
                 // rows whose max did not grow keep alpha = 1; the TMEM round trip is
@@ -478,8 +489,8 @@ bool fwd_bf16_sm100_supported(int D, long long in_stride, long long out_stride) 
 
 // Longest-processing-time-first deal of the items (already in descending
 // cost order) to `ctas` CTAs; item cost = key tiles of both query tiles plus
-// a fixed per-item overhead.
-static void lpt_schedule(attn::fa::Params &p, int ctas) {
+// a fixed per-item overhead.  Output: [kMaxCtas + 1] offsets, then the lists.
+static void lpt_schedule(const attn::fa::Params &p, int ctas, std::vector<unsigned short> &out) {
     using namespace attn::fa;
     std::vector<std::vector<unsigned short>> lists(ctas);
     std::vector<long long> load(ctas, 0);
@@ -494,12 +505,30 @@ static void lpt_schedule(attn::fa::Params &p, int ctas) {
         lists[c].push_back((unsigned short)i);
         load[c] += cost;
     }
+    out.assign(kMaxCtas + 1 + p.n_items, 0);
     int off = 0;
     for (int c = 0; c < ctas; c++) {
-        p.list_off[c] = (unsigned short)off;
-        for (unsigned short v : lists[c]) p.list[off++] = v;
+        out[c] = (unsigned short)off;
+        for (unsigned short v : lists[c]) out[kMaxCtas + 1 + off++] = v;
     }
-    p.list_off[ctas] = (unsigned short)off;
+    for (int c = ctas; c <= kMaxCtas; c++) out[c] = (unsigned short)off;
+}
+
+// Tensor maps are cached per (pointer, shape): encoding one costs a driver
+// call, and training / benchmark loops reuse the same buffers every step.
+static bool cached_map(CUtensorMap *m, const void *ptr, int cols, int T, int B, long long stride) {
+    struct Entry { const void *ptr; int cols, T, B; long long stride; CUtensorMap map; };
+    static thread_local Entry cache[12];
+    static thread_local int next = 0;
+    for (auto &e : cache)
+        if (e.ptr == ptr && e.cols == cols && e.T == T && e.B == B && e.stride == stride) {
+            *m = e.map;
+            return true;
+        }
+    if (!make_map(m, ptr, cols, T, B, stride)) return false;
+    cache[next] = Entry{ptr, cols, T, B, stride, *m};
+    next = (next + 1) % 12;
+    return true;
 }
 
 int launch_fwd_bf16_sm100(int D, const void *q, const void *k, const void *v, void *o, float *lse,
@@ -510,10 +539,22 @@ int launch_fwd_bf16_sm100(int D, const void *q, const void *k, const void *v, vo
     if (((uintptr_t)q | (uintptr_t)k | (uintptr_t)v | (uintptr_t)o) & 15)
         return set_error(ATTN_ERR_INVALID, "tcgen05 forward: tensors must be 16-byte aligned");
     CUtensorMap tq, tk, tv;
-    if (!make_map(&tq, q, H * D, T, B, in_stride) || !make_map(&tk, k, H * D, T, B, in_stride) ||
-        !make_map(&tv, v, H * D, T, B, in_stride))
+    if (!cached_map(&tq, q, H * D, T, B, in_stride) || !cached_map(&tk, k, H * D, T, B, in_stride) ||
+        !cached_map(&tv, v, H * D, T, B, in_stride))
         return set_error(ATTN_ERR_CUDA, "tcgen05 forward: cuTensorMapEncodeTiled failed");
-    static thread_local Params p;   // large (schedule inside); copied into the launch
+    int dev = 0;
+    cudaGetDevice(&dev);
+    static int sm_count[128] = {0};
+    if (dev < 0 || dev >= 128) return set_error(ATTN_ERR_INVALID, "tcgen05 forward: device %d", dev);
+    if (!sm_count[dev]) {
+        int sms = 148;
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        sm_count[dev] = sms;
+    }
+    // The per-CTA item lists live in a small per-device buffer, rewritten only
+    // when the shape or the CTA count changes (calls on one device are
+    // expected to come from one host thread, like the reference's trainer).
+    Params p;
     p.o = static_cast<__nv_bfloat16 *>(o);
     p.lse = lse;
     p.out_stride = out_stride;
@@ -524,12 +565,29 @@ int launch_fwd_bf16_sm100(int D, const void *q, const void *k, const void *v, vo
     p.n_items = p.n_pairs * H * B;
     p.scale_log2 = attn::kLog2e / sqrtf((float)D);
     p.err = err;
-    int dev = 0, sms = 148;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const int ctas = std::max(1, std::min(std::min(sms, kMaxCtas), p.n_items));
+    const int ctas = std::max(1, std::min(std::min(sm_count[dev], kMaxCtas), p.n_items));
     p.use_list = p.n_items <= kMaxItems;
-    if (p.use_list) lpt_schedule(p, ctas);
+    p.sched = nullptr;
+    if (p.use_list) {
+        static unsigned short *sched_buf[128] = {nullptr};
+        static long long sched_key[128];
+        const long long key = (((long long)T * 4096 + H) * 65536 + B) * 256 + ctas;
+        if (!sched_buf[dev]) {
+            if (cudaMalloc(&sched_buf[dev], (kMaxCtas + 1 + kMaxItems) * sizeof(unsigned short)) != cudaSuccess)
+                return set_error(ATTN_ERR_NOMEM, "tcgen05 forward: cannot allocate the schedule buffer");
+            sched_key[dev] = -1;
+        }
+        if (key != sched_key[dev]) {
+            std::vector<unsigned short> h;
+            lpt_schedule(p, ctas, h);
+            if (cudaMemcpyAsync(sched_buf[dev], h.data(), h.size() * sizeof(unsigned short),
+                                cudaMemcpyHostToDevice, s) != cudaSuccess ||
+                cudaStreamSynchronize(s) != cudaSuccess)
+                return set_error(ATTN_ERR_CUDA, "tcgen05 forward: schedule upload failed");
+            sched_key[dev] = key;
+        }
+        p.sched = sched_buf[dev];
+    }
     const size_t smem = Cfg<64>::SMEM;
     if (!ensure_smem_attr((const void *)fwd_kernel<64>, smem))
         return set_error(ATTN_ERR_CUDA, "tcgen05 forward: cannot set shared-memory size");
