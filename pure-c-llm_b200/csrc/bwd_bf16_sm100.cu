@@ -1,0 +1,419 @@
+// bwd_bf16_sm100.cu -- causal attention backward on the Blackwell tensor cores.
+//
+// Semantics: attention_backward, train.c:373-407, with bf16 Q/K/V/dO/dQ/dK/dV
+// and fp32 scores, statistics and accumulators:
+//   P = exp(S - lse),  dP = dO V^T,  dS = P (dP - D) / sqrt(d),  D_i = dO_i . O_i
+//   dV = P^T dO,  dK = dS^T Q,  dQ = dS K
+// P is rebuilt from the forward's lse; the row statistics (lse in base 2, D)
+// come from the shared rowdot pre-pass into the workspace.
+//
+// Two deterministic kernels (no atomics), each one CTA per 128-row tile of one
+// (batch, head), 8 warps: warp 0 TMA producer, warp 1 MMA issuer (one
+// thread), warps 4-7 an elementwise warpgroup (one thread per TMEM lane = one
+// row of the CTA's tile); warps 2-3 idle.
+//   dkdv: key tile kt, loops over query tiles i >= kt.  S^T = K Q_i^T and
+//         dP^T = V dO_i^T (both operands in shared memory) into TMEM; the
+//         warpgroup writes P^T and dS^T as bf16 pairs into TMEM; then
+//         dV += P^T dO_i and dK += dS^T Q_i read them from TMEM (A operand)
+//         with dO_i / Q_i from shared memory (MN-major B operand).
+//   dq:   query tile qt, loops over key tiles j <= qt.  S = Q K_j^T and
+//         dP = dO V_j^T, dS into TMEM, dQ += dS K_j.
+// The MMA warp issues the next tile's S/dP as soon as the warpgroup has read
+// the current ones, so those products overlap the elementwise work.
+// Every mbarrier wait is bounded (device error word + abort flag, as in the
+// forward kernel).
+#include "common.cuh"
+#include "sm100.cuh"
+
+#include <cudaTypedefs.h>
+
+namespace attn {
+namespace fab {
+
+using namespace sm100;
+
+constexpr int BT = 128;           // rows per tile (TMEM lanes) and columns per tile
+constexpr int D = 64;             // head_dim covered by these kernels
+constexpr int kStages = 3;
+constexpr int kThreads = 256;
+constexpr int TILE_BYTES = BT * D * 2;        // one 128 x 64 bf16 tile (16 KB)
+
+// TMEM columns (both kernels): X = S or S^T, Y = dP or dP^T (fp32, 128 each),
+// A1/A2 accumulators (fp32, 64 each), W1/W2 bf16-pair operands (64 each)
+constexpr int TM_X = 0, TM_Y = 128, TM_A1 = 256, TM_A2 = 320, TM_W1 = 384, TM_W2 = 448, TM_COLS = 512;
+
+// barrier slots
+enum { B_FIX = 0, B_SF = 1, B_SE = 1 + kStages, B_XY = 1 + 2 * kStages, B_XYE, B_W, B_ACC, B_COUNT };
+
+struct Params {
+    void *out1, *out2;           // dkdv: dK, dV;  dq: dQ
+    const float *lse2, *dvec;    // [B][H][T]
+    long long out_stride;
+    int T, H, accumulate;
+    float scale_log2;            // log2(e) / sqrt(d)
+    float ds_scale;              // 1 / sqrt(d)
+    int *err;
+};
+
+struct Smem {
+    uint32_t base;
+    uint8_t *ptr;
+};
+
+__device__ __forceinline__ void store_row_bf16(__nv_bfloat16 *dst, const uint32_t (&acc)[D], bool accumulate) {
+#pragma unroll
+    for (int c = 0; c < D; c += 8) {
+        float v[8];
+#pragma unroll
+        for (int u = 0; u < 8; u++) v[u] = __uint_as_float(acc[c + u]);
+        if (accumulate) {
+            const uint4 old = *reinterpret_cast<const uint4 *>(dst + c);
+            const uint32_t w[4] = {old.x, old.y, old.z, old.w};
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const __nv_bfloat162 pr = *reinterpret_cast<const __nv_bfloat162 *>(&w[u]);
+                v[2 * u] += __low2float(pr);
+                v[2 * u + 1] += __high2float(pr);
+            }
+        }
+        uint4 o;
+        o.x = pack_bf16(v[0], v[1]);
+        o.y = pack_bf16(v[2], v[3]);
+        o.z = pack_bf16(v[4], v[5]);
+        o.w = pack_bf16(v[6], v[7]);
+        *reinterpret_cast<uint4 *>(dst + c) = o;
+    }
+}
+
+// KIND 0: dkdv (fixed tiles K, V; streamed Q_i, dO_i), KIND 1: dq (fixed Q, dO;
+// streamed K_j, V_j).  Tensor maps: m_a/m_b are the fixed pair, m_c/m_d the
+// streamed pair, all 3-D {H*D, T, B} views with 64 x 128 boxes, 128B swizzle.
+template <int KIND>
+__global__ void __launch_bounds__(kThreads, 1)
+bwd_kernel(const __grid_constant__ CUtensorMap m_a, const __grid_constant__ CUtensorMap m_b,
+           const __grid_constant__ CUtensorMap m_c, const __grid_constant__ CUtensorMap m_d, const Params p)
+{
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t base = (raw + 1023u) & ~1023u;
+    uint8_t *sb = smem_raw + (base - raw);
+    // layout: fixed A, fixed B, stages x (C, D), row statistics, barriers
+    const uint32_t sA = base, sB = base + TILE_BYTES, sST = base + 2 * TILE_BYTES;
+    const int OFF_STATS = 2 * TILE_BYTES + kStages * 2 * TILE_BYTES;     // kStages x 2 x 128 floats
+    float *stats = reinterpret_cast<float *>(sb + OFF_STATS);
+    const int OFF_BAR = OFF_STATS + kStages * 2 * BT * 4;
+    const uint32_t bar0 = base + OFF_BAR;
+#define BAR(i) (bar0 + 8u * (uint32_t)(i))
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sb + OFF_BAR + 128);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(sb + OFF_BAR + 132);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n_t = (p.T + BT - 1) / BT;
+    const int h = blockIdx.x, b = blockIdx.y;
+    // dkdv: key tile kt = z (small kt has the most query tiles: issued first);
+    // dq: query tile qt = n_t-1-z (large qt has the most key tiles)
+    const int fixed = KIND == 0 ? (int)blockIdx.z : n_t - 1 - (int)blockIdx.z;
+    const int first = KIND == 0 ? fixed : 0;                  // streamed tile range
+    const int count = KIND == 0 ? n_t - fixed : fixed + 1;
+
+    if (threadIdx.x == 0) {
+        mbar_init(BAR(B_FIX), 1);
+        for (int s = 0; s < kStages; s++) { mbar_init(BAR(B_SF + s), 1); mbar_init(BAR(B_SE + s), 1); }
+        mbar_init(BAR(B_XY), 1);
+        mbar_init(BAR(B_XYE), 128);
+        mbar_init(BAR(B_W), 128);
+        mbar_init(BAR(B_ACC), 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 0) {
+        tmem_alloc(smem_u32(tmem_slot), TM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ producer
+        if (lane == 0) {
+            prefetch_tmap(&m_a);
+            prefetch_tmap(&m_b);
+            prefetch_tmap(&m_c);
+            prefetch_tmap(&m_d);
+            mbar_arrive_expect_tx(BAR(B_FIX), 2 * TILE_BYTES);
+            tma_load_3d(sA, &m_a, BAR(B_FIX), h * D, fixed * BT, b);
+            tma_load_3d(sB, &m_b, BAR(B_FIX), h * D, fixed * BT, b);
+            for (int it = 0; it < count; it++) {
+                const int st = it % kStages;
+                if (it >= kStages &&
+                    !mbar_wait(BAR(B_SE + st), ((it / kStages) + 1) & 1, abort_flag, p.err, 0x301))
+                    break;
+                mbar_arrive_expect_tx(BAR(B_SF + st), 2 * TILE_BYTES);
+                const uint32_t dst = sST + st * 2 * TILE_BYTES;
+                tma_load_3d(dst, &m_c, BAR(B_SF + st), h * D, (first + it) * BT, b);
+                tma_load_3d(dst + TILE_BYTES, &m_d, BAR(B_SF + st), h * D, (first + it) * BT, b);
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t idXY = idesc_bf16(BT, BT, 0, 0);    // both operands K-major (along d)
+            constexpr uint32_t idAcc = idesc_bf16(BT, D, 0, 1);    // A from TMEM, B MN-major
+            // X, Y for streamed tile `it`:  dkdv: X = K Q^T, Y = V dO^T;  dq: X = Q K^T, Y = dO V^T
+            auto issue_xy = [&](int it) {
+                const uint32_t stg = sST + (it % kStages) * 2 * TILE_BYTES;
+                const uint64_t fa = sw128_desc(sA, 16, 1024), fb = sw128_desc(sB, 16, 1024);
+                const uint64_t sc = sw128_desc(stg, 16, 1024), sd = sw128_desc(stg + TILE_BYTES, 16, 1024);
+#pragma unroll
+                for (int kk = 0; kk < D / 16; kk++) mma_bf16_ss(tmem + TM_X, fa + 2 * kk, sc + 2 * kk, idXY, kk > 0);
+#pragma unroll
+                for (int kk = 0; kk < D / 16; kk++) mma_bf16_ss(tmem + TM_Y, fb + 2 * kk, sd + 2 * kk, idXY, kk > 0);
+                mma_commit(BAR(B_XY));
+            };
+            // accumulators for streamed tile `it`
+            //   dkdv: A1 (dV) += W1 (P^T) . dO_i,  A2 (dK) += W2 (dS^T) . Q_i
+            //   dq:   A1 (dQ) += W2 (dS) . K_j
+            auto issue_acc = [&](int it) {
+                const uint32_t stg = sST + (it % kStages) * 2 * TILE_BYTES;
+                if (KIND == 0) {
+                    const uint64_t dq_ = sw128_desc(stg, 16384, 1024);          // Q_i, MN-major
+                    const uint64_t ddo = sw128_desc(stg + TILE_BYTES, 16384, 1024);   // dO_i, MN-major
+#pragma unroll
+                    for (int kk = 0; kk < BT / 16; kk++)
+                        mma_bf16_ts(tmem + TM_A1, tmem + TM_W1 + kk * 8, ddo + 128 * kk, idAcc, it > 0 || kk > 0);
+#pragma unroll
+                    for (int kk = 0; kk < BT / 16; kk++)
+                        mma_bf16_ts(tmem + TM_A2, tmem + TM_W2 + kk * 8, dq_ + 128 * kk, idAcc, it > 0 || kk > 0);
+                } else {
+                    const uint64_t dk = sw128_desc(stg, 16384, 1024);           // K_j, MN-major
+#pragma unroll
+                    for (int kk = 0; kk < BT / 16; kk++)
+                        mma_bf16_ts(tmem + TM_A1, tmem + TM_W2 + kk * 8, dk + 128 * kk, idAcc, it > 0 || kk > 0);
+                }
+                mma_commit(BAR(B_ACC));
+                mma_commit(BAR(B_SE + it % kStages));     // streamed stage free
+            };
+            bool ok = mbar_wait(BAR(B_FIX), 0, abort_flag, p.err, 0x311) &&
+                      mbar_wait(BAR(B_SF + 0), 0, abort_flag, p.err, 0x312);
+            if (ok) {
+                tc_fence_after();
+                issue_xy(0);
+            }
+            for (int it = 0; ok && it < count; it++) {
+                if (it + 1 < count) {
+                    const int nx = it + 1;
+                    if (!(ok = mbar_wait(BAR(B_SF + nx % kStages), (nx / kStages) & 1, abort_flag, p.err, 0x313))) break;
+                    if (!(ok = mbar_wait(BAR(B_XYE), it & 1, abort_flag, p.err, 0x314))) break;
+                    tc_fence_after();
+                    issue_xy(nx);
+                }
+                if (!(ok = mbar_wait(BAR(B_W), it & 1, abort_flag, p.err, 0x315))) break;
+                tc_fence_after();
+                issue_acc(it);
+            }
+        }
+    } else if (warp >= 4) {
+        // ------------------------------------------------------------ elementwise
+        const int quad = warp & 3;
+        const int row = quad * 32 + lane;            // TMEM lane = row of the CTA's fixed tile
+        const uint32_t lb = (uint32_t)(quad * 32) << 16;
+        const long long bh = ((long long)b * p.H + h) * p.T;
+        const int grow_ = fixed * BT + row;          // global row index of this thread
+        float my_lse2 = 0.f, my_d = 0.f;             // dq: this query row's statistics
+        if (KIND == 1 && grow_ < p.T) {
+            my_lse2 = __ldg(p.lse2 + bh + grow_);
+            my_d = __ldg(p.dvec + bh + grow_);
+        }
+        bool ok = true;
+        for (int it = 0; it < count; it++) {
+            const int tcol = first + it;             // streamed tile index
+            float *st_l = stats + (it % kStages) * 2 * BT;   // dkdv: lse2 / D of the query columns
+            if (KIND == 0) {
+                const int q = tcol * BT + row;
+                st_l[row] = q < p.T ? __ldg(p.lse2 + bh + q) : 0.f;
+                st_l[BT + row] = q < p.T ? __ldg(p.dvec + bh + q) : 0.f;
+                asm volatile("bar.sync 1, 128;" ::: "memory");
+            }
+            ok = mbar_wait(BAR(B_XY), it & 1, abort_flag, p.err, 0x321);
+            if (it > 0 && ok) ok = mbar_wait(BAR(B_ACC), (it - 1) & 1, abort_flag, p.err, 0x322);
+            if (!(ok = __all_sync(0xffffffffu, ok))) break;
+            tc_fence_after();
+            const bool diag = (tcol == fixed);
+#pragma unroll 1
+            for (int c0 = 0; c0 < BT; c0 += 32) {
+                uint32_t xs[32], ys[32];
+                tmem_ld32(tmem + lb + TM_X + c0, xs);
+                tmem_ld32(tmem + lb + TM_Y + c0, ys);
+                tmem_wait_ld();
+                if (c0 == BT - 32) {                 // X and Y fully read: the next products may start
+                    tc_fence_before();
+                    mbar_arrive(BAR(B_XYE));
+                }
+                uint32_t wp[16], wd[16];
+#pragma unroll
+                for (int c = 0; c < 32; c += 2) {
+                    float pv[2], dv[2];
+#pragma unroll
+                    for (int u = 0; u < 2; u++) {
+                        const int col = c0 + c + u;
+                        float l2, dd;
+                        bool masked;
+                        if (KIND == 0) {             // row = key, col = query
+                            l2 = st_l[col];
+                            dd = st_l[BT + col];
+                            masked = (diag && col < row) || (tcol * BT + col >= p.T);
+                        } else {                     // row = query, col = key
+                            l2 = my_lse2;
+                            dd = my_d;
+                            masked = diag && col > row;
+                        }
+                        const float pr = masked ? 0.f : ex2(fmaf(__uint_as_float(xs[c + u]), p.scale_log2, -l2));
+                        pv[u] = pr;
+                        dv[u] = pr * (__uint_as_float(ys[c + u]) - dd) * p.ds_scale;
+                    }
+                    wp[c / 2] = pack_bf16(pv[0], pv[1]);
+                    wd[c / 2] = pack_bf16(dv[0], dv[1]);
+                }
+                if (KIND == 0) tmem_st16(tmem + lb + TM_W1 + c0 / 2, wp);
+                tmem_st16(tmem + lb + TM_W2 + c0 / 2, wd);
+            }
+            tmem_wait_st();
+            tc_fence_before();
+            mbar_arrive(BAR(B_W));
+        }
+        // epilogue: accumulators -> global
+        if (ok && count > 0) ok = mbar_wait(BAR(B_ACC), (count - 1) & 1, abort_flag, p.err, 0x323);
+        if (__all_sync(0xffffffffu, ok && count > 0)) {
+            tc_fence_after();
+            for (int a = 0; a < (KIND == 0 ? 2 : 1); a++) {
+                uint32_t acc[D];
+#pragma unroll
+                for (int c0 = 0; c0 < D; c0 += 32) {
+                    uint32_t t32[32];
+                    tmem_ld32(tmem + lb + (a ? TM_A2 : TM_A1) + c0, t32);
+#pragma unroll
+                    for (int c = 0; c < 32; c++) acc[c0 + c] = t32[c];
+                }
+                tmem_wait_ld();
+                if (grow_ < p.T) {
+                    // dkdv: a=0 -> dV (out2), a=1 -> dK (out1);  dq: dQ (out1)
+                    void *outp = KIND == 0 ? (a == 0 ? p.out2 : p.out1) : p.out1;
+                    __nv_bfloat16 *dst = static_cast<__nv_bfloat16 *>(outp) +
+                                         ((long long)b * p.T + grow_) * p.out_stride + (long long)h * D;
+                    store_row_bf16(dst, acc, p.accumulate != 0);
+                }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (*abort_flag) {
+        for (int i = 0; i < 1000; i++) __nanosleep(1000);
+    }
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem, TM_COLS);
+    }
+#undef BAR
+}
+
+constexpr int smem_bytes() {
+    return 2 * TILE_BYTES + kStages * 2 * TILE_BYTES + kStages * 2 * BT * 4 + 256 + 1024;
+}
+
+}  // namespace fab
+}  // namespace attn
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+namespace attn_host {
+
+bool ensure_smem_attr(const void *func, size_t bytes);
+int launch_bwd_rowdot(int dtype, int D, const void *o, const void *dout, const float *lse, float *ws,
+                      long long in_stride, long long out_stride, int B, int H, int T, cudaStream_t s);
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn_b() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        void *ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    }
+    return fn;
+}
+
+static bool make_map_b(CUtensorMap *m, const void *ptr, int cols, int T, int B, long long stride) {
+    struct Entry { const void *ptr; int cols, T, B; long long stride; CUtensorMap map; };
+    static thread_local Entry cache[16];
+    static thread_local int next = 0;
+    for (auto &e : cache)
+        if (e.ptr == ptr && e.cols == cols && e.T == T && e.B == B && e.stride == stride) {
+            *m = e.map;
+            return true;
+        }
+    auto fn = encode_fn_b();
+    if (!fn) return false;
+    cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)T, (cuuint64_t)B};
+    cuuint64_t strides[2] = {(cuuint64_t)stride * 2, (cuuint64_t)stride * 2 * T};
+    cuuint32_t box[3] = {64, 128, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    if (fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(ptr), dims, strides, box, estr,
+           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return false;
+    cache[next] = Entry{ptr, cols, T, B, stride, *m};
+    next = (next + 1) % 16;
+    return true;
+}
+
+bool bwd_bf16_sm100_supported(int D, long long in_stride, long long out_stride) {
+    return D == 64 && in_stride % 8 == 0 && out_stride % 8 == 0 && encode_fn_b() != nullptr;
+}
+
+int launch_bwd_bf16_sm100(int D, const void *dout, const void *q, const void *k, const void *v, const void *o,
+                          const float *lse, void *dq, void *dk, void *dv, int accumulate, void *ws,
+                          long long in_stride, long long out_stride, int B, int H, int T, int *err,
+                          cudaStream_t s) {
+    using namespace attn::fab;
+    if (D != 64) return set_error(ATTN_ERR_UNSUPPORTED, "tcgen05 backward: head_dim %d", D);
+    if (((uintptr_t)dout | (uintptr_t)q | (uintptr_t)k | (uintptr_t)v) & 15)
+        return set_error(ATTN_ERR_INVALID, "tcgen05 backward: tensors must be 16-byte aligned");
+    int st = launch_bwd_rowdot(ATTN_BF16, D, o, dout, lse, static_cast<float *>(ws), in_stride, out_stride, B, H,
+                               T, s);
+    if (st) return st;
+    CUtensorMap mq, mk, mv, mdo;
+    if (!make_map_b(&mq, q, H * D, T, B, in_stride) || !make_map_b(&mk, k, H * D, T, B, in_stride) ||
+        !make_map_b(&mv, v, H * D, T, B, in_stride) || !make_map_b(&mdo, dout, H * D, T, B, in_stride))
+        return set_error(ATTN_ERR_CUDA, "tcgen05 backward: cuTensorMapEncodeTiled failed");
+    Params p;
+    p.lse2 = static_cast<const float *>(ws);
+    p.dvec = p.lse2 + (long long)B * H * T;
+    p.out_stride = out_stride;
+    p.T = T;
+    p.H = H;
+    p.accumulate = accumulate;
+    p.scale_log2 = attn::kLog2e / sqrtf((float)D);
+    p.ds_scale = 1.0f / sqrtf((float)D);
+    p.err = err;
+    const size_t smem = smem_bytes();
+    if (!ensure_smem_attr((const void *)bwd_kernel<0>, smem) || !ensure_smem_attr((const void *)bwd_kernel<1>, smem))
+        return set_error(ATTN_ERR_CUDA, "tcgen05 backward: cannot set shared-memory size");
+    const int n_t = (T + BT - 1) / BT;
+    dim3 grid(H, B, n_t);
+    p.out1 = dk;
+    p.out2 = dv;
+    bwd_kernel<0><<<grid, kThreads, smem, s>>>(mk, mv, mq, mdo, p);     // fixed K, V; streamed Q, dO
+    if ((st = check_launch("tcgen05 backward dkdv kernel"))) return st;
+    p.out1 = dq;
+    p.out2 = nullptr;
+    bwd_kernel<1><<<grid, kThreads, smem, s>>>(mq, mdo, mk, mv, p);     // fixed Q, dO; streamed K, V
+    return check_launch("tcgen05 backward dq kernel");
+}
+
+}  // namespace attn_host

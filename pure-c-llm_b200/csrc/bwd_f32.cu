@@ -289,6 +289,29 @@ namespace attn_host {
 
 bool ensure_smem_attr(const void *func, size_t bytes);
 
+// Row statistics for any backward: lse2 = lse * log2(e) and D = dO . O per
+// (b, h, t), into the workspace (shared with the tensor-core backward).
+int launch_bwd_rowdot(int dtype, int D, const void *o, const void *dout, const float *lse, float *ws,
+                      long long in_stride, long long out_stride, int B, int H, int T, cudaStream_t s) {
+    attn::BwdParams p;
+    p.o = o; p.dout = dout; p.lse = lse;
+    p.lse2 = ws;
+    p.dvec = ws + (long long)B * H * T;
+    p.in_stride = in_stride; p.out_stride = out_stride;
+    p.B = B; p.H = H; p.T = T;
+    const long long rows = (long long)B * T * H;
+    const unsigned grid = (unsigned)((rows + 7) / 8);
+    const bool bf = dtype == ATTN_BF16;
+    switch (D) {
+        case 32: bf ? attn::bwd_rowdot_kernel<__nv_bfloat16, 32><<<grid, 256, 0, s>>>(p) : attn::bwd_rowdot_kernel<float, 32><<<grid, 256, 0, s>>>(p); break;
+        case 64: bf ? attn::bwd_rowdot_kernel<__nv_bfloat16, 64><<<grid, 256, 0, s>>>(p) : attn::bwd_rowdot_kernel<float, 64><<<grid, 256, 0, s>>>(p); break;
+        case 96: bf ? attn::bwd_rowdot_kernel<__nv_bfloat16, 96><<<grid, 256, 0, s>>>(p) : attn::bwd_rowdot_kernel<float, 96><<<grid, 256, 0, s>>>(p); break;
+        case 128: bf ? attn::bwd_rowdot_kernel<__nv_bfloat16, 128><<<grid, 256, 0, s>>>(p) : attn::bwd_rowdot_kernel<float, 128><<<grid, 256, 0, s>>>(p); break;
+        default: return set_error(ATTN_ERR_UNSUPPORTED, "bwd: head_dim %d", D);
+    }
+    return check_launch("bwd_rowdot_kernel");
+}
+
 size_t bwd_f32_workspace_bytes(int B, int H, int T) {
     return (size_t)2 * B * H * T * sizeof(float) + 256;
 }
