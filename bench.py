@@ -128,8 +128,14 @@ class Clocks:
 def cpu_reference(cfg, budget_s=12.0):
     import synth
     from oracle import oracle as O
-    cores = os.cpu_count() or 1
-    os.environ.setdefault("OMP_NUM_THREADS", str(cores))
+    cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+    # all host threads for the reference's OpenMP loops (torchrun exports
+    # OMP_NUM_THREADS=1, which would otherwise leave it single-threaded)
+    os.environ["OMP_NUM_THREADS"] = str(cores)
+    try:
+        ctypes.CDLL("libgomp.so.1").omp_set_num_threads(cores)
+    except OSError:
+        pass
     kind = cfg["kind"]
     t_end = time.time() + budget_s
     times = []
