@@ -44,7 +44,7 @@ struct DecodeLaunch {
     cudaStream_t stream;
 };
 int launch_decode(const DecodeLaunch &L);
-size_t decode_workspace_bytes(int n_seq, int heads, int head_dim, int max_len);
+size_t decode_workspace_bytes(int n_seq, int heads, int head_dim, int max_len, int kv_dtype);
 int launch_fwd_f32(int dtype, int D, const void *q, const void *k, const void *v, void *o,
                    float *lse, long long in_stride, long long out_stride, int B, int H, int T,
                    cudaStream_t s);
@@ -299,7 +299,7 @@ static int check_decode(const attn_decode_shape *s, long long *rs) {
 
 size_t attn_decode_workspace_bytes(const attn_decode_shape *s) {
     if (!s || s->n_seq < 1 || s->heads < 1 || s->max_len < 1) return 0;
-    return decode_workspace_bytes(s->n_seq, s->heads, s->head_dim, s->max_len);
+    return decode_workspace_bytes(s->n_seq, s->heads, s->head_dim, s->max_len, s->kv_dtype);
 }
 
 static int decode_common(const attn_decode_shape *s, const float *q, const void *kbase, const void *vbase,
@@ -315,7 +315,7 @@ static int decode_common(const attn_decode_shape *s, const float *q, const void 
     if (!aligned(q, 4) || !aligned(out, 4) || !aligned(lens, 4))
         return set_error(ATTN_ERR_INVALID, "decode: misaligned q/out/lens");
     cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
-    const size_t need = decode_workspace_bytes(s->n_seq, s->heads, s->head_dim, s->max_len);
+    const size_t need = decode_workspace_bytes(s->n_seq, s->heads, s->head_dim, s->max_len, s->kv_dtype);
     if (workspace) {
         if (workspace_bytes < need || !aligned(workspace, 256))
             return set_error(ATTN_ERR_WORKSPACE, "decode: workspace needs %zu bytes (256-byte aligned), got %zu",

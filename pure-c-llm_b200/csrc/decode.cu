@@ -20,7 +20,10 @@
 //   * splits of one (sequence, head) are merged by the last CTA to finish
 //     (threadfence + atomic ticket; nobody waits on anybody).  The tickets
 //     are cleared on the stream before each launch.
+#include <algorithm>
+
 #include "common.cuh"
+#include "sm100.cuh"
 
 namespace attn {
 
@@ -276,6 +279,244 @@ decode_split_kernel(const DecodeParams p)
     if (tid == 0) p.tickets[eh] = 0u;   // re-arm for the next call
 }
 
+// ---------------------------------------------------------------------------
+// INT8 cache, all heads per CTA.  One CTA covers a chunk of rows of one
+// sequence for every head, so each warp streams whole token rows (H*D bytes,
+// 16 bytes per lane per load) instead of one head's 64-byte slice per CTA;
+// DRAM then sees long contiguous reads.  Lane l holds the 16-byte pieces
+// l + 32k (k < CPL) of a row; the D/16 lanes of one head reduce its dot
+// product with shuffles.  Codes become floats exactly through a byte permute
+// into the mantissa of 2^23 and one subtraction (no conversion-pipe op).
+// ---------------------------------------------------------------------------
+// Bytes j, j+1 of w_flipped (= word ^ 0x80808080, so byte = code + 128) as a
+// packed pair of floats 2^23 + code + 128; adding -(2^23 + 128) gives the codes.
+__device__ __forceinline__ uint64_t i8_pair(uint32_t w_flipped, int j) {
+    return sm100::f2(__int_as_float(__byte_perm(w_flipped, 0x4B000000u, 0x7650u + (unsigned)j)),
+                     __int_as_float(__byte_perm(w_flipped, 0x4B000000u, 0x7650u + (unsigned)j + 1)));
+}
+
+constexpr int kRowWarps = 8;
+constexpr int kRowUnroll = 4;
+
+template <int D, int CPL>
+__global__ void __launch_bounds__(kRowWarps * 32)
+decode_rows_i8_kernel(const DecodeParams p)
+{
+    constexpr int DPL = D / 16;            // lanes (16-byte pieces) per head
+    const int H = p.H, HD = H * D;         // == 512 * CPL
+    extern __shared__ float smem[];
+    float *sc = smem;                      // [H][chunk] scores, then weights
+    float *red = sc + H * p.chunk;         // [kRowWarps][HD] partial outputs
+    float *mst = red + kRowWarps * HD;     // [H] chunk max per head
+    float *lst = mst + H;                  // [H] chunk sum per head
+    __shared__ int last_flag;
+
+    const int split = blockIdx.x, e = blockIdx.y;
+    int len = p.lens ? p.lens[e] : p.max_len;
+    if (len < 1 || len > p.max_len) {
+        if (split == 0 && threadIdx.x == 0) atomicExch(p.err, 0x100 + (len < 1 ? 1 : 2));
+        len = len < 1 ? 1 : p.max_len;
+    }
+    const int nsplit = (len + p.chunk - 1) / p.chunk;
+    if (split >= nsplit) return;
+    const int r0 = split * p.chunk;
+    const int n = min(len - r0, p.chunk);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    const char *kb, *vb;
+    const float *ksb, *vsb;
+    if (p.kptrs) {
+        kb = static_cast<const char *>(p.kptrs[e]);
+        vb = static_cast<const char *>(p.vptrs[e]);
+        ksb = p.ksptrs[e];
+        vsb = p.vsptrs[e];
+    } else {
+        const long long off = (long long)e * p.cap * p.row_stride;
+        kb = static_cast<const char *>(p.kbase) + off;
+        vb = static_cast<const char *>(p.vbase) + off;
+        ksb = p.ksbase + (long long)e * p.cap * H;
+        vsb = p.vsbase + (long long)e * p.cap * H;
+    }
+
+    // this lane's query pieces, pre-scaled into the base-2 domain, as packed
+    // fp32 pairs (the dot products run on f32x2 arithmetic: half the issue slots)
+    uint64_t qv[CPL][8];
+#pragma unroll
+    for (int k = 0; k < CPL; k++) {
+        const float *qp = p.q + (long long)e * HD + (lane + 32 * k) * 16;
+#pragma unroll
+        for (int i = 0; i < 8; i++) qv[k][i] = sm100::f2(qp[2 * i] * p.qscale, qp[2 * i + 1] * p.qscale);
+    }
+    const uint64_t bias2 = sm100::f2(-8388736.0f, -8388736.0f);
+
+    // ---- scores: sc[h][r] = kscale * (q_h . code_h) ----------------------------
+    int hk[CPL];                           // head of each of this lane's pieces
+#pragma unroll
+    for (int k = 0; k < CPL; k++) hk[k] = ((lane + 32 * k) * 16) / D;
+    for (int base = warp; base < n; base += kRowWarps * kRowUnroll) {
+        uint4 raw[kRowUnroll][CPL];
+        float ksc[kRowUnroll][CPL];        // scales load together with the rows
+#pragma unroll
+        for (int u = 0; u < kRowUnroll; u++) {
+            const int r = base + u * kRowWarps;
+            if (r < n) {
+                const uint4 *rowp = reinterpret_cast<const uint4 *>(kb + (long long)(r0 + r) * p.row_stride);
+#pragma unroll
+                for (int k = 0; k < CPL; k++) {
+                    raw[u][k] = __ldg(rowp + lane + 32 * k);
+                    ksc[u][k] = __ldg(ksb + (long long)(r0 + r) * H + hk[k]);
+                }
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < kRowUnroll; u++) {
+            const int r = base + u * kRowWarps;
+#pragma unroll
+            for (int k = 0; k < CPL; k++) {
+                float acc = 0.f;
+                if (r < n) {
+                    const uint32_t w[4] = {raw[u][k].x ^ 0x80808080u, raw[u][k].y ^ 0x80808080u,
+                                           raw[u][k].z ^ 0x80808080u, raw[u][k].w ^ 0x80808080u};
+                    uint64_t a2 = 0ull;
+#pragma unroll
+                    for (int i = 0; i < 8; i++) {
+                        const uint64_t x2 = sm100::add2(i8_pair(w[i >> 1], (i & 1) * 2), bias2);
+                        a2 = sm100::fma2(qv[k][i], x2, a2);
+                    }
+                    float al, ah;
+                    sm100::f2_split(a2, al, ah);
+                    acc = al + ah;
+                }
+#pragma unroll
+                for (int o = DPL / 2; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+                if (r < n && (lane % DPL) == 0) sc[hk[k] * p.chunk + r] = acc * ksc[u][k];
+            }
+        }
+    }
+    __syncthreads();
+
+    // ---- per-head softmax statistics of the chunk ------------------------------
+    for (int h = warp; h < H; h += kRowWarps) {
+        float *row = sc + h * p.chunk;
+        float m = -INFINITY;
+        for (int r = lane; r < n; r += 32) m = fmaxf(m, row[r]);
+        m = warp_max(m);
+        float l = 0.f;
+        for (int r = lane; r < n; r += 32) {
+            const float pr = exp2f(row[r] - m);
+            l += pr;
+            row[r] = pr;
+        }
+        l = warp_sum(l);
+        if (lane == 0) { mst[h] = m; lst[h] = l; }
+    }
+    __syncthreads();
+
+    // ---- weighted value rows ------------------------------------------------
+    uint64_t o[CPL][8];
+#pragma unroll
+    for (int k = 0; k < CPL; k++)
+#pragma unroll
+        for (int i = 0; i < 8; i++) o[k][i] = 0ull;
+    for (int base = warp; base < n; base += kRowWarps * kRowUnroll) {
+        uint4 raw[kRowUnroll][CPL];
+        float vsc[kRowUnroll][CPL];
+#pragma unroll
+        for (int u = 0; u < kRowUnroll; u++) {
+            const int r = base + u * kRowWarps;
+            if (r < n) {
+                const uint4 *rowp = reinterpret_cast<const uint4 *>(vb + (long long)(r0 + r) * p.row_stride);
+#pragma unroll
+                for (int k = 0; k < CPL; k++) {
+                    raw[u][k] = __ldg(rowp + lane + 32 * k);
+                    vsc[u][k] = __ldg(vsb + (long long)(r0 + r) * H + hk[k]);
+                }
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < kRowUnroll; u++) {
+            const int r = base + u * kRowWarps;
+            if (r < n) {
+#pragma unroll
+                for (int k = 0; k < CPL; k++) {
+                    const float wgt = sc[hk[k] * p.chunk + r] * vsc[u][k];
+                    const uint64_t w2 = sm100::f2(wgt, wgt);
+                    const uint32_t w[4] = {raw[u][k].x ^ 0x80808080u, raw[u][k].y ^ 0x80808080u,
+                                           raw[u][k].z ^ 0x80808080u, raw[u][k].w ^ 0x80808080u};
+#pragma unroll
+                    for (int i = 0; i < 8; i++)
+                        o[k][i] = sm100::fma2(w2, sm100::add2(i8_pair(w[i >> 1], (i & 1) * 2), bias2), o[k][i]);
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < CPL; k++)
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            float lo, hi;
+            sm100::f2_split(o[k][i], lo, hi);
+            red[warp * HD + (lane + 32 * k) * 16 + 2 * i] = lo;
+            red[warp * HD + (lane + 32 * k) * 16 + 2 * i + 1] = hi;
+        }
+    __syncthreads();
+
+    float *out = p.out + (long long)e * HD;
+    if (nsplit == 1) {
+        for (int x = threadIdx.x; x < HD; x += kRowWarps * 32) {
+            float s = 0.f;
+#pragma unroll
+            for (int w = 0; w < kRowWarps; w++) s += red[w * HD + x];
+            out[x] = s / lst[x / D];
+        }
+        return;
+    }
+    // ---- partial state of this split; the last split's CTA merges -----------
+    float *po = p.part_o + ((long long)e * p.max_splits + split) * HD;
+    for (int x = threadIdx.x; x < HD; x += kRowWarps * 32) {
+        float s = 0.f;
+#pragma unroll
+        for (int w = 0; w < kRowWarps; w++) s += red[w * HD + x];
+        po[x] = s;
+    }
+    for (int h = threadIdx.x; h < H; h += kRowWarps * 32) {
+        float *pm = p.part_ml + (((long long)e * p.max_splits + split) * H + h) * 2;
+        pm[0] = mst[h];
+        pm[1] = lst[h];
+    }
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) last_flag = (atomicAdd(p.tickets + e, 1u) == (unsigned)(nsplit - 1));
+    __syncthreads();
+    if (!last_flag) return;
+    __threadfence();
+    // per (split, head) rescale factors into the score area (no longer needed)
+    float *fac = sc;                       // [nsplit][H], then [H] 1/L
+    float *invl = sc + nsplit * H;
+    for (int h = threadIdx.x; h < H; h += kRowWarps * 32) {
+        float M = -INFINITY;
+        for (int s = 0; s < nsplit; s++)
+            M = fmaxf(M, __ldcg(p.part_ml + (((long long)e * p.max_splits + s) * H + h) * 2));
+        float L = 0.f;
+        for (int s = 0; s < nsplit; s++) {
+            const float *pm = p.part_ml + (((long long)e * p.max_splits + s) * H + h) * 2;
+            const float f = exp2f(__ldcg(pm) - M);
+            fac[s * H + h] = f;
+            L += __ldcg(pm + 1) * f;
+        }
+        invl[h] = 1.f / L;
+    }
+    __syncthreads();
+    for (int x = threadIdx.x; x < HD; x += kRowWarps * 32) {
+        const int h = x / D;
+        float acc = 0.f;
+        for (int s = 0; s < nsplit; s++)
+            acc += __ldcg(p.part_o + ((long long)e * p.max_splits + s) * HD + x) * fac[s * H + h];
+        out[x] = acc * invl[h];
+    }
+    if (threadIdx.x == 0) p.tickets[e] = 0u;
+}
+
 }  // namespace attn
 
 // ---------------------------------------------------------------------------
@@ -293,7 +534,30 @@ int decode_chunk(int max_len, long long units) {
     return (int)c;
 }
 
-size_t decode_workspace_bytes(int n_seq, int heads, int head_dim, int max_len) {
+// INT8 caches whose rows are 512, 1024 or 2048 bytes take the all-heads rows
+// kernel; its rows per split target ~3 CTAs per SM.
+static bool rows_i8_ok(int heads, int head_dim, int kv_dtype) {
+    const int hd = heads * head_dim;
+    return kv_dtype == ATTN_I8 && (head_dim == 32 || head_dim == 64 || head_dim == 128) &&
+           (hd == 512 || hd == 1024 || hd == 2048);
+}
+int rows_chunk(int max_len, int n_seq) {
+    long long c = ((long long)max_len * n_seq + 443) / 444;
+    c = (c + 63) / 64 * 64;
+    return (int)std::max(128LL, std::min(512LL, c));
+}
+
+size_t decode_workspace_bytes(int n_seq, int heads, int head_dim, int max_len, int kv_dtype) {
+    if (rows_i8_ok(heads, head_dim, kv_dtype)) {
+        const int rc = rows_chunk(max_len, n_seq);
+        const long long rsplits = (max_len + rc - 1) / rc;
+        size_t r = (size_t)n_seq * sizeof(unsigned);
+        r = (r + 255) / 256 * 256;
+        r += (size_t)n_seq * rsplits * heads * 2 * sizeof(float);
+        r = (r + 255) / 256 * 256;
+        r += (size_t)n_seq * rsplits * heads * head_dim * sizeof(float);
+        return (r + 255) / 256 * 256;
+    }
     const int chunk = decode_chunk(max_len, (long long)n_seq * heads);
     const long long splits = (max_len + chunk - 1) / chunk;
     const long long eh = (long long)n_seq * heads;
@@ -351,8 +615,59 @@ static int launch_decode_t(const DecodeLaunch &L) {
     return check_launch("decode_split_kernel");
 }
 
+bool ensure_smem_attr(const void *func, size_t bytes);
+
+template <int D, int CPL>
+static int launch_rows_i8_t(const DecodeLaunch &L) {
+    using namespace attn;
+    DecodeParams p;
+    p.chunk = rows_chunk(L.max_len, L.n_seq);
+    p.max_splits = (L.max_len + p.chunk - 1) / p.chunk;
+    const int H = L.heads, HD = H * D;
+    // workspace: [tickets (n_seq) | part_ml | part_o], 256-byte aligned regions
+    char *ws = static_cast<char *>(L.ws);
+    const size_t t_bytes = ((size_t)L.n_seq * sizeof(unsigned) + 255) / 256 * 256;
+    const size_t ml_bytes = ((size_t)L.n_seq * p.max_splits * H * 2 * sizeof(float) + 255) / 256 * 256;
+    p.tickets = reinterpret_cast<unsigned *>(ws);
+    p.part_ml = reinterpret_cast<float *>(ws + t_bytes);
+    p.part_o = reinterpret_cast<float *>(ws + t_bytes + ml_bytes);
+    if (p.max_splits > 1) {
+        cudaError_t e = cudaMemsetAsync(p.tickets, 0, (size_t)L.n_seq * sizeof(unsigned), L.stream);
+        if (e != cudaSuccess) return set_error(ATTN_ERR_CUDA, "decode: ticket clear: %s", cudaGetErrorString(e));
+    }
+    p.q = L.q; p.kbase = L.kbase; p.vbase = L.vbase; p.kptrs = L.kptrs; p.vptrs = L.vptrs;
+    p.ksbase = L.ksbase; p.vsbase = L.vsbase; p.ksptrs = L.ksptrs; p.vsptrs = L.vsptrs;
+    p.lens = L.lens; p.out = L.out; p.err = L.err;
+    p.row_stride = L.row_stride; p.cap = L.cap; p.H = H; p.max_len = L.max_len;
+    p.qscale = kLog2e / sqrtf((float)D);
+    const size_t smem = (size_t)(H * p.chunk + kRowWarps * HD + 2 * H) * sizeof(float);
+    if (!ensure_smem_attr((const void *)decode_rows_i8_kernel<D, CPL>, smem))
+        return set_error(ATTN_ERR_CUDA, "decode: cannot set shared-memory size");
+    cudaFuncSetAttribute(decode_rows_i8_kernel<D, CPL>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    dim3 grid(p.max_splits, L.n_seq);
+    decode_rows_i8_kernel<D, CPL><<<grid, kRowWarps * 32, smem, L.stream>>>(p);
+    return check_launch("decode_rows_i8_kernel");
+}
+
+static int launch_rows_i8(const DecodeLaunch &L) {
+    const int cpl = L.heads * L.head_dim / 512;
+    switch (L.head_dim * 10 + cpl) {
+        case 321: return launch_rows_i8_t<32, 1>(L);
+        case 322: return launch_rows_i8_t<32, 2>(L);
+        case 324: return launch_rows_i8_t<32, 4>(L);
+        case 641: return launch_rows_i8_t<64, 1>(L);
+        case 642: return launch_rows_i8_t<64, 2>(L);
+        case 644: return launch_rows_i8_t<64, 4>(L);
+        case 1281: return launch_rows_i8_t<128, 1>(L);
+        case 1282: return launch_rows_i8_t<128, 2>(L);
+        case 1284: return launch_rows_i8_t<128, 4>(L);
+        default: return set_error(ATTN_ERR_UNSUPPORTED, "decode: no rows kernel for H*d=%d", L.heads * L.head_dim);
+    }
+}
+
 int launch_decode(const DecodeLaunch &L) {
     const bool i8 = L.kv_dtype == ATTN_I8;
+    if (rows_i8_ok(L.heads, L.head_dim, L.kv_dtype)) return launch_rows_i8(L);
     switch (L.head_dim) {
         case 32: return i8 ? launch_decode_t<32, true>(L) : launch_decode_t<32, false>(L);
         case 64: return i8 ? launch_decode_t<64, true>(L) : launch_decode_t<64, false>(L);
