@@ -60,7 +60,8 @@ struct Cfg {
     static constexpr int OFF_KV = 4 * Q_BYTES;
     static constexpr int STAGE_BYTES = 2 * KV_BYTES;
     static constexpr int OFF_BAR = OFF_KV + kStages * STAGE_BYTES;
-    static constexpr int SMEM = OFF_BAR + 256 + 1024;
+    static constexpr int OFF_ITEMS = OFF_BAR + 256;     // kLocalItems packed items
+    static constexpr int SMEM = OFF_ITEMS + 4 * 256 + 1024;
     static constexpr int TM_S0 = 0, TM_S1 = 128, TM_O0 = 256, TM_O1 = 256 + D;
     static constexpr int TM_P0 = 256 + 2 * D, TM_P1 = 256 + 2 * D + BN / 2;
     static constexpr int TM_COLS = 512;
@@ -89,6 +90,7 @@ struct Params {
     float scale_log2;            // log2(e) / sqrt(d)
     int *err;
     int use_list;                // 1: per-CTA lists in `sched`; 0: round-robin over items
+    int packable;                // B < 4096, H < 1024, n_pairs < 1024: items fit pack_item
     const unsigned short *sched; // [kMaxCtas + 1] list offsets, then the item lists
 };
 
@@ -123,6 +125,42 @@ __device__ __forceinline__ int item_of(const Params &p, int k) {
     return i < p.n_items ? i : -1;
 }
 
+// Item fields packed into 32 bits (batch 12 bits, head 10, query pair 10).
+// The CTA decodes its whole list into shared memory once, at kernel start:
+// every role walks the same list, and at each item boundary a dependent
+// chain of global loads and integer divisions would stall all of them.
+constexpr int kLocalItems = 256;
+__device__ __forceinline__ uint32_t pack_item(const Params &p, int id) {
+    const int hb = p.H * p.B;
+    const int pair = p.n_pairs - 1 - id / hb;
+    const int r = id % hb;
+    return (uint32_t)(r / p.H) | (uint32_t)(r % p.H) << 12 | (uint32_t)pair << 22;
+}
+__device__ __forceinline__ Item unpack_item(const Params &p, uint32_t v) {
+    Item it;
+    it.b = (int)(v & 0xfffu);
+    it.h = (int)((v >> 12) & 0x3ffu);
+    it.q0 = (int)(v >> 22) * 2 * BM;
+    it.has_q1 = (it.q0 + BM) < p.T;
+    it.n0 = it.q0 / BN + 1;
+    it.n1 = it.has_q1 ? it.n0 + 1 : 0;
+    it.n_kv = it.has_q1 ? it.n1 : it.n0;
+    return it;
+}
+// Items of this CTA: from the shared-memory copy when it holds them all
+// (n_local >= 0), otherwise decoded from global memory per item.
+__device__ __forceinline__ bool next_item(const Params &p, const uint32_t *items_s, int n_local, int k, Item &it) {
+    if (n_local >= 0) {
+        if (k >= n_local) return false;
+        it = unpack_item(p, items_s[k]);
+        return true;
+    }
+    const int id = item_of(p, k);
+    if (id < 0) return false;
+    it = decode_item(p, id);
+    return true;
+}
+
 template <int D>
 __global__ void __launch_bounds__(kThreads, 1)
 fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
@@ -141,6 +179,23 @@ fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
     volatile int *abort_flag = reinterpret_cast<volatile int *>(sb + C::OFF_BAR + 196);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    uint32_t *items_s = reinterpret_cast<uint32_t *>(sb + C::OFF_ITEMS);
+    int n_local = -1;                             // -1: items decoded from global memory
+    {
+        int beg = 0, n_mine;
+        if (p.use_list) {
+            beg = (int)__ldg(p.sched + blockIdx.x);
+            n_mine = (int)__ldg(p.sched + blockIdx.x + 1) - beg;
+        } else {
+            n_mine = (p.n_items - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
+        }
+        if (p.packable && n_mine <= kLocalItems) {
+            n_local = n_mine;
+            for (int i = threadIdx.x; i < n_mine; i += blockDim.x)
+                items_s[i] = pack_item(p, p.use_list ? (int)__ldg(p.sched + kMaxCtas + 1 + beg + i)
+                                                     : (int)blockIdx.x + i * (int)gridDim.x);
+        }
+    }
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < 2; i++) {
@@ -172,117 +227,131 @@ fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
     if (warp < 4) regs_dec<72>();
     if (warp == 0) {
         // ------------------------------------------------------------ producer
-        if (lane == 0) {
+        // warp-wide loop like the MMA issuer; the elected lane issues the copies
+        const bool leader = elect_one();
+        if (leader) {
             prefetch_tmap(&tq);
             prefetch_tmap(&tk);
             prefetch_tmap(&tv);
-            int g = 0;                                  // key/value tiles issued so far
-            bool ok = true;
-            for (int k = 0; ok; k++) {
-                const int id = item_of(p, k);
-                if (id < 0) break;
-                const Item it = decode_item(p, id);
-                const int qb = k & 1;
-                if (k >= 2 && !(ok = mbar_wait(BAR(B_QE + qb), ((k >> 1) + 1) & 1, abort_flag, p.err, 0x201)))
-                    break;
-                const uint32_t qdst = sQ + qb * 2 * C::Q_BYTES;
+        }
+        int g = 0;                                  // key/value tiles issued so far
+        bool ok = true;
+        for (int k = 0; ok; k++) {
+            Item it;
+            if (!next_item(p, items_s, n_local, k, it)) break;
+            const int qb = k & 1;
+            if (k >= 2 &&
+                !(ok = __all_sync(0xffffffffu, mbar_wait(BAR(B_QE + qb), ((k >> 1) + 1) & 1, abort_flag, p.err, 0x201))))
+                break;
+            const uint32_t qdst = sQ + qb * 2 * C::Q_BYTES;
+            if (leader) {
                 mbar_arrive_expect_tx(BAR(B_QF + qb), (it.has_q1 ? 2 : 1) * C::Q_BYTES);
                 tma_load_3d(qdst, &tq, BAR(B_QF + qb), it.h * D, it.q0, it.b);
                 if (it.has_q1) tma_load_3d(qdst + C::Q_BYTES, &tq, BAR(B_QF + qb), it.h * D, it.q0 + BM, it.b);
-                for (int j = 0; j < it.n_kv; j++, g++) {
-                    const int st = g % kStages;
-                    if (g >= kStages &&
-                        !(ok = mbar_wait(BAR(B_KVE + st), ((g / kStages) + 1) & 1, abort_flag, p.err, 0x202)))
-                        break;
+            }
+            __syncwarp();
+            for (int j = 0; j < it.n_kv; j++, g++) {
+                const int st = g % kStages;
+                if (g >= kStages &&
+                    !(ok = __all_sync(0xffffffffu, mbar_wait(BAR(B_KVE + st), ((g / kStages) + 1) & 1, abort_flag,
+                                                             p.err, 0x202))))
+                    break;
+                if (leader) {
                     mbar_arrive_expect_tx(BAR(B_KVF + st), 2 * C::KV_BYTES);
                     const uint32_t dst = sKV + st * C::STAGE_BYTES;
                     tma_load_3d(dst, &tk, BAR(B_KVF + st), it.h * D, j * BN, it.b);
                     tma_load_3d(dst + C::KV_BYTES, &tv, BAR(B_KVF + st), it.h * D, j * BN, it.b);
                 }
+                __syncwarp();
             }
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
-        if (lane == 0) {
-            constexpr uint32_t idS = idesc_bf16(BM, BN, 0, 0);   // Q, K both K-major
-            constexpr uint32_t idO = idesc_bf16(BM, D, 0, 1);    // P K-major (TMEM), V MN-major
-            int g = 0;                 // key/value tiles consumed
-            int t[2] = {0, 0};         // tiles processed per warpgroup (S/P/O barrier phases)
-            int kw[2] = {0, 0};        // items processed per warpgroup (O-free phases)
-            bool ok = true;
-            // Descriptors of consecutive K-steps differ only in the start-address
-            // field (bits 0-13, 16-byte units), so each step adds a constant to a
-            // base descriptor: the issuing thread shares its SMSP with two busy
-            // softmax warps, and rebuilding descriptors per MMA starved it.
-            auto issue_S = [&](int i, int qb, int stage) {
-                const uint64_t kd = sw128_desc(sKV + stage * C::STAGE_BYTES, 16, 1024);
-                const uint64_t qd = sw128_desc(sQ + (qb * 2 + i) * C::Q_BYTES, 16, 1024);
-                const uint32_t d_t = tmem + (i ? C::TM_S1 : C::TM_S0);
+        // The whole warp runs the loop (its state stays warp-uniform, so the
+        // descriptors live in uniform registers); one elected lane issues the
+        // MMAs and their commits.  Waits are taken by every lane.
+        const bool leader = elect_one();
+        constexpr uint32_t idS = idesc_bf16(BM, BN, 0, 0);   // Q, K both K-major
+        constexpr uint32_t idO = idesc_bf16(BM, D, 0, 1);    // P K-major (TMEM), V MN-major
+        int g = 0;                 // key/value tiles consumed
+        int t[2] = {0, 0};         // tiles processed per warpgroup (S/P/O barrier phases)
+        int kw[2] = {0, 0};        // items processed per warpgroup (O-free phases)
+        bool ok = true;
+        auto wait = [&](int b, int parity, int code) -> bool {
+            return __all_sync(0xffffffffu, mbar_wait(BAR(b), parity & 1, abort_flag, p.err, code));
+        };
+        // Descriptors of consecutive K-steps differ only in the start-address
+        // field (bits 0-13, 16-byte units), so each step adds a constant.
+        auto issue_S = [&](int i, int qb, int stage) {
+            const uint64_t kd = sw128_desc(sKV + stage * C::STAGE_BYTES, 16, 1024);
+            const uint64_t qd = sw128_desc(sQ + (qb * 2 + i) * C::Q_BYTES, 16, 1024);
+            const uint32_t d_t = tmem + (i ? C::TM_S1 : C::TM_S0);
+            if (leader) {
 #pragma unroll
                 for (int kk = 0; kk < D / 16; kk++)          // +32 bytes along K per step
                     mma_bf16_ss(d_t, qd + 2 * kk, kd + 2 * kk, idS, kk > 0);
                 mma_commit(BAR(B_SF + i));
-            };
-            auto issue_PV = [&](int i, int stage, bool first) {
-                const uint64_t vd = sw128_desc(sKV + stage * C::STAGE_BYTES + C::KV_BYTES, 16384, 1024);
-                const uint32_t pt = tmem + (i ? C::TM_P1 : C::TM_P0);
-                const uint32_t d_t = tmem + (i ? C::TM_O1 : C::TM_O0);
+            }
+            __syncwarp();
+        };
+        auto issue_PV = [&](int i, int stage, bool first) {
+            const uint64_t vd = sw128_desc(sKV + stage * C::STAGE_BYTES + C::KV_BYTES, 16384, 1024);
+            const uint32_t pt = tmem + (i ? C::TM_P1 : C::TM_P0);
+            const uint32_t d_t = tmem + (i ? C::TM_O1 : C::TM_O0);
+            if (leader) {
 #pragma unroll
                 for (int kk = 0; kk < BN / 16; kk++)      // 16 keys per step: 8 packed TMEM columns of P,
                     mma_bf16_ts(d_t, pt + kk * 8, vd + 128 * kk, idO, (!first || kk > 0));   // 2 KB of V
                 mma_commit(BAR(B_OD + i));
-            };
-            // S of warpgroup i for its global tile index ti, key stage of tile g+j
-            auto s_step = [&](int i, int qb, int ti, int gj) -> bool {
-                if (ti > 0 && !mbar_wait(BAR(B_SE + i), (ti - 1) & 1, abort_flag, p.err, 0x211 + i)) return false;
-                tc_fence_after();
-                issue_S(i, qb, gj % kStages);
-                return true;
-            };
-            for (int k = 0; ok; k++) {
-                const int id = item_of(p, k);
-                if (id < 0) break;
-                const Item it = decode_item(p, id);
-                const int qb = k & 1;
-                if (!(ok = mbar_wait(BAR(B_QF + qb), (k >> 1) & 1, abort_flag, p.err, 0x213))) break;
-                if (!(ok = mbar_wait(BAR(B_KVF + g % kStages), (g / kStages) & 1, abort_flag, p.err, 0x214))) break;
-                const int b0 = t[0], b1 = t[1];
-                if (!(ok = s_step(0, qb, b0, g))) break;
-                if (it.has_q1 && !(ok = s_step(1, qb, b1, g))) break;
-                for (int j = 0; ok && j < it.n_kv; j++) {
-                    const int nx = j + 1;
-                    const bool s0_next = nx < it.n0, s1_next = it.has_q1 && nx < it.n1;
-                    if (s0_next || s1_next) {
-                        if (!(ok = mbar_wait(BAR(B_KVF + (g + nx) % kStages), ((g + nx) / kStages) & 1, abort_flag,
-                                             p.err, 0x215)))
-                            break;
-                    }
-                    if (s0_next && !(ok = s_step(0, qb, b0 + nx, g + nx))) break;
-                    if (s1_next && !(ok = s_step(1, qb, b1 + nx, g + nx))) break;
-                    if (nx == it.n_kv) mma_commit(BAR(B_QE + qb));   // this item's last S issued
-                    if (j < it.n0) {
-                        if (j == 0 && kw[0] > 0 &&
-                            !(ok = mbar_wait(BAR(B_OF + 0), (kw[0] - 1) & 1, abort_flag, p.err, 0x216)))
-                            break;
-                        if (!(ok = mbar_wait(BAR(B_PF + 0), (b0 + j) & 1, abort_flag, p.err, 0x217))) break;
-                        tc_fence_after();
-                        issue_PV(0, (g + j) % kStages, j == 0);
-                    }
-                    if (it.has_q1) {
-                        if (j == 0 && kw[1] > 0 &&
-                            !(ok = mbar_wait(BAR(B_OF + 1), (kw[1] - 1) & 1, abort_flag, p.err, 0x218)))
-                            break;
-                        if (!(ok = mbar_wait(BAR(B_PF + 1), (b1 + j) & 1, abort_flag, p.err, 0x219))) break;
-                        tc_fence_after();
-                        issue_PV(1, (g + j) % kStages, j == 0);
-                    }
-                    mma_commit(BAR(B_KVE + (g + j) % kStages));   // stage free once these MMAs finish
-                }
-                g += it.n_kv;
-                t[0] += it.n0;
-                kw[0] += 1;
-                if (it.has_q1) { t[1] += it.n1; kw[1] += 1; }
             }
+            __syncwarp();
+        };
+        auto commit = [&](int b) {
+            if (leader) mma_commit(BAR(b));
+            __syncwarp();
+        };
+        // S of warpgroup i for its global tile index ti, key stage of tile g+j
+        auto s_step = [&](int i, int qb, int ti, int gj) -> bool {
+            if (ti > 0 && !wait(B_SE + i, ti - 1, 0x211 + i)) return false;
+            tc_fence_after();
+            issue_S(i, qb, gj % kStages);
+            return true;
+        };
+        for (int k = 0; ok; k++) {
+            Item it;
+            if (!next_item(p, items_s, n_local, k, it)) break;
+            const int qb = k & 1;
+            if (!(ok = wait(B_QF + qb, k >> 1, 0x213))) break;
+            if (!(ok = wait(B_KVF + g % kStages, g / kStages, 0x214))) break;
+            const int b0 = t[0], b1 = t[1];
+            if (!(ok = s_step(0, qb, b0, g))) break;
+            if (it.has_q1 && !(ok = s_step(1, qb, b1, g))) break;
+            for (int j = 0; ok && j < it.n_kv; j++) {
+                const int nx = j + 1;
+                const bool s0_next = nx < it.n0, s1_next = it.has_q1 && nx < it.n1;
+                if ((s0_next || s1_next) && !(ok = wait(B_KVF + (g + nx) % kStages, (g + nx) / kStages, 0x215)))
+                    break;
+                if (s0_next && !(ok = s_step(0, qb, b0 + nx, g + nx))) break;
+                if (s1_next && !(ok = s_step(1, qb, b1 + nx, g + nx))) break;
+                if (nx == it.n_kv) commit(B_QE + qb);        // this item's last S issued
+                if (j < it.n0) {
+                    if (j == 0 && kw[0] > 0 && !(ok = wait(B_OF + 0, kw[0] - 1, 0x216))) break;
+                    if (!(ok = wait(B_PF + 0, b0 + j, 0x217))) break;
+                    tc_fence_after();
+                    issue_PV(0, (g + j) % kStages, j == 0);
+                }
+                if (it.has_q1) {
+                    if (j == 0 && kw[1] > 0 && !(ok = wait(B_OF + 1, kw[1] - 1, 0x218))) break;
+                    if (!(ok = wait(B_PF + 1, b1 + j, 0x219))) break;
+                    tc_fence_after();
+                    issue_PV(1, (g + j) % kStages, j == 0);
+                }
+                commit(B_KVE + (g + j) % kStages);           // stage free once these MMAs finish
+            }
+            g += it.n_kv;
+            t[0] += it.n0;
+            kw[0] += 1;
+            if (it.has_q1) { t[1] += it.n1; kw[1] += 1; }
         }
     } else if (warp >= 4) {
         // ------------------------------------------------------------ softmax
@@ -297,9 +366,8 @@ fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
         int t = 0;                                   // global tile index of this warpgroup
         bool ok = true;
         for (int k = 0; ok; k++) {
-            const int id = item_of(p, k);
-            if (id < 0) break;
-            const Item it = decode_item(p, id);
+            Item it;
+            if (!next_item(p, items_s, n_local, k, it)) break;
             const int n = wg ? it.n1 : it.n0;
             if (n == 0) continue;                    // no second query tile in this item
             const int qs = it.q0 + wg * BM;
@@ -567,6 +635,7 @@ int launch_fwd_bf16_sm100(int D, const void *q, const void *k, const void *v, vo
     p.err = err;
     const int ctas = std::max(1, std::min(std::min(sm_count[dev], kMaxCtas), p.n_items));
     p.use_list = p.n_items <= kMaxItems;
+    p.packable = B < 4096 && H < 1024 && p.n_pairs < 1024;
     p.sched = nullptr;
     if (p.use_list) {
         static unsigned short *sched_buf[128] = {nullptr};

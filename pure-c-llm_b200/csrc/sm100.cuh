@@ -122,6 +122,18 @@ __device__ __forceinline__ void mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, ui
                  "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
                  ::"r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate) : "memory");
 }
+// One lane of a converged warp (elect.sync over the full mask).  A role that
+// issues single-thread instructions (TMA, tcgen05.mma) runs its loop on the
+// whole warp, so loop state stays warp-uniform, and only the elected lane
+// issues.
+__device__ __forceinline__ bool elect_one() {
+    uint32_t pred;
+    asm volatile("{\n\t.reg .pred P;\n\t.reg .b32 l;\n\t"
+                 "elect.sync l|P, 0xffffffff;\n\t"
+                 "selp.u32 %0, 1, 0, P;\n\t}"
+                 : "=r"(pred));
+    return pred != 0;
+}
 // Arrives on `bar` once all previously issued tcgen05 ops of this thread finish.
 __device__ __forceinline__ void mma_commit(uint32_t bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
