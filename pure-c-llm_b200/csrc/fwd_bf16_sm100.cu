@@ -11,10 +11,10 @@
 //   warp 0      TMA producer: Q tiles into a double buffer (the next item's Q
 //               loads while the current item runs), K_j/V_j into a 4-stage
 //               ring that runs across item boundaries
-//   warp 1      MMA issuer (one thread): S_i = Q_i K_j^T (both operands in
-//               shared memory) and O_i += P_i V_j (P from TMEM, V from shared
-//               memory), tcgen05.mma kind::f16, fp32 accumulators in TMEM
-//   warps 2-3   spare (they only give their registers to the softmax warps)
+//   warps 1-3   MMA issuers, tcgen05.mma kind::f16 with fp32 accumulators in
+//               TMEM: warp 1 issues S_i = Q_i K_j^T for both query tiles (both
+//               operands in shared memory), warp 2 O_0 += P_0 V_j and warp 3
+//               O_1 += P_1 V_j (P from TMEM, V from shared memory)
 //   warps 4-7   softmax for query tile 0 of each item; warps 8-11 for tile 1.
 //               A thread owns one query row (= one TMEM lane): it reads its S
 //               row with tcgen05.ld, keeps the running max/sum, writes its row
@@ -22,11 +22,11 @@
 //               its O row in TMEM when the max grew by more than 2^8
 //               (otherwise the stale max is kept; the final normalisation uses
 //               the same max for O and the sum).
-// The two query tiles ping-pong on the tensor core, and the MMA warp issues
-// S_{j+1} as soon as a warpgroup has drained S_j, so a warpgroup never waits
-// for its own products between tiles.  The first S of the next item is issued
-// while the warpgroups still finish the current one; its first PV waits until
-// the warpgroup has read out the previous O.
+// The S issuer runs one key tile ahead: it issues S_{j+1} as soon as a
+// warpgroup has drained S_j, so a warpgroup never waits for its next scores,
+// and the first S of the next item while the warpgroups still finish the
+// current one; that item's first PV waits until the warpgroup has read out
+// the previous O.
 //
 // TMEM: S0 cols [0,128), S1 [128,256), O0 [256,256+D), O1 [256+D, 256+2D),
 // P0 and P1 64 columns each after the O tiles.
@@ -48,6 +48,10 @@ using namespace sm100;
 constexpr int BM = 128;           // query rows per tile (TMEM lanes)
 constexpr int BN = 128;           // keys per tile
 constexpr int kStages = 4;
+#ifndef ATTN_FWD_POLY_PAIRS
+#define ATTN_FWD_POLY_PAIRS 3
+#endif
+constexpr int kPolyPairs = ATTN_FWD_POLY_PAIRS;   // exponential pairs (of 8) computed by exp2_poly2
 constexpr int kThreads = 384;
 constexpr int kMaxCtas = 160;     // >= SM count of a B200 (148)
 constexpr int kMaxItems = 6144;   // schedule carried in the kernel parameters
@@ -207,7 +211,7 @@ fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
             mbar_init(BAR(B_OD + i), 1);
             mbar_init(BAR(B_OF + i), 128);
         }
-        for (int s = 0; s < kStages; s++) { mbar_init(BAR(B_KVF + s), 1); mbar_init(BAR(B_KVE + s), 1); }
+        for (int s = 0; s < kStages; s++) { mbar_init(BAR(B_KVF + s), 1); mbar_init(BAR(B_KVE + s), 3); }
         *abort_flag = 0;
         fence_mbar_init();
     }
@@ -265,93 +269,99 @@ fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
                 __syncwarp();
             }
         }
-    } else if (warp == 1) {
-        // ------------------------------------------------------------ MMA issuer
-        // The whole warp runs the loop (its state stays warp-uniform, so the
-        // descriptors live in uniform registers); one elected lane issues the
-        // MMAs and their commits.  Waits are taken by every lane.
+    } else if (warp <= 3) {
+        // ------------------------------------------------------------ MMA issuers
+        // Three issuing warps, so that no single thread's instruction stream
+        // paces the tensor core: warp 1 issues S_i = Q_i K_j^T for both query
+        // tiles, warp 2 issues O_0 += P_0 V_j, warp 3 issues O_1 += P_1 V_j.
+        // Each runs its loop on the whole warp (warp-uniform state, descriptors
+        // in uniform registers); the elected lane issues the MMAs and their
+        // commits, which track that lane's own MMAs.  A key/value stage is
+        // free once all three have released it (KVE counts three arrivals).
         const bool leader = elect_one();
-        constexpr uint32_t idS = idesc_bf16(BM, BN, 0, 0);   // Q, K both K-major
-        constexpr uint32_t idO = idesc_bf16(BM, D, 0, 1);    // P K-major (TMEM), V MN-major
-        int g = 0;                 // key/value tiles consumed
-        int t[2] = {0, 0};         // tiles processed per warpgroup (S/P/O barrier phases)
-        int kw[2] = {0, 0};        // items processed per warpgroup (O-free phases)
-        bool ok = true;
         auto wait = [&](int b, int parity, int code) -> bool {
             return __all_sync(0xffffffffu, mbar_wait(BAR(b), parity & 1, abort_flag, p.err, code));
         };
-        // Descriptors of consecutive K-steps differ only in the start-address
-        // field (bits 0-13, 16-byte units), so each step adds a constant.
-        auto issue_S = [&](int i, int qb, int stage) {
-            const uint64_t kd = sw128_desc(sKV + stage * C::STAGE_BYTES, 16, 1024);
-            const uint64_t qd = sw128_desc(sQ + (qb * 2 + i) * C::Q_BYTES, 16, 1024);
-            const uint32_t d_t = tmem + (i ? C::TM_S1 : C::TM_S0);
+        auto release = [&](int b, bool after_mma) {   // commit (after this lane's MMAs) or plain arrive
             if (leader) {
-#pragma unroll
-                for (int kk = 0; kk < D / 16; kk++)          // +32 bytes along K per step
-                    mma_bf16_ss(d_t, qd + 2 * kk, kd + 2 * kk, idS, kk > 0);
-                mma_commit(BAR(B_SF + i));
+                if (after_mma) mma_commit(BAR(b));
+                else mbar_arrive(BAR(b));
             }
             __syncwarp();
         };
-        auto issue_PV = [&](int i, int stage, bool first) {
-            const uint64_t vd = sw128_desc(sKV + stage * C::STAGE_BYTES + C::KV_BYTES, 16384, 1024);
+        int g = 0;                 // key/value tiles consumed
+        bool ok = true;
+        if (warp == 1) {
+            constexpr uint32_t idS = idesc_bf16(BM, BN, 0, 0);   // Q, K both K-major
+            int t[2] = {0, 0};     // S tiles issued per query tile (S-empty phases)
+            for (int k = 0; ok; k++) {
+                Item it;
+                if (!next_item(p, items_s, n_local, k, it)) break;
+                const int qb = k & 1;
+                if (!(ok = wait(B_QF + qb, k >> 1, 0x213))) break;
+                for (int j = 0; ok && j < it.n_kv; j++) {
+                    const int st = (g + j) % kStages;
+                    if (!(ok = wait(B_KVF + st, (g + j) / kStages, 0x214))) break;
+                    // Descriptors of consecutive K-steps differ only in the
+                    // start-address field, so each step adds a constant.
+                    const uint64_t kd = sw128_desc(sKV + st * C::STAGE_BYTES, 16, 1024);
+                    for (int i = 0; i < 2; i++) {
+                        if (j >= (i ? it.n1 : it.n0)) continue;
+                        if (t[i] > 0 && !(ok = wait(B_SE + i, t[i] - 1, 0x211 + i))) break;
+                        tc_fence_after();
+                        const uint64_t qd = sw128_desc(sQ + (qb * 2 + i) * C::Q_BYTES, 16, 1024);
+                        const uint32_t d_t = tmem + (i ? C::TM_S1 : C::TM_S0);
+                        if (leader) {
+#pragma unroll
+                            for (int kk = 0; kk < D / 16; kk++)   // +32 bytes along K per step
+                                mma_bf16_ss(d_t, qd + 2 * kk, kd + 2 * kk, idS, kk > 0);
+                            mma_commit(BAR(B_SF + i));
+                        }
+                        __syncwarp();
+                        t[i]++;
+                    }
+                    if (!ok) break;
+                    release(B_KVE + st, true);
+                    if (j == it.n_kv - 1) release(B_QE + qb, true);   // this item's last S issued
+                }
+                g += it.n_kv;
+            }
+        } else {
+            const int i = warp - 2;                               // query tile of this issuer
+            constexpr uint32_t idO = idesc_bf16(BM, D, 0, 1);    // P K-major (TMEM), V MN-major
             const uint32_t pt = tmem + (i ? C::TM_P1 : C::TM_P0);
             const uint32_t d_t = tmem + (i ? C::TM_O1 : C::TM_O0);
-            if (leader) {
+            int t = 0, kw = 0;     // PV tiles issued, items finished (P-full / O-free phases)
+            for (int k = 0; ok; k++) {
+                Item it;
+                if (!next_item(p, items_s, n_local, k, it)) break;
+                const int n = i ? it.n1 : it.n0;
+                for (int j = 0; ok && j < it.n_kv; j++) {
+                    const int st = (g + j) % kStages;
+                    // the stage's load completing orders this release after the
+                    // stage's previous use was released by all three issuers
+                    if (!(ok = wait(B_KVF + st, (g + j) / kStages, 0x215))) break;
+                    if (j >= n) {                                 // stage not used by this query tile
+                        release(B_KVE + st, false);
+                        continue;
+                    }
+                    if (j == 0 && kw > 0 && !(ok = wait(B_OF + i, kw - 1, 0x216 + i))) break;
+                    if (!(ok = wait(B_PF + i, t, 0x218 + i))) break;
+                    tc_fence_after();
+                    const uint64_t vd = sw128_desc(sKV + st * C::STAGE_BYTES + C::KV_BYTES, 16384, 1024);
+                    if (leader) {
 #pragma unroll
-                for (int kk = 0; kk < BN / 16; kk++)      // 16 keys per step: 8 packed TMEM columns of P,
-                    mma_bf16_ts(d_t, pt + kk * 8, vd + 128 * kk, idO, (!first || kk > 0));   // 2 KB of V
-                mma_commit(BAR(B_OD + i));
-            }
-            __syncwarp();
-        };
-        auto commit = [&](int b) {
-            if (leader) mma_commit(BAR(b));
-            __syncwarp();
-        };
-        // S of warpgroup i for its global tile index ti, key stage of tile g+j
-        auto s_step = [&](int i, int qb, int ti, int gj) -> bool {
-            if (ti > 0 && !wait(B_SE + i, ti - 1, 0x211 + i)) return false;
-            tc_fence_after();
-            issue_S(i, qb, gj % kStages);
-            return true;
-        };
-        for (int k = 0; ok; k++) {
-            Item it;
-            if (!next_item(p, items_s, n_local, k, it)) break;
-            const int qb = k & 1;
-            if (!(ok = wait(B_QF + qb, k >> 1, 0x213))) break;
-            if (!(ok = wait(B_KVF + g % kStages, g / kStages, 0x214))) break;
-            const int b0 = t[0], b1 = t[1];
-            if (!(ok = s_step(0, qb, b0, g))) break;
-            if (it.has_q1 && !(ok = s_step(1, qb, b1, g))) break;
-            for (int j = 0; ok && j < it.n_kv; j++) {
-                const int nx = j + 1;
-                const bool s0_next = nx < it.n0, s1_next = it.has_q1 && nx < it.n1;
-                if ((s0_next || s1_next) && !(ok = wait(B_KVF + (g + nx) % kStages, (g + nx) / kStages, 0x215)))
-                    break;
-                if (s0_next && !(ok = s_step(0, qb, b0 + nx, g + nx))) break;
-                if (s1_next && !(ok = s_step(1, qb, b1 + nx, g + nx))) break;
-                if (nx == it.n_kv) commit(B_QE + qb);        // this item's last S issued
-                if (j < it.n0) {
-                    if (j == 0 && kw[0] > 0 && !(ok = wait(B_OF + 0, kw[0] - 1, 0x216))) break;
-                    if (!(ok = wait(B_PF + 0, b0 + j, 0x217))) break;
-                    tc_fence_after();
-                    issue_PV(0, (g + j) % kStages, j == 0);
+                        for (int kk = 0; kk < BN / 16; kk++)      // 16 keys per step: 8 packed TMEM
+                            mma_bf16_ts(d_t, pt + kk * 8, vd + 128 * kk, idO, (j > 0 || kk > 0));   // columns of P
+                        mma_commit(BAR(B_OD + i));
+                    }
+                    __syncwarp();
+                    release(B_KVE + st, true);
+                    t++;
                 }
-                if (it.has_q1) {
-                    if (j == 0 && kw[1] > 0 && !(ok = wait(B_OF + 1, kw[1] - 1, 0x218))) break;
-                    if (!(ok = wait(B_PF + 1, b1 + j, 0x219))) break;
-                    tc_fence_after();
-                    issue_PV(1, (g + j) % kStages, j == 0);
-                }
-                commit(B_KVE + (g + j) % kStages);           // stage free once these MMAs finish
+                if (n > 0) kw++;
+                g += it.n_kv;
             }
-            g += it.n_kv;
-            t[0] += it.n0;
-            kw[0] += 1;
-            if (it.has_q1) { t[1] += it.n1; kw[1] += 1; }
         }
     } else if (warp >= 4) {
         // ------------------------------------------------------------ softmax
@@ -424,7 +434,8 @@ fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
                     const uint64_t x2 = fma2(f2(__uint_as_float(s[2 * c2]), __uint_as_float(s[2 * c2 + 1])), scale2, negm2);
                     float xl, xh;
                     f2_split(x2, xl, xh);
-                    const uint64_t e2 = f2(ex2(xl), ex2(xh));
+                    // kPolyPairs of every 8 pairs on the FMA pipe, the rest on MUFU
+                    const uint64_t e2 = (c2 & 7) < kPolyPairs ? exp2_poly2(x2) : f2(ex2(xl), ex2(xh));
                     lp2[c2 & 3] = add2(lp2[c2 & 3], e2);
                     float el, eh;
                     f2_split(e2, el, eh);

@@ -251,6 +251,31 @@ __device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
     asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
     return d;
 }
+// 2^x for a pair of floats on the FMA pipe (moves part of a softmax's
+// exponentials off the MUFU unit).  x is clamped to [-125, +inf) (smaller
+// values give 2^-125, negligible against a row sum >= 1); x = r + f with
+// r = round(x) taken with the 1.5 * 2^23 shifter, 2^f on [-0.5, 0.5] from a
+// cubic whose coefficients are this file's own minimax fit of 2^f on that
+// interval (relative error 7.5e-5; the result feeds bf16 probabilities), and
+// the integer r added to the exponent field.
+__device__ __forceinline__ uint64_t exp2_poly2(uint64_t x2) {
+    float xl, xh;
+    f2_split(x2, xl, xh);
+    const uint64_t x = f2(fmaxf(xl, -125.f), fmaxf(xh, -125.f));
+    const uint64_t shifter = f2(12582912.f, 12582912.f);
+    const uint64_t t = add2(x, shifter);                                   // 1.5 * 2^23 + round(x)
+    const uint64_t r = add2(t, f2(-12582912.f, -12582912.f));              // round(x), exact
+    const uint64_t fr = fma2(r, f2(-1.f, -1.f), x);                        // x - round(x), exact
+    uint64_t p = fma2(f2(0.0551716685f, 0.0551716685f), fr, f2(0.242611125f, 0.242611125f));
+    p = fma2(p, fr, f2(0.693260968f, 0.693260968f));
+    p = fma2(p, fr, f2(0.999928057f, 0.999928057f));
+    float pl, ph, tl, th;
+    f2_split(p, pl, ph);
+    f2_split(t, tl, th);
+    // the low mantissa bits of t hold round(x); shifted by 23 they are the exponent increment
+    return f2(__uint_as_float(__float_as_uint(pl) + (__float_as_uint(tl) << 23)),
+              __uint_as_float(__float_as_uint(ph) + (__float_as_uint(th) << 23)));
+}
 __device__ __forceinline__ float max3(float a, float b, float c) {
     float d;
     asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
