@@ -11,8 +11,9 @@ A step is one call of the path over one batch of synthetic input that is
 already resident in HBM.  Multi-GPU (torchrun, one process per GPU) is weak
 scaling: every rank runs its own full-size batch of (batch x head) units; no
 collective touches the data path.  The per-step device time comes from CUDA
-events around the call on the launching stream; the L2 is flushed between
-steps when the working set fits in it.  `e2e` times the same call through the
+events around the call on the launching stream.  No step starts L2-warm:
+when one step's working set is below 2 x L2, the step's device tensors are
+rotated over enough copies that together they exceed it.  `e2e` times the same call through the
 C ABI with the inputs copied from pinned host memory and the output copied
 back inside the timed region.
 
@@ -277,9 +278,32 @@ class Workload:
             self.out_bytes = n * H * d * 4
             self.working_set = self.work
 
+    # device tensors a step reads or writes, per kind (the rotated input sets)
+    _ROT = {"fwd": ("q", "k", "v", "o", "lse"), "bwd": ("q", "k", "v", "o", "lse", "do", "dq", "dk", "dv"),
+            "decode": ("kc", "vc", "kp", "vp"), "ragged": ()}
+
+    def rotate_inputs(self, n):
+        """Keeps n copies of the step's device tensors and cycles through them,
+        so that with n x working set > 2 x L2 every step starts from inputs that
+        are not L2-resident (instead of flushing the L2 between steps)."""
+        names = self._ROT[self.cfg["kind"]]
+        base = {k: getattr(self, k) for k in names}
+        self.sets = [base]
+        for _ in range(n - 1):
+            cp = {k: (v.clone() if not isinstance(v, list) else [t.clone() for t in v]) for k, v in base.items()}
+            if "kp" in cp:   # the decode pointer tables point at this copy's caches
+                cp["kp"] = self.torch.tensor([t.data_ptr() for t in cp["kc"]], dtype=self.torch.int64, device=self.dev)
+                cp["vp"] = self.torch.tensor([t.data_ptr() for t in cp["vc"]], dtype=self.torch.int64, device=self.dev)
+            self.sets.append(cp)
+        self.rot = 0
+
     def step(self, stream):
         A, c = self.A, self.cfg
         kind = c["kind"]
+        if getattr(self, "sets", None) and len(self.sets) > 1:
+            for k_, v_ in self.sets[self.rot % len(self.sets)].items():
+                setattr(self, k_, v_)
+            self.rot += 1
         if kind == "fwd":
             A.fwd_ex(self.shape, self.dtype_code, self.q.data_ptr(), self.k.data_ptr(), self.v.data_ptr(),
                      self.o.data_ptr(), self.lse.data_ptr(), stream)
@@ -343,8 +367,11 @@ def run_ours(args, cfg):
 
     wl = Workload(cfg, A, torch, dev)
     stream = torch.cuda.Stream(device=dev)
-    flush = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device=dev) if wl.working_set < 2 * L2_BYTES \
-        else None
+    # Inputs larger than L2 between timed steps: when one step's working set is
+    # below 2 x L2, the step's tensors are rotated over enough copies.
+    n_sets = 1 if wl.working_set >= 2 * L2_BYTES else max(2, -(-5 * L2_BYTES // (2 * int(wl.working_set))))
+    if n_sets > 1:
+        wl.rotate_inputs(n_sets)
 
     def barrier():
         if world > 1:
@@ -352,8 +379,6 @@ def run_ours(args, cfg):
 
     with torch.cuda.stream(stream):
         for _ in range(args.warmup):
-            if flush is not None:
-                flush.zero_()
             wl.step(stream.cuda_stream)
         stream.synchronize()
         starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
@@ -363,8 +388,9 @@ def run_ours(args, cfg):
         with Clocks(local) as clk:
             t_wall = time.perf_counter()
             for i in range(args.steps):
-                if flush is not None:
-                    flush.zero_()
+                # ~50 us of device sleep ahead of the start event, so that the
+                # host's enqueue of the call is not inside the timed interval
+                torch.cuda._sleep(100000)
                 starts[i].record(stream)
                 wl.step(stream.cuda_stream)
                 ends[i].record(stream)
@@ -415,7 +441,9 @@ def run_ours(args, cfg):
             "data": "synthetic (seeded normal inputs of the config's shape)",
             "config": {"workload": cfg["workload"], "config_key": args.config,
                        "parallelism": f"dp{world} over (batch x head) units, no collective",
-                       "l2": "flushed between steps" if flush is not None else "working set > L2",
+                       "l2": (f"inputs larger than L2: {n_sets} rotated copies of the step's tensors "
+                              f"({n_sets} x {wl.working_set / 2**20:.0f} MiB)") if n_sets > 1
+                             else "inputs larger than L2 (working set > 2 x L2)",
                        "wall_s_timed": round(t_wall, 4)},
             "roofline": {"bound": bound, "achieved": round(achieved, 2), "peak": peak, "unit": punit,
                          "frac": round(achieved / peak, 4), "traffic": TRAFFIC.get(args.config),
