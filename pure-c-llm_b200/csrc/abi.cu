@@ -1,6 +1,7 @@
 // abi.cu -- the C ABI of libattn_b200 (include/attn_b200.h): argument
 // checking, workspaces, the macro-shaped drop-ins for gpu_kernels.h, the device
 // KV cache, and the multi-GPU partition helpers.
+#include "decode_launch.cuh"
 #include <algorithm>
 #include <cstdarg>
 #include <cstdio>
@@ -29,20 +30,6 @@
 
 // ---- kernels' host launchers (other translation units) ----------------------
 namespace attn_host {
-struct DecodeLaunch {
-    int n_seq, heads, head_dim, kv_dtype, max_len;
-    long long row_stride, cap;
-    const float *q;
-    const void *kbase, *vbase;
-    const void *const *kptrs, *const *vptrs;
-    const float *ksbase, *vsbase;
-    const float *const *ksptrs, *const *vsptrs;
-    const int *lens;
-    float *out;
-    void *ws;
-    int *err;
-    cudaStream_t stream;
-};
 int launch_decode(const DecodeLaunch &L);
 size_t decode_workspace_bytes(int n_seq, int heads, int head_dim, int max_len, int kv_dtype);
 int launch_fwd_f32(int dtype, int D, const void *q, const void *k, const void *v, void *o,

@@ -23,6 +23,7 @@
 #include <algorithm>
 
 #include "common.cuh"
+#include "decode_launch.cuh"
 #include "sm100.cuh"
 
 namespace attn {
@@ -547,7 +548,10 @@ int rows_chunk(int max_len, int n_seq) {
     return (int)std::max(128LL, std::min(512LL, c));
 }
 
-size_t decode_workspace_bytes(int n_seq, int heads, int head_dim, int max_len, int kv_dtype) {
+size_t decode_stream_ws_bytes(int n_seq, int heads, int head_dim, int max_len);
+bool decode_stream_shape_ok(int heads, int head_dim, int kv_dtype);
+
+static size_t decode_split_ws_bytes(int n_seq, int heads, int head_dim, int max_len, int kv_dtype) {
     if (rows_i8_ok(heads, head_dim, kv_dtype)) {
         const int rc = rows_chunk(max_len, n_seq);
         const long long rsplits = (max_len + rc - 1) / rc;
@@ -569,20 +573,15 @@ size_t decode_workspace_bytes(int n_seq, int heads, int head_dim, int max_len, i
     return (b + 255) / 256 * 256;
 }
 
-struct DecodeLaunch {
-    int n_seq, heads, head_dim, kv_dtype, max_len;
-    long long row_stride, cap;
-    const float *q;
-    const void *kbase, *vbase;
-    const void *const *kptrs, *const *vptrs;
-    const float *ksbase, *vsbase;
-    const float *const *ksptrs, *const *vsptrs;
-    const int *lens;
-    float *out;
-    void *ws;
-    int *err;
-    cudaStream_t stream;
-};
+// Covers whichever kernel the call's pointers select: the streaming kernel
+// (shape and alignment permitting) or the split kernels.
+size_t decode_workspace_bytes(int n_seq, int heads, int head_dim, int max_len, int kv_dtype) {
+    size_t b = decode_split_ws_bytes(n_seq, heads, head_dim, max_len, kv_dtype);
+    if (decode_stream_shape_ok(heads, head_dim, kv_dtype))
+        b = std::max(b, decode_stream_ws_bytes(n_seq, heads, head_dim, max_len));
+    return b;
+}
+
 
 template <int D, bool I8>
 static int launch_decode_t(const DecodeLaunch &L) {
@@ -665,8 +664,14 @@ static int launch_rows_i8(const DecodeLaunch &L) {
     }
 }
 
+bool decode_stream_ok(const DecodeLaunch &L);
+bool decode_stream_shape_ok(int heads, int head_dim, int kv_dtype);
+size_t decode_stream_ws_bytes(int n_seq, int heads, int head_dim, int max_len);
+int launch_decode_stream(const DecodeLaunch &L);
+
 int launch_decode(const DecodeLaunch &L) {
     const bool i8 = L.kv_dtype == ATTN_I8;
+    if (decode_stream_ok(L)) return launch_decode_stream(L);
     if (rows_i8_ok(L.heads, L.head_dim, L.kv_dtype)) return launch_rows_i8(L);
     switch (L.head_dim) {
         case 32: return i8 ? launch_decode_t<32, true>(L) : launch_decode_t<32, false>(L);
