@@ -43,7 +43,8 @@ constexpr int TILE_BYTES = BT * D * 2;        // one 128 x 64 bf16 tile (16 KB)
 constexpr int TM_X = 0, TM_Y = 128, TM_A1 = 256, TM_A2 = 320, TM_W1 = 384, TM_W2 = 448, TM_COLS = 512;
 
 // barrier slots
-enum { B_FIX = 0, B_SF = 1, B_SE = 1 + kStages, B_XY = 1 + 2 * kStages, B_XYE, B_W, B_ACC, B_COUNT };
+enum { B_FIX = 0, B_SF = 1, B_SE = 1 + kStages, B_XY = 1 + 2 * kStages, B_XYE, B_W, B_ACC, B_ST, B_COUNT };
+static_assert(B_COUNT * 8 <= 128, "barrier area");
 
 struct Params {
     void *out1, *out2;           // dkdv: dK, dV;  dq: dQ
@@ -123,6 +124,7 @@ bwd_kernel(const __grid_constant__ CUtensorMap m_a, const __grid_constant__ CUte
         mbar_init(BAR(B_XYE), 128);
         mbar_init(BAR(B_W), 128);
         mbar_init(BAR(B_ACC), 1);
+        mbar_init(BAR(B_ST), 128);
         *abort_flag = 0;
         fence_mbar_init();
     }
@@ -234,7 +236,14 @@ bwd_kernel(const __grid_constant__ CUtensorMap m_a, const __grid_constant__ CUte
                 const int q = tcol * BT + row;
                 st_l[row] = q < p.T ? __ldg(p.lse2 + bh + q) : 0.f;
                 st_l[BT + row] = q < p.T ? __ldg(p.dvec + bh + q) : 0.f;
-                asm volatile("bar.sync 1, 128;" ::: "memory");
+                // the warpgroup's statistics are in shared memory before anyone reads
+                // them (an mbarrier with a bounded wait, so a warp that gave up on an
+                // earlier wait cannot leave the others blocked here)
+                mbar_arrive(BAR(B_ST));
+                if (!__all_sync(0xffffffffu, mbar_wait(BAR(B_ST), it & 1, abort_flag, p.err, 0x323))) {
+                    ok = false;
+                    break;
+                }
             }
             ok = mbar_wait(BAR(B_XY), it & 1, abort_flag, p.err, 0x321);
             if (it > 0 && ok) ok = mbar_wait(BAR(B_ACC), (it - 1) & 1, abort_flag, p.err, 0x322);
