@@ -19,8 +19,9 @@
 //   * warps 0-7 consume: warp w takes rows w and w + 8 of every 16-row block
 //     (two independent rows in flight per warp); lane l holds
 //     the 16-byte pieces l + 32k (k < CPL) of a row, the lanes of one head
-//     reduce its dot product with shuffles (codes become floats through a
-//     byte permute, f32x2 arithmetic), and each lane keeps an online
+//     reduce its dot product with shuffles (K codes meet the query's
+//     fixed-point digits in dp4a; V codes become floats through a byte
+//     permute, f32x2 arithmetic), and each lane keeps an online
 //     softmax state (running max, sum, weighted value sum) for its heads.
 //     The running max is only moved when a score exceeds it by more than 2^8
 //     (base-2 domain), so rescales are rare;
@@ -284,7 +285,11 @@ decode_stream_kernel(const __grid_constant__ Params p)
     } else {
         // ------------------------------------------------------------ consumers
         // this lane's query pieces (base-2 domain) as packed pairs; the head of each piece
-        uint64_t qv[CPL][8];
+        // The query as 24-bit fixed point per 16-value piece (max|q| * 2^e < 2^22),
+        // three signed byte digits per value, so K codes enter the dot products
+        // as raw bytes through dp4a; the int32 sums are exact.
+        uint32_t qd[CPL][3][4];
+        float qe[CPL];                               // 2^-e of each piece's fixed point
         int hk[CPL];
 #pragma unroll
         for (int k = 0; k < CPL; k++) hk[k] = (lane + 32 * k) / G::LPH;
@@ -336,11 +341,38 @@ decode_stream_kernel(const __grid_constant__ Params p)
                 if (e != cur_e) {
                     const float *qp = p.q + (long long)e * HD;
 #pragma unroll
-                    for (int k = 0; k < CPL; k++)
+                    for (int k = 0; k < CPL; k++) {
+                        float qf[16];
+                        float mxq = 0.f;
 #pragma unroll
-                        for (int i = 0; i < 8; i++)
-                            qv[k][i] = f2(qp[(lane + 32 * k) * 16 + 2 * i] * p.qscale,
-                                          qp[(lane + 32 * k) * 16 + 2 * i + 1] * p.qscale);
+                        for (int i = 0; i < 16; i++) {
+                            qf[i] = qp[(lane + 32 * k) * 16 + i] * p.qscale;
+                            mxq = fmaxf(mxq, fabsf(qf[i]));
+                        }
+                        // scale 2^e with max|q| * 2^e < 2^22
+                        // (capped: a query below 2^-79 keeps an absolute error under 2^-101)
+                        const int ex = mxq > 0.f ? min(100, 21 - (int)((__float_as_uint(mxq) >> 23) & 0xff) + 127) : 0;
+                        const float up = ldexpf(1.f, ex);
+                        qe[k] = ldexpf(1.f, -ex);
+#pragma unroll
+                        for (int wd = 0; wd < 4; wd++) {
+                            uint32_t d0w = 0, d1w = 0, d2w = 0;
+#pragma unroll
+                            for (int j = 0; j < 4; j++) {
+                                const int qi = __float2int_rn(qf[4 * wd + j] * up);
+                                const int d0 = ((qi & 0xff) ^ 0x80) - 0x80;
+                                const int r1 = (qi - d0) >> 8;
+                                const int d1 = ((r1 & 0xff) ^ 0x80) - 0x80;
+                                const int d2 = (r1 - d1) >> 8;
+                                d0w |= (uint32_t)(d0 & 0xff) << (8 * j);
+                                d1w |= (uint32_t)(d1 & 0xff) << (8 * j);
+                                d2w |= (uint32_t)(d2 & 0xff) << (8 * j);
+                            }
+                            qd[k][0][wd] = d0w;
+                            qd[k][1][wd] = d1w;
+                            qd[k][2][wd] = d2w;
+                        }
+                    }
                     cur_e = e;
                 }
 #pragma unroll
@@ -368,14 +400,18 @@ decode_stream_kernel(const __grid_constant__ Params p)
                 for (int k = 0; k < CPL; k++) {
                     const uint4 kw = kr[lane + 32 * k];
                     vraw[j][k] = vr[lane + 32 * k];
-                    const uint32_t w[4] = {kw.x ^ 0x80808080u, kw.y ^ 0x80808080u, kw.z ^ 0x80808080u,
-                                           kw.w ^ 0x80808080u};
-                    uint64_t a2 = 0ull;
+                    // signed codes . fixed-point query digits (exact int32 sums)
+                    const int kwv[4] = {(int)kw.x, (int)kw.y, (int)kw.z, (int)kw.w};
+                    int ia[3] = {0, 0, 0};
 #pragma unroll
-                    for (int x = 0; x < 8; x++) a2 = fma2(qv[k][x], add2(codes2(w[x >> 1], (x & 1) * 2), bias2), a2);
-                    float al, ah;
-                    f2_split(a2, al, ah);
-                    float acc = al + ah;
+                    for (int wd = 0; wd < 4; wd++)
+#pragma unroll
+                        for (int d = 0; d < 3; d++) ia[d] = __dp4a(kwv[wd], (int)qd[k][d][wd], ia[d]);
+                    // |sum| < 2^22: exact float through the 1.5 * 2^23 shifter
+                    const float c0 = __int_as_float(ia[0] + 0x4B400000) - 12582912.f;
+                    const float c1 = __int_as_float(ia[1] + 0x4B400000) - 12582912.f;
+                    const float c2 = __int_as_float(ia[2] + 0x4B400000) - 12582912.f;
+                    float acc = fmaf(c2, 65536.f, fmaf(c1, 256.f, c0)) * qe[k];
 #pragma unroll
                     for (int off = G::LPH / 2; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
                     sc[j][k] = live ? acc * ks[hk[k]] : -INFINITY;
