@@ -59,9 +59,9 @@ CONFIGS = {
 }
 L2_BYTES = 126 * 2 ** 20
 # dram__bytes_read.sum + dram__bytes_write.sum per launch of the dominant
-# kernel, from the ncu captures summarised under profiles/ (fwd_bf16_c3.md,
-# decode_c4f32.md, decode_c4int8.md, fwd_f32_c2.md); None where not captured
-TRAFFIC = {"c3-bf16": 51208192, "c4-f32": 2153309904, "c4-int8": 576229888, "c2": 52688896}
+# kernel, each from one ncu capture of that kernel at the config's size;
+# None where not captured
+TRAFFIC = {"c3-bf16": 51817984, "c4-f32": 2153309904, "c4-int8": 577940736, "c2": 52688896}
 
 
 def causal_flops(B, H, T, d):
