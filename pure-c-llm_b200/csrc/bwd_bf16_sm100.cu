@@ -8,9 +8,11 @@
 // come from the shared rowdot pre-pass into the workspace.
 //
 // Two deterministic kernels (no atomics), each one CTA per 128-row tile of one
-// (batch, head), 8 warps: warp 0 TMA producer, warp 1 MMA issuer (one
-// thread), warps 4-7 an elementwise warpgroup (one thread per TMEM lane = one
-// row of the CTA's tile); warps 2-3 idle.
+// (batch, head), 12 warps: warp 0 TMA producer; warps 1 and 2 MMA issuers
+// (warp 1 the S/dP products, warp 2 the accumulations; warp-converged loops,
+// the elected lane issues); warp 3 idle; warps 4-7 and 8-11 two elementwise
+// warpgroups, one thread per TMEM lane (= one row of the CTA's tile), the
+// first taking columns 0-63 of each streamed tile, the second 64-127.
 //   dkdv: key tile kt, loops over query tiles i >= kt.  S^T = K Q_i^T and
 //         dP^T = V dO_i^T (both operands in shared memory) into TMEM; the
 //         warpgroup writes P^T and dS^T as bf16 pairs into TMEM; then
@@ -35,7 +37,8 @@ using namespace sm100;
 constexpr int BT = 128;           // rows per tile (TMEM lanes) and columns per tile
 constexpr int D = 64;             // head_dim covered by these kernels
 constexpr int kStages = 3;
-constexpr int kThreads = 256;
+constexpr int kThreads = 384;
+constexpr int kPolyPairs = 3;     // exponential pairs (of 8) computed by exp2_poly2 on the FMA pipe
 constexpr int TILE_BYTES = BT * D * 2;        // one 128 x 64 bf16 tile (16 KB)
 
 // TMEM columns (both kernels): X = S or S^T, Y = dP or dP^T (fp32, 128 each),
@@ -61,9 +64,10 @@ struct Smem {
     uint8_t *ptr;
 };
 
-__device__ __forceinline__ void store_row_bf16(__nv_bfloat16 *dst, const uint32_t (&acc)[D], bool accumulate) {
+template <int N>
+__device__ __forceinline__ void store_row_bf16(__nv_bfloat16 *dst, const uint32_t (&acc)[N], bool accumulate) {
 #pragma unroll
-    for (int c = 0; c < D; c += 8) {
+    for (int c = 0; c < N; c += 8) {
         float v[8];
 #pragma unroll
         for (int u = 0; u < 8; u++) v[u] = __uint_as_float(acc[c + u]);
@@ -121,10 +125,10 @@ bwd_kernel(const __grid_constant__ CUtensorMap m_a, const __grid_constant__ CUte
         mbar_init(BAR(B_FIX), 1);
         for (int s = 0; s < kStages; s++) { mbar_init(BAR(B_SF + s), 1); mbar_init(BAR(B_SE + s), 1); }
         mbar_init(BAR(B_XY), 1);
-        mbar_init(BAR(B_XYE), 128);
-        mbar_init(BAR(B_W), 128);
+        mbar_init(BAR(B_XYE), 256);
+        mbar_init(BAR(B_W), 256);
         mbar_init(BAR(B_ACC), 1);
-        mbar_init(BAR(B_ST), 128);
+        mbar_init(BAR(B_ST), 256);
         *abort_flag = 0;
         fence_mbar_init();
     }
@@ -137,6 +141,10 @@ bwd_kernel(const __grid_constant__ CUtensorMap m_a, const __grid_constant__ CUte
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
+    // registers: 384 x 168 at launch; warpgroup 0 (TMA, MMA warps) gives back
+    // down to 72 so the two elementwise warpgroups can hold 216 each
+    // (128 x 72 + 256 x 216 = 384 x 168); each setmaxnreg inside its branch.
+    if (warp < 4) regs_dec<72>();
     if (warp == 0) {
         // ------------------------------------------------------------ producer
         if (lane == 0) {
@@ -158,66 +166,71 @@ bwd_kernel(const __grid_constant__ CUtensorMap m_a, const __grid_constant__ CUte
                 tma_load_3d(dst + TILE_BYTES, &m_d, BAR(B_SF + st), h * D, (first + it) * BT, b);
             }
         }
-    } else if (warp == 1) {
-        // ------------------------------------------------------------ MMA issuer
-        if (lane == 0) {
+    } else if (warp == 1 || warp == 2) {
+        // ------------------------------------------------------------ MMA issuers
+        // warp 1: X/Y products of each streamed tile; warp 2: the accumulations.
+        const bool leader = elect_one();
+        auto wait = [&](int b, int parity, int code) -> bool {
+            return __all_sync(0xffffffffu, mbar_wait(BAR(b), parity & 1, abort_flag, p.err, code));
+        };
+        if (warp == 1) {
             constexpr uint32_t idXY = idesc_bf16(BT, BT, 0, 0);    // both operands K-major (along d)
-            constexpr uint32_t idAcc = idesc_bf16(BT, D, 0, 1);    // A from TMEM, B MN-major
             // X, Y for streamed tile `it`:  dkdv: X = K Q^T, Y = V dO^T;  dq: X = Q K^T, Y = dO V^T
-            auto issue_xy = [&](int it) {
+            bool ok = wait(B_FIX, 0, 0x311);
+            for (int it = 0; ok && it < count; it++) {
+                if (!(ok = wait(B_SF + it % kStages, it / kStages, 0x312))) break;
+                if (it > 0 && !(ok = wait(B_XYE, it - 1, 0x314))) break;   // X/Y of the previous tile read
+                tc_fence_after();
                 const uint32_t stg = sST + (it % kStages) * 2 * TILE_BYTES;
                 const uint64_t fa = sw128_desc(sA, 16, 1024), fb = sw128_desc(sB, 16, 1024);
                 const uint64_t sc = sw128_desc(stg, 16, 1024), sd = sw128_desc(stg + TILE_BYTES, 16, 1024);
+                if (leader) {
 #pragma unroll
-                for (int kk = 0; kk < D / 16; kk++) mma_bf16_ss(tmem + TM_X, fa + 2 * kk, sc + 2 * kk, idXY, kk > 0);
+                    for (int kk = 0; kk < D / 16; kk++)
+                        mma_bf16_ss(tmem + TM_X, fa + 2 * kk, sc + 2 * kk, idXY, kk > 0);
 #pragma unroll
-                for (int kk = 0; kk < D / 16; kk++) mma_bf16_ss(tmem + TM_Y, fb + 2 * kk, sd + 2 * kk, idXY, kk > 0);
-                mma_commit(BAR(B_XY));
-            };
-            // accumulators for streamed tile `it`
+                    for (int kk = 0; kk < D / 16; kk++)
+                        mma_bf16_ss(tmem + TM_Y, fb + 2 * kk, sd + 2 * kk, idXY, kk > 0);
+                    mma_commit(BAR(B_XY));
+                }
+                __syncwarp();
+            }
+        } else {
+            constexpr uint32_t idAcc = idesc_bf16(BT, D, 0, 1);    // A from TMEM, B MN-major
             //   dkdv: A1 (dV) += W1 (P^T) . dO_i,  A2 (dK) += W2 (dS^T) . Q_i
             //   dq:   A1 (dQ) += W2 (dS) . K_j
-            auto issue_acc = [&](int it) {
+            // (tile it's X/Y products finished before its W was written, so this
+            // warp's commit alone frees the stage)
+            for (int it = 0; it < count; it++) {
+                if (!wait(B_W, it, 0x315)) break;
+                tc_fence_after();
                 const uint32_t stg = sST + (it % kStages) * 2 * TILE_BYTES;
-                if (KIND == 0) {
-                    const uint64_t dq_ = sw128_desc(stg, 16384, 1024);          // Q_i, MN-major
-                    const uint64_t ddo = sw128_desc(stg + TILE_BYTES, 16384, 1024);   // dO_i, MN-major
+                if (leader) {
+                    if (KIND == 0) {
+                        const uint64_t dq_ = sw128_desc(stg, 16384, 1024);                 // Q_i, MN-major
+                        const uint64_t ddo = sw128_desc(stg + TILE_BYTES, 16384, 1024);    // dO_i, MN-major
 #pragma unroll
-                    for (int kk = 0; kk < BT / 16; kk++)
-                        mma_bf16_ts(tmem + TM_A1, tmem + TM_W1 + kk * 8, ddo + 128 * kk, idAcc, it > 0 || kk > 0);
+                        for (int kk = 0; kk < BT / 16; kk++)
+                            mma_bf16_ts(tmem + TM_A1, tmem + TM_W1 + kk * 8, ddo + 128 * kk, idAcc, it > 0 || kk > 0);
 #pragma unroll
-                    for (int kk = 0; kk < BT / 16; kk++)
-                        mma_bf16_ts(tmem + TM_A2, tmem + TM_W2 + kk * 8, dq_ + 128 * kk, idAcc, it > 0 || kk > 0);
-                } else {
-                    const uint64_t dk = sw128_desc(stg, 16384, 1024);           // K_j, MN-major
+                        for (int kk = 0; kk < BT / 16; kk++)
+                            mma_bf16_ts(tmem + TM_A2, tmem + TM_W2 + kk * 8, dq_ + 128 * kk, idAcc, it > 0 || kk > 0);
+                    } else {
+                        const uint64_t dk = sw128_desc(stg, 16384, 1024);                  // K_j, MN-major
 #pragma unroll
-                    for (int kk = 0; kk < BT / 16; kk++)
-                        mma_bf16_ts(tmem + TM_A1, tmem + TM_W2 + kk * 8, dk + 128 * kk, idAcc, it > 0 || kk > 0);
+                        for (int kk = 0; kk < BT / 16; kk++)
+                            mma_bf16_ts(tmem + TM_A1, tmem + TM_W2 + kk * 8, dk + 128 * kk, idAcc, it > 0 || kk > 0);
+                    }
+                    mma_commit(BAR(B_ACC));
+                    mma_commit(BAR(B_SE + it % kStages));     // streamed stage free
                 }
-                mma_commit(BAR(B_ACC));
-                mma_commit(BAR(B_SE + it % kStages));     // streamed stage free
-            };
-            bool ok = mbar_wait(BAR(B_FIX), 0, abort_flag, p.err, 0x311) &&
-                      mbar_wait(BAR(B_SF + 0), 0, abort_flag, p.err, 0x312);
-            if (ok) {
-                tc_fence_after();
-                issue_xy(0);
-            }
-            for (int it = 0; ok && it < count; it++) {
-                if (it + 1 < count) {
-                    const int nx = it + 1;
-                    if (!(ok = mbar_wait(BAR(B_SF + nx % kStages), (nx / kStages) & 1, abort_flag, p.err, 0x313))) break;
-                    if (!(ok = mbar_wait(BAR(B_XYE), it & 1, abort_flag, p.err, 0x314))) break;
-                    tc_fence_after();
-                    issue_xy(nx);
-                }
-                if (!(ok = mbar_wait(BAR(B_W), it & 1, abort_flag, p.err, 0x315))) break;
-                tc_fence_after();
-                issue_acc(it);
+                __syncwarp();
             }
         }
     } else if (warp >= 4) {
         // ------------------------------------------------------------ elementwise
+        regs_inc<216>();
+        const int half = (warp - 4) >> 2;            // columns [64 half, 64 half + 64) of each tile
         const int quad = warp & 3;
         const int row = quad * 32 + lane;            // TMEM lane = row of the CTA's fixed tile
         const uint32_t lb = (uint32_t)(quad * 32) << 16;
@@ -233,12 +246,14 @@ bwd_kernel(const __grid_constant__ CUtensorMap m_a, const __grid_constant__ CUte
             const int tcol = first + it;             // streamed tile index
             float *st_l = stats + (it % kStages) * 2 * BT;   // dkdv: lse2 / D of the query columns
             if (KIND == 0) {
-                const int q = tcol * BT + row;
-                st_l[row] = q < p.T ? __ldg(p.lse2 + bh + q) : 0.f;
-                st_l[BT + row] = q < p.T ? __ldg(p.dvec + bh + q) : 0.f;
-                // the warpgroup's statistics are in shared memory before anyone reads
-                // them (an mbarrier with a bounded wait, so a warp that gave up on an
-                // earlier wait cannot leave the others blocked here)
+                if (half == 0) {
+                    const int q = tcol * BT + row;
+                    st_l[row] = q < p.T ? __ldg(p.lse2 + bh + q) : 0.f;
+                    st_l[BT + row] = q < p.T ? __ldg(p.dvec + bh + q) : 0.f;
+                }
+                // the statistics are in shared memory before anyone reads them (an
+                // mbarrier with a bounded wait, so a warp that gave up on an earlier
+                // wait cannot leave the others blocked here)
                 mbar_arrive(BAR(B_ST));
                 if (!__all_sync(0xffffffffu, mbar_wait(BAR(B_ST), it & 1, abort_flag, p.err, 0x323))) {
                     ok = false;
@@ -250,68 +265,82 @@ bwd_kernel(const __grid_constant__ CUtensorMap m_a, const __grid_constant__ CUte
             if (!(ok = __all_sync(0xffffffffu, ok))) break;
             tc_fence_after();
             const bool diag = (tcol == fixed);
-#pragma unroll 1
-            for (int c0 = 0; c0 < BT; c0 += 32) {
-                uint32_t xs[32], ys[32];
-                tmem_ld32(tmem + lb + TM_X + c0, xs);
-                tmem_ld32(tmem + lb + TM_Y + c0, ys);
-                tmem_wait_ld();
-                if (c0 == BT - 32) {                 // X and Y fully read: the next products may start
-                    tc_fence_before();
-                    mbar_arrive(BAR(B_XYE));
+            // this half's 64 columns of X and Y in one round trip
+            uint32_t xs[64], ys[64];
+#pragma unroll
+            for (int q2 = 0; q2 < 2; q2++) {
+                uint32_t t0[32], t1[32];
+                tmem_ld32(tmem + lb + TM_X + 64 * half + 32 * q2, t0);
+                tmem_ld32(tmem + lb + TM_Y + 64 * half + 32 * q2, t1);
+#pragma unroll
+                for (int c = 0; c < 32; c++) {
+                    xs[32 * q2 + c] = t0[c];
+                    ys[32 * q2 + c] = t1[c];
                 }
+            }
+            tmem_wait_ld();
+            tc_fence_before();
+            mbar_arrive(BAR(B_XYE));                 // X and Y read: the next products may start
+#pragma unroll
+            for (int q2 = 0; q2 < 2; q2++) {
                 uint32_t wp[16], wd[16];
 #pragma unroll
                 for (int c = 0; c < 32; c += 2) {
-                    float pv[2], dv[2];
+                    const int cc = 32 * q2 + c;          // column within this half
+                    float xa[2], l2[2], dd[2];
+                    bool masked[2];
 #pragma unroll
                     for (int u = 0; u < 2; u++) {
-                        const int col = c0 + c + u;
-                        float l2, dd;
-                        bool masked;
+                        const int col = 64 * half + cc + u;
                         if (KIND == 0) {             // row = key, col = query
-                            l2 = st_l[col];
-                            dd = st_l[BT + col];
-                            masked = (diag && col < row) || (tcol * BT + col >= p.T);
+                            l2[u] = st_l[col];
+                            dd[u] = st_l[BT + col];
+                            masked[u] = (diag && col < row) || (tcol * BT + col >= p.T);
                         } else {                     // row = query, col = key
-                            l2 = my_lse2;
-                            dd = my_d;
-                            masked = diag && col > row;
+                            l2[u] = my_lse2;
+                            dd[u] = my_d;
+                            masked[u] = diag && col > row;
                         }
-                        const float pr = masked ? 0.f : ex2(fmaf(__uint_as_float(xs[c + u]), p.scale_log2, -l2));
-                        pv[u] = pr;
-                        dv[u] = pr * (__uint_as_float(ys[c + u]) - dd) * p.ds_scale;
+                        xa[u] = fmaf(__uint_as_float(xs[cc + u]), p.scale_log2, -l2[u]);
+                    }
+                    // kPolyPairs of every 8 pairs on the FMA pipe, the rest on MUFU
+                    float pv[2];
+                    if (((cc >> 1) & 7) < kPolyPairs) {
+                        f2_split(exp2_poly2(f2(xa[0], xa[1])), pv[0], pv[1]);
+                    } else {
+                        pv[0] = ex2(xa[0]);
+                        pv[1] = ex2(xa[1]);
+                    }
+                    float dv[2];
+#pragma unroll
+                    for (int u = 0; u < 2; u++) {
+                        if (masked[u]) pv[u] = 0.f;
+                        dv[u] = pv[u] * (__uint_as_float(ys[cc + u]) - dd[u]) * p.ds_scale;
                     }
                     wp[c / 2] = pack_bf16(pv[0], pv[1]);
                     wd[c / 2] = pack_bf16(dv[0], dv[1]);
                 }
-                if (KIND == 0) tmem_st16(tmem + lb + TM_W1 + c0 / 2, wp);
-                tmem_st16(tmem + lb + TM_W2 + c0 / 2, wd);
+                if (KIND == 0) tmem_st16(tmem + lb + TM_W1 + 32 * half + 16 * q2, wp);
+                tmem_st16(tmem + lb + TM_W2 + 32 * half + 16 * q2, wd);
             }
             tmem_wait_st();
             tc_fence_before();
             mbar_arrive(BAR(B_W));
         }
-        // epilogue: accumulators -> global
+        // epilogue: this half's 32 columns of each accumulator -> global
         if (ok && count > 0) ok = mbar_wait(BAR(B_ACC), (count - 1) & 1, abort_flag, p.err, 0x323);
         if (__all_sync(0xffffffffu, ok && count > 0)) {
             tc_fence_after();
             for (int a = 0; a < (KIND == 0 ? 2 : 1); a++) {
-                uint32_t acc[D];
-#pragma unroll
-                for (int c0 = 0; c0 < D; c0 += 32) {
-                    uint32_t t32[32];
-                    tmem_ld32(tmem + lb + (a ? TM_A2 : TM_A1) + c0, t32);
-#pragma unroll
-                    for (int c = 0; c < 32; c++) acc[c0 + c] = t32[c];
-                }
+                uint32_t acc[32];
+                tmem_ld32(tmem + lb + (a ? TM_A2 : TM_A1) + 32 * half, acc);
                 tmem_wait_ld();
                 if (grow_ < p.T) {
                     // dkdv: a=0 -> dV (out2), a=1 -> dK (out1);  dq: dQ (out1)
                     void *outp = KIND == 0 ? (a == 0 ? p.out2 : p.out1) : p.out1;
                     __nv_bfloat16 *dst = static_cast<__nv_bfloat16 *>(outp) +
-                                         ((long long)b * p.T + grow_) * p.out_stride + (long long)h * D;
-                    store_row_bf16(dst, acc, p.accumulate != 0);
+                                         ((long long)b * p.T + grow_) * p.out_stride + (long long)h * D + 32 * half;
+                    store_row_bf16<32>(dst, acc, p.accumulate != 0);
                 }
             }
         }
