@@ -394,3 +394,95 @@ def test_gather_permute(A):
     torch.cuda.synchronize()
     ref = staging.transpose(1, 2, 0, 3, 4).reshape(B * T, H * d)
     assert np.array_equal(host(out), ref)
+
+
+# ---------------------------------------------------------------------------
+# INT8 streaming decode kernel (1024-code rows): the paths its producer takes
+# ---------------------------------------------------------------------------
+def _int8_decode_case(A, H, d, lens, cap, row_pad=0, seed=90):
+    """Quantised caches (optionally with padded rows), decode, and the oracle
+    over the dequantised cache; returns (out, refs)."""
+    import torch
+    n_seq = len(lens)
+    width = H * d
+    kc = synth.normal(seed, (n_seq * cap, width))
+    vc = synth.normal(seed + 1, (n_seq * cap, width))
+    q = synth.normal(seed + 2, (n_seq, width))
+    kq, ksc = A.quantize_int8_t(dev(kc), H)
+    vq, vsc = A.quantize_int8_t(dev(vc), H)
+    if row_pad:
+        # the same codes in rows of width + row_pad bytes (strided slabs)
+        kp = torch.zeros((n_seq * cap, width + row_pad), dtype=torch.int8, device="cuda")
+        vp = torch.zeros_like(kp)
+        kp[:, :width] = kq
+        vp[:, :width] = vq
+        kq_in, vq_in = kp[:, :width], vp[:, :width]
+    else:
+        kq_in, vq_in = kq, vq
+    lens_t = dev(np.asarray(lens, dtype=np.int32))
+    out = A.decode_t(dev(q), kq_in, vq_in, lens_t, H, cap, cap, kscale=ksc, vscale=vsc)
+    torch.cuda.synchronize()
+    kd = O.dequantize_kv_int8(host(kq), host(ksc), H, d)
+    vd = O.dequantize_kv_int8(host(vq), host(vsc), H, d)
+    refs = [O.cached_attention(q[s], kd[s * cap:(s + 1) * cap], vd[s * cap:(s + 1) * cap], int(lens[s]) - 1, H, d)
+            for s in range(n_seq)]
+    return host(out), refs
+
+
+@pytest.mark.parametrize("H,d", [(16, 64), (8, 128)])
+def test_int8_stream_piece_boundaries(A, H, d):
+    """Lengths of 1 row, exactly one piece, one piece + 1, several pieces and the
+    capacity: every branch of the piece table and of the last, partial block."""
+    cap = 2100
+    lens = [1, 2, 15, 16, 17, 64, 65, 511, 512, 513, 1024, 1500, 2099, cap]
+    out, refs = _int8_decode_case(A, H, d, lens, cap)
+    for s, ref in enumerate(refs):
+        assert rel_err(out[s], ref) < F32_TOL, (s, lens[s])
+
+
+def test_int8_stream_strided_rows(A):
+    """Rows wider than H*d (per-row bulk copies instead of one copy per block)."""
+    lens = [300, 1, 777]
+    out, refs = _int8_decode_case(A, 16, 64, lens, 800, row_pad=64, seed=95)
+    for s, ref in enumerate(refs):
+        assert rel_err(out[s], ref) < F32_TOL, s
+
+
+def test_int8_stream_pointer_slabs(A):
+    """attn_decode_ptrs_ex with INT8 slabs and per-slab scale arrays."""
+    import torch
+    L, H, d, cap = 3, 16, 64, 700
+    lens = np.asarray([700, 123, 512], dtype=np.int32)
+    ks = [synth.normal(110 + l, (cap, H * d)) for l in range(L)]
+    vs = [synth.normal(120 + l, (cap, H * d)) for l in range(L)]
+    q = synth.normal(130, (L, H * d))
+    kq, ksc, vq, vsc = [], [], [], []
+    for l in range(L):
+        a, b = A.quantize_int8_t(dev(ks[l]), H)
+        c, e = A.quantize_int8_t(dev(vs[l]), H)
+        kq.append(a), ksc.append(b), vq.append(c), vsc.append(e)
+    ptrs = lambda ts: torch.tensor([t.data_ptr() for t in ts], dtype=torch.int64, device="cuda")
+    kp, vp, ksp, vsp = ptrs(kq), ptrs(vq), ptrs(ksc), ptrs(vsc)
+    qd = dev(q)
+    out = torch.empty_like(qd)
+    lens_t = dev(lens)
+    shape = A.DecodeShape(L, H, d, A.I8, 0, cap, cap)
+    A.check(A.lib.attn_decode_ptrs_ex(ctypes.byref(shape), qd.data_ptr(), kp.data_ptr(), vp.data_ptr(),
+                                      ksp.data_ptr(), vsp.data_ptr(), lens_t.data_ptr(), out.data_ptr(), None, 0,
+                                      None))
+    torch.cuda.synchronize()
+    for l in range(L):
+        kd = O.dequantize_kv_int8(host(kq[l]), host(ksc[l]), H, d)
+        vd = O.dequantize_kv_int8(host(vq[l]), host(vsc[l]), H, d)
+        ref = O.cached_attention(q[l], kd, vd, int(lens[l]) - 1, H, d)
+        assert rel_err(host(out)[l], ref) < F32_TOL, l
+
+
+def test_int8_decode_many_sequences_fallback(A):
+    """More sequences than the stream kernel's piece table holds (1024): the
+    split kernels take the call, with the same results."""
+    n_seq, H, d, cap = 1030, 16, 64, 24
+    lens = synth.uniform_int(140, n_seq, 1, cap)
+    out, refs = _int8_decode_case(A, H, d, [int(x) for x in lens], cap, seed=140)
+    for s in range(0, n_seq, 97):
+        assert rel_err(out[s], refs[s]) < F32_TOL, s
