@@ -39,6 +39,10 @@ int launch_fwd_bf16_sm100(int D, const void *q, const void *k, const void *v, vo
                           long long in_stride, long long out_stride, int B, int H, int T,
                           int *err, cudaStream_t s);
 bool fwd_bf16_sm100_supported(int D, long long in_stride, long long out_stride);
+int launch_fwd_tf32_sm100(int D, const void *q, const void *k, const void *v, void *o, float *lse,
+                          long long in_stride, long long out_stride, int B, int H, int T, int *err,
+                          cudaStream_t s);
+bool fwd_tf32_sm100_supported(int D, long long in_stride, long long out_stride);
 int launch_bwd_f32(int dtype, int D, const void *dout, const void *q, const void *k,
                    const void *v, const void *o, const float *lse, void *dq, void *dk, void *dv,
                    int accumulate, void *ws, long long in_stride, long long out_stride, int B,
@@ -184,6 +188,9 @@ int attn_fwd_ex(const attn_shape *s, int dtype, const void *Q, const void *K, co
     cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
     if (dtype == ATTN_BF16 && fwd_bf16_sm100_supported(s->head_dim, in_st, out_st))
         return launch_fwd_bf16_sm100(s->head_dim, Q, K, V, O, lse, in_st, out_st, s->batch,
+                                     s->heads, s->seq_len, device_error_ptr(), cs);
+    if (dtype == ATTN_F32 && fwd_tf32_sm100_supported(s->head_dim, in_st, out_st))
+        return launch_fwd_tf32_sm100(s->head_dim, Q, K, V, O, lse, in_st, out_st, s->batch,
                                      s->heads, s->seq_len, device_error_ptr(), cs);
     return launch_fwd_f32(dtype, s->head_dim, Q, K, V, O, lse, in_st, out_st, s->batch, s->heads,
                           s->seq_len, cs);

@@ -1,0 +1,672 @@
+// fwd_tf32_sm100.cu -- causal flash forward for fp32 tensors on the Blackwell
+// tensor cores with 3xTF32 products (sm_100a).
+//
+// Semantics: attention_forward, train.c:339-370, fp32 in and out.  Every
+// product of two fp32 values x * y is formed as xh*yh + xh*yl + xl*yh, where
+// xh is x with its 13 low mantissa bits cleared (exactly representable in
+// tf32, so the MMA's operand conversion leaves it unchanged) and xl = x - xh
+// (exact in fp32); the dropped xl*yl term and the tf32 view of the low parts
+// are ~2^-21 relative.  Scores, exponentials (MUFU ex2, no polynomial), sums
+// and accumulators are fp32, so results track the fp32 reference to ~1e-6.
+//
+// Persistent kernel, one query tile (128 rows) of one (batch, head) per work
+// item, items dealt longest-first to the CTAs (LPT); key tiles of 64 rows.
+// 12 warps per CTA:
+//   warp 0      TMA producer: the raw fp32 Q tile into the Q-high buffer, raw
+//               K and V tiles into the high halves of a 2-stage ring
+//   warp 1      S issuer: S = Qh Kh^T + Qh Kl^T + Ql Kh^T, M=128, N=64, K=8,
+//               tcgen05.mma kind::tf32, into one of two S buffers in TMEM
+//   warp 2      PV issuer: O += Ph Vh + Ph Vl + Pl Vh (P from TMEM)
+//   warp 3      spare
+//   warps 4-7   splitters: clear the low bits of each landed Q and K tile in
+//               place and write its low part next to it; write V transposed
+//               (V^T, K-major, so that PV's B operand is K-major) as high and
+//               low parts; then fence for the MMAs
+//   warps 8-11  softmax: a thread owns one query row (one TMEM lane), reads
+//               its S row, keeps the running max (rescaling O only when it
+//               grows by more than 2^8) and sum, and writes P's high part over
+//               the S row it read and P's low part to a separate TMEM block
+// TMEM (256 columns): S/Ph buffers [0,64) and [64,128), Pl [128,192), O
+// [192, 192+D).  An S buffer is reused once the PV that read its P finished.
+// Every mbarrier wait is bounded; a timeout records a code in the device
+// error word, raises a CTA-wide abort flag, and all roles fall through to the
+// teardown, which frees TMEM.
+#include "common.cuh"
+#include "sm100.cuh"
+
+#include <algorithm>
+#include <cudaTypedefs.h>
+#include <functional>
+#include <queue>
+#include <vector>
+
+namespace attn {
+namespace ftf {
+
+using namespace sm100;
+
+constexpr int BM = 128;            // query rows per tile (TMEM lanes)
+constexpr int BN = 64;             // keys per tile
+constexpr int kThreads = 384;
+constexpr int kMaxCtas = 320;
+constexpr int kMaxItems = 32768;
+constexpr int kLocalItems = 256;
+
+template <int D>
+struct Cfg {
+    static constexpr int CH = D / 32;               // 128-byte column chunks of a row
+    static constexpr int QB = BM * D * 4;           // one fp32 Q tile (high or low part)
+    static constexpr int KB = BN * D * 4;           // one fp32 K or V tile
+    static constexpr int OFF_QH = 0, OFF_QL = QB;
+    static constexpr int OFF_ST = 2 * QB;           // stages: Kh, Kl, V raw then V^T low, V^T high
+    static constexpr int STAGE = 4 * KB;
+    static constexpr int OFF_BAR = OFF_ST + 2 * STAGE;
+    static constexpr int OFF_ITEMS = OFF_BAR + 256;
+    static constexpr int SMEM = OFF_ITEMS + 4 * kLocalItems + 1024;
+    static constexpr int CTAS = 2 * (SMEM + 1024) <= 228 * 1024 ? 2 : 1;
+    static constexpr int TM_S = 0, TM_PL = 128, TM_O = 192, TM_COLS = 256;
+    // per-thread registers after setmaxnreg: warpgroup 0, splitters, softmax
+    // (two CTAs per SM: 384 x 80 at launch = 128 x (40 + 56 + 144); one CTA:
+    // 384 x 160 at launch >= 128 x (40 + 128 + 160))
+    static constexpr int REG_SPLIT = CTAS == 2 ? 56 : 128;
+    static constexpr int REG_SOFT = CTAS == 2 ? 144 : 160;
+    static_assert(TM_O + D <= TM_COLS, "TMEM budget");
+};
+
+enum {
+    B_QF = 0, B_QS, B_QE,          // query tile landed / split / free (item's last S done)
+    B_KVF = 3,                     // 2: stage landed
+    B_KVS = 5,                     // 2: stage split
+    B_KVE = 7,                     // 2: stage free (its S and its PV finished)
+    B_SF = 9,                      // 2: S buffer ready
+    B_BF = 11,                     // 2: S buffer free (the PV that read its P finished)
+    B_PF = 13,                     // P written (and O rescaled)
+    B_OD = 14,                     // PV finished
+    B_SPL = 15,                    // splitters: raw V read (before V^T overwrites it)
+    B_COUNT = 16
+};
+
+struct Params {
+    float *o;
+    float *lse;
+    long long out_stride;
+    int T, H, B, n_qt, n_items;
+    float scale_log2;              // log2(e) / sqrt(d)
+    int *err;
+    int use_list;
+    int packable;
+    const unsigned short *sched;   // [kMaxCtas + 1] list offsets, then the item lists
+};
+
+struct Item {
+    int h, b, q0, n_kv;
+};
+
+__device__ __forceinline__ void split_item(const Params &p, int i, int &b, int &h, int &qt) {
+    const int hb = p.H * p.B;
+    qt = p.n_qt - 1 - i / hb;
+    const int r = i % hb;
+    h = r % p.H;
+    b = r / p.H;
+}
+__device__ __forceinline__ Item make_item(int b, int h, int qt, int T) {
+    Item it;
+    it.b = b;
+    it.h = h;
+    it.q0 = qt * BM;
+    it.n_kv = (min(it.q0 + BM, T) + BN - 1) / BN;   // key tiles up to the diagonal
+    return it;
+}
+__device__ __forceinline__ int item_of(const Params &p, int k) {
+    if (p.use_list) {
+        const int idx = (int)__ldg(p.sched + blockIdx.x) + k;
+        return idx < (int)__ldg(p.sched + blockIdx.x + 1) ? (int)__ldg(p.sched + kMaxCtas + 1 + idx) : -1;
+    }
+    const int i = (int)blockIdx.x + k * (int)gridDim.x;
+    return i < p.n_items ? i : -1;
+}
+__device__ __forceinline__ uint32_t pack_item(const Params &p, int id) {
+    int b, h, qt;
+    split_item(p, id, b, h, qt);
+    return (uint32_t)b | (uint32_t)h << 12 | (uint32_t)qt << 22;
+}
+__device__ __forceinline__ bool next_item(const Params &p, const uint32_t *items_s, int n_local, int k, Item &it) {
+    if (n_local >= 0) {
+        if (k >= n_local) return false;
+        const uint32_t v = items_s[k];
+        it = make_item((int)(v & 0xfffu), (int)((v >> 12) & 0x3ffu), (int)(v >> 22), p.T);
+        return true;
+    }
+    const int id = item_of(p, k);
+    if (id < 0) return false;
+    int b, h, qt;
+    split_item(p, id, b, h, qt);
+    it = make_item(b, h, qt, p.T);
+    return true;
+}
+
+// x -> (high part in place, low part at the same offset of `lo`): n floats, 16-byte vectors
+__device__ __forceinline__ void split_hi_lo(float *hi, float *lo, int n, int tid, int nthreads) {
+    for (int i = tid * 4; i < n; i += nthreads * 4) {
+        float4 x = *reinterpret_cast<float4 *>(hi + i);
+        float4 h, l;
+        h.x = __uint_as_float(__float_as_uint(x.x) & 0xFFFFE000u);
+        h.y = __uint_as_float(__float_as_uint(x.y) & 0xFFFFE000u);
+        h.z = __uint_as_float(__float_as_uint(x.z) & 0xFFFFE000u);
+        h.w = __uint_as_float(__float_as_uint(x.w) & 0xFFFFE000u);
+        l.x = x.x - h.x;
+        l.y = x.y - h.y;
+        l.z = x.z - h.z;
+        l.w = x.w - h.w;
+        *reinterpret_cast<float4 *>(hi + i) = h;
+        *reinterpret_cast<float4 *>(lo + i) = l;
+    }
+}
+
+template <int D>
+__global__ void __launch_bounds__(kThreads, Cfg<D>::CTAS)
+fwd_tf32_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                const __grid_constant__ CUtensorMap tv, const __grid_constant__ Params p)
+{
+    using C = Cfg<D>;
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t base = (raw + 1023u) & ~1023u;
+    uint8_t *sb = smem_raw + (base - raw);
+    const uint32_t bar0 = base + C::OFF_BAR;
+#define BAR(i) (bar0 + 8u * (uint32_t)(i))
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sb + C::OFF_BAR + 192);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(sb + C::OFF_BAR + 196);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    uint32_t *items_s = reinterpret_cast<uint32_t *>(sb + C::OFF_ITEMS);
+    int n_local = -1;
+    {
+        int beg = 0, n_mine;
+        if (p.use_list) {
+            beg = (int)__ldg(p.sched + blockIdx.x);
+            n_mine = (int)__ldg(p.sched + blockIdx.x + 1) - beg;
+        } else {
+            n_mine = (p.n_items - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
+        }
+        if (p.packable && n_mine <= kLocalItems) {
+            n_local = n_mine;
+            for (int i = threadIdx.x; i < n_mine; i += blockDim.x)
+                items_s[i] = pack_item(p, p.use_list ? (int)__ldg(p.sched + kMaxCtas + 1 + beg + i)
+                                                     : (int)blockIdx.x + i * (int)gridDim.x);
+        }
+    }
+    if (threadIdx.x == 0) {
+        mbar_init(BAR(B_QF), 1);
+        mbar_init(BAR(B_QS), 128);
+        mbar_init(BAR(B_QE), 1);
+        for (int i = 0; i < 2; i++) {
+            mbar_init(BAR(B_KVF + i), 1);
+            mbar_init(BAR(B_KVS + i), 128);
+            mbar_init(BAR(B_KVE + i), 2);
+            mbar_init(BAR(B_SF + i), 1);
+            mbar_init(BAR(B_BF + i), 1);
+        }
+        mbar_init(BAR(B_PF), 128);
+        mbar_init(BAR(B_OD), 1);
+        mbar_init(BAR(B_SPL), 128);
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 0) {
+        tmem_alloc(smem_u32(tmem_slot), C::TM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    auto wait_w = [&](int b, int parity, int code) -> bool {       // warp-wide bounded wait
+        return __all_sync(0xffffffffu, mbar_wait(BAR(b), parity & 1, abort_flag, p.err, code));
+    };
+
+    // registers: see Cfg (each setmaxnreg inside its role's branch)
+    if (warp < 8) {
+        if (warp < 4) regs_dec<40>();
+        if (warp == 0) {
+            // -------------------------------------------------------- producer
+            const bool leader = elect_one();
+            if (leader) {
+                prefetch_tmap(&tq);
+                prefetch_tmap(&tk);
+                prefetch_tmap(&tv);
+            }
+            int t = 0;                                       // key tiles issued
+            bool ok = true;
+            for (int k = 0; ok; k++) {
+                Item it;
+                if (!next_item(p, items_s, n_local, k, it)) break;
+                if (k > 0 && !(ok = wait_w(B_QE, k - 1, 0x401))) break;
+                if (leader) {
+                    mbar_arrive_expect_tx(BAR(B_QF), C::QB);
+#pragma unroll
+                    for (int c = 0; c < C::CH; c++)
+                        tma_load_3d(base + C::OFF_QH + c * (BM * 128), &tq, BAR(B_QF), it.h * D + 32 * c, it.q0, it.b);
+                }
+                __syncwarp();
+                for (int j = 0; j < it.n_kv; j++, t++) {
+                    const int st = t & 1;
+                    if (t >= 2 && !(ok = wait_w(B_KVE + st, (t >> 1) - 1, 0x402))) break;
+                    if (leader) {
+                        const uint32_t sbase = base + C::OFF_ST + st * C::STAGE;
+                        mbar_arrive_expect_tx(BAR(B_KVF + st), 2 * C::KB);
+#pragma unroll
+                        for (int c = 0; c < C::CH; c++) {
+                            tma_load_3d(sbase + c * (BN * 128), &tk, BAR(B_KVF + st), it.h * D + 32 * c, j * BN, it.b);
+                            tma_load_3d(sbase + 2 * C::KB + c * (BN * 128), &tv, BAR(B_KVF + st), it.h * D + 32 * c,
+                                        j * BN, it.b);
+                        }
+                    }
+                    __syncwarp();
+                }
+            }
+        } else if (warp == 1) {
+            // -------------------------------------------------------- S issuer
+            const bool leader = elect_one();
+            constexpr uint32_t idS = idesc_tf32(BM, BN, 0, 0);     // Q, K both K-major
+            int t = 0;
+            bool ok = true;
+            for (int k = 0; ok; k++) {
+                Item it;
+                if (!next_item(p, items_s, n_local, k, it)) break;
+                if (!(ok = wait_w(B_QS, k, 0x411))) break;
+                for (int j = 0; j < it.n_kv; j++, t++) {
+                    const int st = t & 1, sbuf = t & 1;
+                    if (!(ok = wait_w(B_KVS + st, t >> 1, 0x412))) break;
+                    if (t >= 2 && !(ok = wait_w(B_BF + sbuf, (t >> 1) - 1, 0x413))) break;
+                    tc_fence_after();
+                    const uint32_t kh = base + C::OFF_ST + st * C::STAGE, kl = kh + C::KB;
+                    const uint32_t d_t = tmem + C::TM_S + 64 * sbuf;
+                    if (leader) {
+                        // K-step kk: chunk kk/4 (128-byte columns), +32 bytes within it
+#pragma unroll
+                        for (int part = 0; part < 3; part++) {       // hh, hl, lh
+                            const uint32_t qa = base + (part == 2 ? C::OFF_QL : C::OFF_QH);
+                            const uint32_t kb = part == 1 ? kl : kh;
+#pragma unroll
+                            for (int kk = 0; kk < D / 8; kk++) {
+                                const uint64_t ad = sw128_desc(qa + (kk >> 2) * (BM * 128) + (kk & 3) * 32, 16, 1024);
+                                const uint64_t bd = sw128_desc(kb + (kk >> 2) * (BN * 128) + (kk & 3) * 32, 16, 1024);
+                                mma_tf32_ss(d_t, ad, bd, idS, (part > 0 || kk > 0));
+                            }
+                        }
+                        mma_commit(BAR(B_SF + sbuf));
+                        mma_commit(BAR(B_KVE + st));              // (this stage's K part)
+                        if (j == it.n_kv - 1) mma_commit(BAR(B_QE));
+                    }
+                    __syncwarp();
+                }
+            }
+        } else if (warp == 2) {
+            // -------------------------------------------------------- PV issuer
+            const bool leader = elect_one();
+            constexpr uint32_t idO = idesc_tf32(BM, D, 0, 0);      // P from TMEM, V^T K-major
+            int t = 0;
+            bool ok = true;
+            for (int k = 0; ok; k++) {
+                Item it;
+                if (!next_item(p, items_s, n_local, k, it)) break;
+                for (int j = 0; j < it.n_kv; j++, t++) {
+                    const int st = t & 1, sbuf = t & 1;
+                    if (!(ok = wait_w(B_KVS + st, t >> 1, 0x421))) break;
+                    if (!(ok = wait_w(B_PF, t, 0x422))) break;
+                    tc_fence_after();
+                    const uint32_t vl = base + C::OFF_ST + st * C::STAGE + 2 * C::KB, vh = vl + C::KB;
+                    const uint32_t ph = tmem + C::TM_S + 64 * sbuf, pl = tmem + C::TM_PL;
+                    if (leader) {
+                        // V^T tile [D rows][64 keys] K-major: key chunk kk/4 (32 keys, D*128
+                        // bytes apart), +32 bytes per 8-key step within it
+#pragma unroll
+                        for (int part = 0; part < 3; part++) {       // hh, hl, lh
+                            const uint32_t pa = part == 2 ? pl : ph;
+                            const uint32_t vb = part == 1 ? vl : vh;
+#pragma unroll
+                            for (int kk = 0; kk < BN / 8; kk++) {
+                                const uint64_t bd = sw128_desc(vb + (kk >> 2) * (D * 128) + (kk & 3) * 32, 16, 1024);
+                                mma_tf32_ts(tmem + C::TM_O, pa + 8 * kk, bd, idO, (j > 0 || part > 0 || kk > 0));
+                            }
+                        }
+                        mma_commit(BAR(B_OD));
+                        mma_commit(BAR(B_BF + sbuf));
+                        mma_commit(BAR(B_KVE + st));              // (this stage's V part)
+                    }
+                    __syncwarp();
+                }
+            }
+        } else if (warp >= 4) {
+            // -------------------------------------------------------- splitters
+            regs_dec<C::REG_SPLIT>();
+            const int tid = threadIdx.x - 128;
+            float *qh = reinterpret_cast<float *>(sb + C::OFF_QH), *ql = reinterpret_cast<float *>(sb + C::OFF_QL);
+            int t = 0;
+            bool ok = true;
+            for (int k = 0; ok; k++) {
+                Item it;
+                if (!next_item(p, items_s, n_local, k, it)) break;
+                if (!(ok = wait_w(B_QF, k, 0x431))) break;
+                split_hi_lo(qh, ql, BM * D, tid, 128);
+                fence_async_smem();
+                mbar_arrive(BAR(B_QS));
+                for (int j = 0; j < it.n_kv; j++, t++) {
+                    const int st = t & 1;
+                    if (!(ok = wait_w(B_KVF + st, t >> 1, 0x432))) break;
+                    uint8_t *s0 = sb + C::OFF_ST + st * C::STAGE;
+                    split_hi_lo(reinterpret_cast<float *>(s0), reinterpret_cast<float *>(s0 + C::KB), BN * D, tid,
+                                128);                                                     // K
+                    // V: raw tile (TMA, 128-byte swizzle, [64 keys][32-dim chunks]) ->
+                    // V^T high and low parts ([D rows][32-key chunks], same swizzle).
+                    // All raw values are read before the low part overwrites them.
+                    constexpr int PER = BN * D / 128;
+                    float vr[PER];
+                    uint8_t *vraw = s0 + 2 * C::KB;
+#pragma unroll
+                    for (int i = 0; i < PER; i++) {
+                        const int idx = tid + 128 * i, key = idx / D, dim = idx % D;
+                        vr[i] = *reinterpret_cast<const float *>(
+                            vraw + (dim >> 5) * (BN * 128) + key * 128 + ((((dim & 31) >> 2) ^ (key & 7)) << 4) +
+                            (dim & 3) * 4);
+                    }
+                    mbar_arrive(BAR(B_SPL));
+                    if (!(ok = wait_w(B_SPL, t, 0x433))) break;
+#pragma unroll
+                    for (int i = 0; i < PER; i++) {
+                        const int idx = tid + 128 * i, key = idx / D, dim = idx % D;
+                        const int off = (key >> 5) * (D * 128) + dim * 128 + ((((key & 31) >> 2) ^ (dim & 7)) << 4) +
+                                        (key & 3) * 4;
+                        const float h = __uint_as_float(__float_as_uint(vr[i]) & 0xFFFFE000u);
+                        *reinterpret_cast<float *>(s0 + 3 * C::KB + off) = h;           // V^T high
+                        *reinterpret_cast<float *>(vraw + off) = vr[i] - h;             // V^T low
+                    }
+                    fence_async_smem();
+                    mbar_arrive(BAR(B_KVS + st));
+                }
+            }
+        }
+    } else {
+        // ------------------------------------------------------------ softmax
+        if (C::CTAS == 2) regs_inc<C::REG_SOFT>();   // (one CTA per SM: the launch allocation suffices)
+        const int quad = warp & 3;
+        const int row = quad * 32 + lane;
+        const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
+        const uint32_t tPL = tmem + lane_base + C::TM_PL, tO = tmem + lane_base + C::TM_O;
+        int t = 0;
+        bool ok = true;
+        for (int k = 0; ok; k++) {
+            Item it;
+            if (!next_item(p, items_s, n_local, k, it)) break;
+            const int qrow = it.q0 + row;
+            float m_run = -INFINITY, l_run = 0.f;
+            for (int j = 0; j < it.n_kv; j++, t++) {
+                const int sbuf = t & 1;
+                const uint32_t tS = tmem + lane_base + C::TM_S + 64 * sbuf;
+                ok = mbar_wait(BAR(B_SF + sbuf), (t >> 1) & 1, abort_flag, p.err, 0x441);
+                if (!(ok = __all_sync(0xffffffffu, ok))) break;
+                tc_fence_after();
+                float s[64];
+                {
+                    uint32_t t0[32], t1[32];
+                    tmem_ld32(tS, t0);
+                    tmem_ld32(tS + 32, t1);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int c = 0; c < 32; c++) {
+                        s[c] = __uint_as_float(t0[c]);
+                        s[32 + c] = __uint_as_float(t1[c]);
+                    }
+                }
+                const int key0 = j * BN;
+                if (key0 + BN - 1 > it.q0 || key0 + BN > p.T) {   // tiles touching the diagonal or T
+#pragma unroll
+                    for (int c = 0; c < 64; c++)
+                        if (key0 + c > qrow || key0 + c >= p.T) s[c] = -INFINITY;
+                }
+                float mx = -INFINITY;
+#pragma unroll
+                for (int c = 0; c < 64; c += 2) mx = max3(mx, s[c], s[c + 1]);
+                mx *= p.scale_log2;
+                float alpha = 1.f;
+                const bool grow = mx > m_run + 8.f;               // also true on the first tile
+                if (grow) {
+                    alpha = ex2(m_run - mx);
+                    m_run = mx;
+                    l_run *= alpha;
+                }
+#pragma unroll
+                for (int c = 0; c < 64; c++) {
+                    s[c] = ex2(fmaf(s[c], p.scale_log2, -m_run));
+                    l_run += s[c];
+                }
+                // the previous PV has read Pl and finished with O
+                if (t > 0) ok = mbar_wait(BAR(B_OD), (t - 1) & 1, abort_flag, p.err, 0x442);
+                if (!(ok = __all_sync(0xffffffffu, ok))) break;
+                tc_fence_after();
+#pragma unroll
+                for (int h2 = 0; h2 < 2; h2++) {
+                    uint32_t hi[32], lo[32];
+#pragma unroll
+                    for (int c = 0; c < 32; c++) {
+                        const float x = s[32 * h2 + c];
+                        const float xh = __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
+                        hi[c] = __float_as_uint(xh);
+                        lo[c] = __float_as_uint(x - xh);
+                    }
+                    tmem_st32(tS + 32 * h2, hi);
+                    tmem_st32(tPL + 32 * h2, lo);
+                }
+                if (__any_sync(0xffffffffu, j > 0 && grow)) {
+                    uint32_t o[32];
+#pragma unroll
+                    for (int c0 = 0; c0 < D; c0 += 32) {
+                        tmem_ld32(tO + c0, o);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int c = 0; c < 32; c++) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
+                        tmem_st32(tO + c0, o);
+                    }
+                }
+                tmem_wait_st();
+                tc_fence_before();
+                mbar_arrive(BAR(B_PF));
+            }
+            if (!ok) break;
+            // epilogue: O / l of this item (the next item's first PV waits for
+            // this warpgroup's next P, written after these loads completed)
+            ok = mbar_wait(BAR(B_OD), (t - 1) & 1, abort_flag, p.err, 0x443);
+            if (!(ok = __all_sync(0xffffffffu, ok))) break;
+            tc_fence_after();
+            float o[D];
+#pragma unroll
+            for (int c0 = 0; c0 < D; c0 += 32) {
+                uint32_t tt[32];
+                tmem_ld32(tO + c0, tt);
+#pragma unroll
+                for (int c = 0; c < 32; c++) o[c0 + c] = __uint_as_float(tt[c]);
+            }
+            tmem_wait_ld();
+            tc_fence_before();
+            if (qrow < p.T) {
+                const float inv = 1.f / l_run;
+                float *dst = p.o + ((long long)it.b * p.T + qrow) * p.out_stride + (long long)it.h * D;
+#pragma unroll
+                for (int c = 0; c < D; c += 4)
+                    *reinterpret_cast<float4 *>(dst + c) = make_float4(o[c] * inv, o[c + 1] * inv, o[c + 2] * inv,
+                                                                       o[c + 3] * inv);
+                if (p.lse) p.lse[((long long)it.b * p.H + it.h) * p.T + qrow] = (m_run + __log2f(l_run)) * kLn2;
+            }
+        }
+    }
+
+    // ---------------------------------------------------------------- teardown
+    tc_fence_before();
+    __syncthreads();
+    if (*abort_flag) {
+        for (int i = 0; i < 1000; i++) __nanosleep(1000);
+    }
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem, C::TM_COLS);
+    }
+#undef BAR
+}
+
+}  // namespace ftf
+}  // namespace attn
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+namespace attn_host {
+
+bool ensure_smem_attr(const void *func, size_t bytes);
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn_t() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        void *ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    }
+    return fn;
+}
+
+// 3-D view {columns, T, B} of a (B*T, stride) fp32 activation; 32 x rows boxes
+// (128 bytes wide) with the 128-byte swizzle the MMA descriptors expect.
+static bool cached_map_f32(CUtensorMap *m, const void *ptr, int cols, int T, int B, long long stride, int rows) {
+    struct Entry { const void *ptr; int cols, T, B, rows; long long stride; CUtensorMap map; };
+    static thread_local Entry cache[12];
+    static thread_local int next = 0;
+    for (auto &e : cache)
+        if (e.ptr == ptr && e.cols == cols && e.T == T && e.B == B && e.rows == rows && e.stride == stride) {
+            *m = e.map;
+            return true;
+        }
+    auto fn = encode_fn_t();
+    if (!fn) return false;
+    cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)T, (cuuint64_t)B};
+    cuuint64_t strides[2] = {(cuuint64_t)stride * 4, (cuuint64_t)stride * 4 * T};
+    cuuint32_t box[3] = {32, (cuuint32_t)rows, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    if (fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<void *>(ptr), dims, strides, box, estr,
+           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return false;
+    cache[next] = Entry{ptr, cols, T, B, rows, stride, *m};
+    next = (next + 1) % 12;
+    return true;
+}
+
+bool fwd_tf32_sm100_supported(int D, long long in_stride, long long out_stride) {
+    return (D == 32 || D == 64) && in_stride % 4 == 0 && out_stride % 4 == 0 && encode_fn_t() != nullptr;
+}
+
+static void lpt_schedule_tf32(const attn::ftf::Params &p, int ctas, std::vector<unsigned short> &out) {
+    using namespace attn::ftf;
+    std::vector<std::vector<unsigned short>> lists(ctas);
+    std::priority_queue<std::pair<long long, int>, std::vector<std::pair<long long, int>>, std::greater<>> heap;
+    for (int c = 0; c < ctas; c++) heap.push({0, c});
+    const int hb = p.H * p.B;
+    for (int i = 0; i < p.n_items; i++) {
+        const int qt = p.n_qt - 1 - i / hb;
+        const long long cost = 2LL * (qt + 1) + 2;      // key tiles + per-item overhead
+        auto [load, c] = heap.top();
+        heap.pop();
+        lists[c].push_back((unsigned short)i);
+        heap.push({load + cost, c});
+    }
+    out.assign(kMaxCtas + 1 + p.n_items, 0);
+    int off = 0;
+    for (int c = 0; c < ctas; c++) {
+        out[c] = (unsigned short)off;
+        for (unsigned short v : lists[c]) out[kMaxCtas + 1 + off++] = v;
+    }
+    for (int c = ctas; c <= kMaxCtas; c++) out[c] = (unsigned short)off;
+}
+
+template <int D>
+static int launch_tf32_t(const void *q, const void *k, const void *v, void *o, float *lse, long long in_stride,
+                         long long out_stride, int B, int H, int T, int *err, cudaStream_t s) {
+    using namespace attn::ftf;
+    using Cg = Cfg<D>;
+    CUtensorMap mq, mk, mv;
+    if (!cached_map_f32(&mq, q, H * D, T, B, in_stride, BM) || !cached_map_f32(&mk, k, H * D, T, B, in_stride, BN) ||
+        !cached_map_f32(&mv, v, H * D, T, B, in_stride, BN))
+        return set_error(ATTN_ERR_CUDA, "3xTF32 forward: cuTensorMapEncodeTiled failed");
+    int dev = 0;
+    cudaGetDevice(&dev);
+    static int sm_count[128] = {0};
+    if (dev < 0 || dev >= 128) return set_error(ATTN_ERR_INVALID, "3xTF32 forward: device %d", dev);
+    if (!sm_count[dev]) {
+        int sms = 148;
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        sm_count[dev] = sms;
+    }
+    Params p;
+    p.o = static_cast<float *>(o);
+    p.lse = lse;
+    p.out_stride = out_stride;
+    p.T = T;
+    p.H = H;
+    p.B = B;
+    p.n_qt = (T + BM - 1) / BM;
+    p.n_items = p.n_qt * H * B;
+    p.scale_log2 = attn::kLog2e / sqrtf((float)D);
+    p.err = err;
+    const int ctas = std::max(1, std::min(std::min(Cg::CTAS * sm_count[dev], kMaxCtas), p.n_items));
+    p.use_list = p.n_items <= kMaxItems;
+    p.packable = B < 4096 && H < 1024 && p.n_qt < 1024;
+    p.sched = nullptr;
+    if (p.use_list) {
+        static unsigned short *sched_buf[128][2] = {{nullptr}};
+        static long long sched_key[128][2];
+        const int slot = D == 64;
+        const long long key = (((long long)T * 4096 + H) * 65536 + B) * 512 + ctas;
+        if (!sched_buf[dev][slot]) {
+            if (cudaMalloc(&sched_buf[dev][slot], (kMaxCtas + 1 + kMaxItems) * sizeof(unsigned short)) != cudaSuccess)
+                return set_error(ATTN_ERR_NOMEM, "3xTF32 forward: cannot allocate the schedule buffer");
+            sched_key[dev][slot] = -1;
+        }
+        if (key != sched_key[dev][slot]) {
+            std::vector<unsigned short> h;
+            lpt_schedule_tf32(p, ctas, h);
+            if (cudaMemcpyAsync(sched_buf[dev][slot], h.data(), h.size() * sizeof(unsigned short),
+                                cudaMemcpyHostToDevice, s) != cudaSuccess ||
+                cudaStreamSynchronize(s) != cudaSuccess)
+                return set_error(ATTN_ERR_CUDA, "3xTF32 forward: schedule upload failed");
+            sched_key[dev][slot] = key;
+        }
+        p.sched = sched_buf[dev][slot];
+    }
+    const size_t smem = Cg::SMEM;
+    if (!ensure_smem_attr((const void *)fwd_tf32_kernel<D>, smem))
+        return set_error(ATTN_ERR_CUDA, "3xTF32 forward: cannot set shared-memory size");
+    static bool carveout_set[128][2] = {{false}};
+    if (!carveout_set[dev][D == 64]) {
+        if (cudaFuncSetAttribute((const void *)fwd_tf32_kernel<D>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                 100) != cudaSuccess)
+            return set_error(ATTN_ERR_CUDA, "3xTF32 forward: cannot set the shared-memory carveout");
+        carveout_set[dev][D == 64] = true;
+    }
+    fwd_tf32_kernel<D><<<ctas, kThreads, smem, s>>>(mq, mk, mv, p);
+    return check_launch("3xTF32 forward kernel");
+}
+
+int launch_fwd_tf32_sm100(int D, const void *q, const void *k, const void *v, void *o, float *lse,
+                          long long in_stride, long long out_stride, int B, int H, int T, int *err,
+                          cudaStream_t s) {
+    if (((uintptr_t)q | (uintptr_t)k | (uintptr_t)v | (uintptr_t)o) & 15)
+        return set_error(ATTN_ERR_INVALID, "3xTF32 forward: tensors must be 16-byte aligned");
+    switch (D) {
+        case 32: return launch_tf32_t<32>(q, k, v, o, lse, in_stride, out_stride, B, H, T, err, s);
+        case 64: return launch_tf32_t<64>(q, k, v, o, lse, in_stride, out_stride, B, H, T, err, s);
+        default: return set_error(ATTN_ERR_UNSUPPORTED, "3xTF32 forward: head_dim %d", D);
+    }
+}
+
+}  // namespace attn_host
