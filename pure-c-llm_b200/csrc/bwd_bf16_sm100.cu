@@ -28,6 +28,7 @@
 #include "sm100.cuh"
 
 #include <cudaTypedefs.h>
+#include <type_traits>
 
 namespace attn {
 namespace fab {
@@ -236,20 +237,21 @@ bwd_kernel(const __grid_constant__ CUtensorMap m_a, const __grid_constant__ CUte
         const uint32_t lb = (uint32_t)(quad * 32) << 16;
         const long long bh = ((long long)b * p.H + h) * p.T;
         const int grow_ = fixed * BT + row;          // global row index of this thread
-        float my_lse2 = 0.f, my_d = 0.f;             // dq: this query row's statistics
+        float my_nl2 = 0.f, my_ndd = 0.f;            // dq: this query row's -lse2 and -D / sqrt(d)
         if (KIND == 1 && grow_ < p.T) {
-            my_lse2 = __ldg(p.lse2 + bh + grow_);
-            my_d = __ldg(p.dvec + bh + grow_);
+            my_nl2 = -__ldg(p.lse2 + bh + grow_);
+            my_ndd = -__ldg(p.dvec + bh + grow_) * p.ds_scale;
         }
+        const uint64_t scale2 = f2(p.scale_log2, p.scale_log2), ds2 = f2(p.ds_scale, p.ds_scale);
         bool ok = true;
         for (int it = 0; it < count; it++) {
             const int tcol = first + it;             // streamed tile index
             float *st_l = stats + (it % kStages) * 2 * BT;   // dkdv: lse2 / D of the query columns
             if (KIND == 0) {
-                if (half == 0) {
+                if (half == 0) {                     // staged as -lse2 and -D / sqrt(d)
                     const int q = tcol * BT + row;
-                    st_l[row] = q < p.T ? __ldg(p.lse2 + bh + q) : 0.f;
-                    st_l[BT + row] = q < p.T ? __ldg(p.dvec + bh + q) : 0.f;
+                    st_l[row] = q < p.T ? -__ldg(p.lse2 + bh + q) : 0.f;
+                    st_l[BT + row] = q < p.T ? -__ldg(p.dvec + bh + q) * p.ds_scale : 0.f;
                 }
                 // the statistics are in shared memory before anyone reads them (an
                 // mbarrier with a bounded wait, so a warp that gave up on an earlier
@@ -281,48 +283,59 @@ bwd_kernel(const __grid_constant__ CUtensorMap m_a, const __grid_constant__ CUte
             tmem_wait_ld();
             tc_fence_before();
             mbar_arrive(BAR(B_XYE));                 // X and Y read: the next products may start
+            // P = 2^(S scale - lse2), dS = P (dP - D) / sqrt(d), pairwise on f32x2;
+            // the mask (diagonal tile, or key/query columns past T) only where needed
+            const bool need_mask = diag || (KIND == 0 && tcol * BT + BT > p.T);
+            auto tile = [&](auto masked_tag) {
+                constexpr bool MASKED = decltype(masked_tag)::value;
 #pragma unroll
-            for (int q2 = 0; q2 < 2; q2++) {
-                uint32_t wp[16], wd[16];
+                for (int q2 = 0; q2 < 2; q2++) {
+                    uint32_t wp[16], wd[16];
 #pragma unroll
-                for (int c = 0; c < 32; c += 2) {
-                    const int cc = 32 * q2 + c;          // column within this half
-                    float xa[2], l2[2], dd[2];
-                    bool masked[2];
-#pragma unroll
-                    for (int u = 0; u < 2; u++) {
-                        const int col = 64 * half + cc + u;
-                        if (KIND == 0) {             // row = key, col = query
-                            l2[u] = st_l[col];
-                            dd[u] = st_l[BT + col];
-                            masked[u] = (diag && col < row) || (tcol * BT + col >= p.T);
-                        } else {                     // row = query, col = key
-                            l2[u] = my_lse2;
-                            dd[u] = my_d;
-                            masked[u] = diag && col > row;
+                    for (int c = 0; c < 32; c += 2) {
+                        const int cc = 32 * q2 + c;      // column within this half
+                        const int col = 64 * half + cc;
+                        uint64_t nl2, ndd;
+                        if (KIND == 0) {                 // row = key, col = query
+                            nl2 = *reinterpret_cast<const uint64_t *>(st_l + col);
+                            ndd = *reinterpret_cast<const uint64_t *>(st_l + BT + col);
+                        } else {                         // row = query, col = key
+                            nl2 = f2(my_nl2, my_nl2);
+                            ndd = f2(my_ndd, my_ndd);
                         }
-                        xa[u] = fmaf(__uint_as_float(xs[cc + u]), p.scale_log2, -l2[u]);
-                    }
-                    // kPolyPairs of every 8 pairs on the FMA pipe, the rest on MUFU
-                    float pv[2];
-                    if (((cc >> 1) & 7) < kPolyPairs) {
-                        f2_split(exp2_poly2(f2(xa[0], xa[1])), pv[0], pv[1]);
-                    } else {
-                        pv[0] = ex2(xa[0]);
-                        pv[1] = ex2(xa[1]);
-                    }
-                    float dv[2];
+                        const uint64_t xa2 = fma2(f2(__uint_as_float(xs[cc]), __uint_as_float(xs[cc + 1])), scale2, nl2);
+                        // kPolyPairs of every 8 pairs on the FMA pipe, the rest on MUFU
+                        float pv[2];
+                        if (((cc >> 1) & 7) < kPolyPairs) {
+                            f2_split(exp2_poly2(xa2), pv[0], pv[1]);
+                        } else {
+                            float a0, a1;
+                            f2_split(xa2, a0, a1);
+                            pv[0] = ex2(a0);
+                            pv[1] = ex2(a1);
+                        }
+                        if (MASKED) {
 #pragma unroll
-                    for (int u = 0; u < 2; u++) {
-                        if (masked[u]) pv[u] = 0.f;
-                        dv[u] = pv[u] * (__uint_as_float(ys[cc + u]) - dd[u]) * p.ds_scale;
+                            for (int u = 0; u < 2; u++) {
+                                const int cu = col + u;
+                                const bool m = KIND == 0 ? ((diag && cu < row) || (tcol * BT + cu >= p.T))
+                                                         : (diag && cu > row);
+                                if (m) pv[u] = 0.f;
+                            }
+                        }
+                        const uint64_t pv2 = f2(pv[0], pv[1]);
+                        const uint64_t t2 = fma2(f2(__uint_as_float(ys[cc]), __uint_as_float(ys[cc + 1])), ds2, ndd);
+                        float d0, d1;
+                        f2_split(fma2(pv2, t2, 0ull), d0, d1);
+                        wp[c / 2] = pack_bf16(pv[0], pv[1]);
+                        wd[c / 2] = pack_bf16(d0, d1);
                     }
-                    wp[c / 2] = pack_bf16(pv[0], pv[1]);
-                    wd[c / 2] = pack_bf16(dv[0], dv[1]);
+                    if (KIND == 0) tmem_st16(tmem + lb + TM_W1 + 32 * half + 16 * q2, wp);
+                    tmem_st16(tmem + lb + TM_W2 + 32 * half + 16 * q2, wd);
                 }
-                if (KIND == 0) tmem_st16(tmem + lb + TM_W1 + 32 * half + 16 * q2, wp);
-                tmem_st16(tmem + lb + TM_W2 + 32 * half + 16 * q2, wd);
-            }
+            };
+            if (need_mask) tile(std::true_type{});
+            else tile(std::false_type{});
             tmem_wait_st();
             tc_fence_before();
             mbar_arrive(BAR(B_W));

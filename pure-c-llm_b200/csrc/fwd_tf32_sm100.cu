@@ -89,6 +89,8 @@ enum {
 struct Params {
     float *o;
     float *lse;
+    const float *v;                // V itself, for the first query row (see the epilogue)
+    long long in_stride;
     long long out_stride;
     int T, H, B, n_qt, n_items;
     float scale_log2;              // log2(e) / sqrt(d)
@@ -490,8 +492,18 @@ fwd_tf32_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
             tmem_wait_ld();
             tc_fence_before();
             if (qrow < p.T) {
-                const float inv = 1.f / l_run;
+                float inv = 1.f / l_run;
                 float *dst = p.o + ((long long)it.b * p.T + qrow) * p.out_stride + (long long)it.h * D;
+                if (qrow == 0) {
+                    // The first query row attends to key 0 alone: its output is V_0
+                    // exactly (the products would leave a 2^-22 relative error, and a
+                    // backward pass turns O_0 - V_0 into a nonzero gradient where the
+                    // exact one is zero).
+                    const float *src = p.v + (long long)it.b * p.T * p.in_stride + (long long)it.h * D;
+#pragma unroll
+                    for (int c = 0; c < D; c++) o[c] = src[c];
+                    inv = 1.f;
+                }
 #pragma unroll
                 for (int c = 0; c < D; c += 4)
                     *reinterpret_cast<float4 *>(dst + c) = make_float4(o[c] * inv, o[c + 1] * inv, o[c + 2] * inv,
@@ -610,6 +622,8 @@ static int launch_tf32_t(const void *q, const void *k, const void *v, void *o, f
     Params p;
     p.o = static_cast<float *>(o);
     p.lse = lse;
+    p.v = static_cast<const float *>(v);
+    p.in_stride = in_stride;
     p.out_stride = out_stride;
     p.T = T;
     p.H = H;
