@@ -39,7 +39,10 @@ constexpr int BT = 128;           // rows per tile (TMEM lanes) and columns per 
 constexpr int D = 64;             // head_dim covered by these kernels
 constexpr int kStages = 3;
 constexpr int kThreads = 384;
-constexpr int kPolyPairs = 3;     // exponential pairs (of 8) computed by exp2_poly2 on the FMA pipe
+#ifndef ATTN_BWD_POLY_PAIRS
+#define ATTN_BWD_POLY_PAIRS 3
+#endif
+constexpr int kPolyPairs = ATTN_BWD_POLY_PAIRS;   // exponential pairs (of 8) computed by exp2_poly2 on the FMA pipe
 constexpr int TILE_BYTES = BT * D * 2;        // one 128 x 64 bf16 tile (16 KB)
 
 // TMEM columns (both kernels): X = S or S^T, Y = dP or dP^T (fp32, 128 each),
