@@ -61,7 +61,7 @@ L2_BYTES = 126 * 2 ** 20
 # dram__bytes_read.sum + dram__bytes_write.sum per launch of the dominant
 # kernel, each from one ncu capture of that kernel at the config's size;
 # None where not captured
-TRAFFIC = {"c3-bf16": 51817984, "c4-f32": 2153309904, "c4-int8": 577940736, "c2": 52688896}
+TRAFFIC = {"c3-bf16": 51817984, "c4-f32": 2153309904, "c4-int8": 577940736, "c2": 51463168}
 
 
 def causal_flops(B, H, T, d):
