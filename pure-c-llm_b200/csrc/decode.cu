@@ -550,6 +550,8 @@ int rows_chunk(int max_len, int n_seq) {
 
 size_t decode_stream_ws_bytes(int n_seq, int heads, int head_dim, int max_len);
 bool decode_stream_shape_ok(int heads, int head_dim, int kv_dtype);
+size_t decode_i8mma_ws_bytes(int n_seq, int heads, int head_dim, int max_len);
+bool decode_i8mma_shape_ok(int heads, int head_dim, int kv_dtype);
 
 static size_t decode_split_ws_bytes(int n_seq, int heads, int head_dim, int max_len, int kv_dtype) {
     if (rows_i8_ok(heads, head_dim, kv_dtype)) {
@@ -573,12 +575,15 @@ static size_t decode_split_ws_bytes(int n_seq, int heads, int head_dim, int max_
     return (b + 255) / 256 * 256;
 }
 
-// Covers whichever kernel the call's pointers select: the streaming kernel
-// (shape and alignment permitting) or the split kernels.
+// Covers whichever kernel the call's pointers select: the tensor-core INT8
+// kernel or the streaming kernel (shape and alignment permitting), or the
+// split kernels.
 size_t decode_workspace_bytes(int n_seq, int heads, int head_dim, int max_len, int kv_dtype) {
     size_t b = decode_split_ws_bytes(n_seq, heads, head_dim, max_len, kv_dtype);
     if (decode_stream_shape_ok(heads, head_dim, kv_dtype))
         b = std::max(b, decode_stream_ws_bytes(n_seq, heads, head_dim, max_len));
+    if (decode_i8mma_shape_ok(heads, head_dim, kv_dtype))
+        b = std::max(b, decode_i8mma_ws_bytes(n_seq, heads, head_dim, max_len));
     return b;
 }
 
@@ -668,9 +673,12 @@ bool decode_stream_ok(const DecodeLaunch &L);
 bool decode_stream_shape_ok(int heads, int head_dim, int kv_dtype);
 size_t decode_stream_ws_bytes(int n_seq, int heads, int head_dim, int max_len);
 int launch_decode_stream(const DecodeLaunch &L);
+bool decode_i8mma_ok(const DecodeLaunch &L);
+int launch_decode_i8mma(const DecodeLaunch &L);
 
 int launch_decode(const DecodeLaunch &L) {
     const bool i8 = L.kv_dtype == ATTN_I8;
+    if (decode_i8mma_ok(L)) return launch_decode_i8mma(L);
     if (decode_stream_ok(L)) return launch_decode_stream(L);
     if (rows_i8_ok(L.heads, L.head_dim, L.kv_dtype)) return launch_rows_i8(L);
     switch (L.head_dim) {

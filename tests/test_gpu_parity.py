@@ -399,9 +399,10 @@ def test_gather_permute(A):
 # ---------------------------------------------------------------------------
 # INT8 streaming decode kernel (1024-code rows): the paths its producer takes
 # ---------------------------------------------------------------------------
-def _int8_decode_case(A, H, d, lens, cap, row_pad=0, seed=90):
+def _int8_decode_case(A, H, d, lens, cap, row_pad=0, seed=90, mutate=None):
     """Quantised caches (optionally with padded rows), decode, and the oracle
-    over the dequantised cache; returns (out, refs)."""
+    over the dequantised cache; returns (out, refs).  `mutate(q, kscale,
+    vscale)` may edit the query (numpy) and the scales (device) in place first."""
     import torch
     n_seq = len(lens)
     width = H * d
@@ -410,6 +411,8 @@ def _int8_decode_case(A, H, d, lens, cap, row_pad=0, seed=90):
     q = synth.normal(seed + 2, (n_seq, width))
     kq, ksc = A.quantize_int8_t(dev(kc), H)
     vq, vsc = A.quantize_int8_t(dev(vc), H)
+    if mutate:
+        mutate(q, ksc, vsc)
     if row_pad:
         # the same codes in rows of width + row_pad bytes (strided slabs)
         kp = torch.zeros((n_seq * cap, width + row_pad), dtype=torch.int8, device="cuda")
@@ -436,6 +439,25 @@ def test_int8_stream_piece_boundaries(A, H, d):
     cap = 2100
     lens = [1, 2, 15, 16, 17, 64, 65, 511, 512, 513, 1024, 1500, 2099, cap]
     out, refs = _int8_decode_case(A, H, d, lens, cap)
+    for s, ref in enumerate(refs):
+        assert rel_err(out[s], ref) < F32_TOL, (s, lens[s])
+
+
+@pytest.mark.parametrize("H,d", [(16, 64), (8, 128)])
+def test_int8_decode_signed_scales_and_zero_query(A, H, d):
+    """Scales of either sign (the dequantised value is code * scale whatever
+    its sign), a zero query row and a zero value scale, at lengths on and
+    around the 128-row tile and the 512-row piece."""
+    lens = [1, 127, 128, 129, 383, 384, 385, 511, 512, 513, 1030]
+    cap = 1040
+
+    def mutate(q, ksc, vsc):
+        ksc[::3] *= -1
+        vsc[::5] *= -1
+        vsc[7] = 0.0
+        q[3] = 0.0
+
+    out, refs = _int8_decode_case(A, H, d, lens, cap, seed=150, mutate=mutate)
     for s, ref in enumerate(refs):
         assert rel_err(out[s], ref) < F32_TOL, (s, lens[s])
 
