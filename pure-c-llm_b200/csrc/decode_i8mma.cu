@@ -19,9 +19,10 @@
 // an N = 8 operand holds four digits of each of the block's heads, and the
 // int32 sums stay exact (|D_S| < 2^21, |D_O| < 2^21 per 128-row tile).
 //
-// Work items are pieces of up to 512 rows of one sequence (all heads), handed
-// out through a global counter; a CTA's pieces form one stream of 128-row
-// tiles.  Per tile, the softmax warpgroups (one thread per token) turn the
+// Work split: the sequences' rows, concatenated, are cut into one equal
+// range per CTA (so every SM streams the same number of bytes, whatever the
+// lengths); a piece is the part of one sequence inside one CTA's range (all
+// heads), and a CTA's pieces form one stream of 128-row tiles.  Per tile, the softmax warpgroups (one thread per token) turn the
 // score digit sums into base-2 logits x, take the tile maxima of x and of the
 // weight logits x + log2|vscale| over the warpgroup, fold the tile into the
 // running (max, sum) per head, and write each token's weight
@@ -53,11 +54,11 @@ using namespace sm100;
 constexpr int TT = 128;                 // tokens per tile (TMEM lanes of the score products)
 constexpr int NB = 8;                   // 128-byte column blocks per cache row (H * D = 1024)
 constexpr int HD = NB * 128;            // codes per cache row
-constexpr int PT = 512;                 // tokens per piece, at most
 constexpr int KS = 8;                   // code-tile ring stages
 constexpr int QN = 4;                   // piece-descriptor queue slots
 constexpr int kThreads = 384;              // warp 0 TMA, warp 1 MMA, warps 4-11 softmax
-constexpr int kMaxSeq = 1024;           // sequences per call (piece table in shared memory)
+constexpr int kMaxSeq = 1024;           // sequences per call (row table in shared memory)
+constexpr int kMaxGrid = 160;           // CTAs at most (>= the SM count of a B200)
 constexpr int TILE = TT * 128;          // bytes of one code tile: 128 tokens x 128 codes
 constexpr int TM_COLS = 256;            // D_S and D_O double buffers (4 x 64 columns)
 constexpr int TM_O = 128;
@@ -68,10 +69,9 @@ struct Params {
     float *out;
     float *part_o;                      // [n_items][HD]
     float *part_ml;                     // [n_items][H][2]
-    int *starts;                        // [n_seq + 1] first piece of each sequence
-    unsigned *counter;                  // piece counter, zero before the call
+    int *starts;                        // [n_seq + 1] first row of each sequence (rows concatenated)
     int *err;
-    int n_seq, max_len, piece;
+    int n_seq, max_len, grid;           // partials: slot cta + sequence (< grid + n_seq)
     float qscale;                       // log2(e) / sqrt(D)
 };
 
@@ -89,7 +89,7 @@ struct Geo {
     static constexpr int OFF_Q = OFF_SC + 4 * SC;                 // [2][HD] query rows
     static constexpr int OFF_RED = OFF_Q + 2 * HD * 4;            // [2 wg][2 parity][4 warps][HW][2]
     static constexpr int OFF_REDQ = OFF_RED + 2 * 2 * 4 * HW * 2 * 4;   // [2 wg][4 warps][BW] query maxima
-    static constexpr int OFF_TAB = OFF_REDQ + 2 * 4 * BW * 4;     // lens, piece starts
+    static constexpr int OFF_TAB = OFF_REDQ + 2 * 4 * BW * 4;     // lens, first rows
     static constexpr int OFF_PQ = OFF_TAB + (2 * kMaxSeq + 1) * 4;   // [QN][4] piece descriptors
     static constexpr int OFF_BAR = (OFF_PQ + QN * 16 + 7) / 8 * 8;
     static constexpr int B_FULL = 0, B_EMPTY = KS, B_SCF = 2 * KS, B_SCE = B_SCF + 2, B_SF = B_SCF + 4,
@@ -138,6 +138,7 @@ __device__ __forceinline__ float o2f(int o) { return __int_as_float(o ^ ((o >> 3
 template <int D>
 __global__ void __launch_bounds__(kThreads, 1)
 decode_i8mma_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
+                    const __grid_constant__ CUtensorMap tk32, const __grid_constant__ CUtensorMap tv32,
                     const __grid_constant__ CUtensorMap tks, const __grid_constant__ CUtensorMap tvs,
                     const __grid_constant__ Params p)
 {
@@ -204,7 +205,7 @@ decode_i8mma_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constan
     if (warp == 0) {
         const int per = (p.n_seq + 31) / 32, e0 = lane * per, e1 = min(p.n_seq, e0 + per);
         int sum = 0;
-        for (int e = e0; e < e1; e++) sum += (lens_s[e] + p.piece - 1) / p.piece;
+        for (int e = e0; e < e1; e++) sum += lens_s[e];
         int incl = sum;
 #pragma unroll
         for (int off = 1; off < 32; off <<= 1) {
@@ -214,7 +215,7 @@ decode_i8mma_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constan
         int run = incl - sum;
         for (int e = e0; e < e1; e++) {
             start_s[e] = run;
-            run += (lens_s[e] + p.piece - 1) / p.piece;
+            run += lens_s[e];
         }
         if (lane == 31) start_s[p.n_seq] = incl;
     }
@@ -222,8 +223,10 @@ decode_i8mma_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constan
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const int n_pieces = start_s[p.n_seq];
-    if (blockIdx.x == 0)                            // piece table for the merge kernel
+    // this CTA's rows [row0, row1) of the concatenated sequences
+    const long long rows_all = start_s[p.n_seq];
+    const int row0 = (int)(rows_all * blockIdx.x / gridDim.x), row1 = (int)(rows_all * (blockIdx.x + 1) / gridDim.x);
+    if (blockIdx.x == 0)                            // row table for the merge kernel
         for (int e = threadIdx.x; e <= p.n_seq; e += kThreads) p.starts[e] = start_s[e];
 
     // The CTA's pieces form one stream of 128-row tiles.  Order of the
@@ -236,23 +239,33 @@ decode_i8mma_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constan
         if (lane == 0) {
             prefetch_tmap(&tk);
             prefetch_tmap(&tv);
+            prefetch_tmap(&tk32);
+            prefetch_tmap(&tv32);
             prefetch_tmap(&tks);
             prefetch_tmap(&tvs);
             int s = 0, use = 0, sc = 0, pq = 0;
             bool ok = true;
-            auto load_codes = [&](const CUtensorMap *map, int y, int e) -> bool {
+            // the eight code blocks of one tile; a tile with fewer than 128 rows
+            // left in its piece loads only the 32-row boxes that hold them (the
+            // rest of the stage keeps stale codes, which meet masked scores and
+            // zero weights)
+            auto load_codes = [&](bool vals, int y, int e, int rows) -> bool {
+                const int nb = rows >= TT ? 1 : (rows + 31) / 32;
+                const CUtensorMap *map = rows >= TT ? (vals ? &tv : &tk) : (vals ? &tv32 : &tk32);
                 for (int b = 0; b < NB; b++) {
                     if (use >= KS && !mbar_wait(BAR(G::B_EMPTY + s), (uint32_t)(use / KS + 1) & 1u, abort_flag,
                                                 p.err, 0x401))
                         return false;
-                    mbar_arrive_expect_tx(BAR(G::B_FULL + s), TILE);
-                    tma_load_3d(base + G::OFF_RING + s * TILE, map, BAR(G::B_FULL + s), b * 128, y, e);
+                    const uint32_t dst = base + G::OFF_RING + s * TILE;
+                    mbar_arrive_expect_tx(BAR(G::B_FULL + s), rows >= TT ? TILE : nb * 32 * 128);
+                    for (int j = 0; j < nb; j++)
+                        tma_load_3d(dst + j * 32 * 128, map, BAR(G::B_FULL + s), b * 128, y + j * 32, e);
                     s = (s + 1) % KS;
                     use++;
                 }
                 return true;
             };
-            auto load_k = [&](int y, int e) -> bool {   // scales of the tile, then its eight K blocks
+            auto load_k = [&](int y, int e, int rows) -> bool {   // scales of the tile, then its eight K blocks
                 const int ss = sc & 1;
                 if (sc >= 2 &&
                     !mbar_wait(BAR(G::B_SCE + ss), (uint32_t)(sc / 2 + 1) & 1u, abort_flag, p.err, 0x403))
@@ -262,7 +275,7 @@ decode_i8mma_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constan
                 tma_load_3d(sdst, &tks, BAR(G::B_SCF + ss), 0, y, e);
                 tma_load_3d(sdst + G::SC, &tvs, BAR(G::B_SCF + ss), 0, y, e);
                 sc++;
-                return load_codes(&tk, y, e);
+                return load_codes(false, y, e, rows);
             };
             // the piece's descriptor into the queue and its query row into the
             // query buffer of its parity (pieces and queue entries count alike)
@@ -287,29 +300,40 @@ decode_i8mma_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constan
                 return true;
             };
             struct Piece { int v, e, r0, n, nt; };
-            auto claim = [&]() -> Piece {
-                const int v = (int)atomicAdd(p.counter, 1u);
-                if (v >= n_pieces) return Piece{-1, 0, 0, 0, 0};
-                int lo = 0, hi = p.n_seq - 1;           // sequence e with start[e] <= v < start[e + 1]
+            int e_cur = 0;                           // sequence holding row0
+            {
+                int lo = 0, hi = p.n_seq - 1;        // last e with start[e] <= row0
                 while (lo < hi) {
                     const int mid = (lo + hi + 1) >> 1;
-                    if (start_s[mid] <= v) lo = mid; else hi = mid - 1;
+                    if (start_s[mid] <= row0) lo = mid; else hi = mid - 1;
                 }
-                const int r0 = (v - start_s[lo]) * p.piece, n = min(lens_s[lo] - r0, p.piece);
-                return Piece{v, lo, r0, n, (n + TT - 1) / TT};
+                e_cur = lo;
+            }
+            auto claim = [&]() -> Piece {            // the next piece of this CTA's range
+                while (e_cur < p.n_seq) {
+                    const int e = e_cur++;
+                    const int a0 = max(row0, start_s[e]), a1 = min(row1, start_s[e + 1]);
+                    if (a0 >= row1) break;
+                    if (a1 > a0) {
+                        const int n = a1 - a0;
+                        return Piece{(int)blockIdx.x + e, e, a0 - start_s[e], n, (n + TT - 1) / TT};
+                    }
+                }
+                e_cur = p.n_seq;
+                return Piece{-1, 0, 0, 0, 0};
             };
             Piece cur = claim();
-            if (cur.v >= 0) ok = publish(cur.v, cur.e, cur.r0, cur.n) && load_k(cur.r0, cur.e);
+            if (cur.v >= 0) ok = publish(cur.v, cur.e, cur.r0, cur.n) && load_k(cur.r0, cur.e, cur.n);
             while (ok && cur.v >= 0) {
                 Piece nxt{-1, 0, 0, 0, 0};
                 for (int t = 0; ok && t < cur.nt; t++) {
                     if (t + 1 < cur.nt) {
-                        ok = load_k(cur.r0 + (t + 1) * TT, cur.e);
+                        ok = load_k(cur.r0 + (t + 1) * TT, cur.e, cur.n - (t + 1) * TT);
                     } else {
                         nxt = claim();
-                        if (nxt.v >= 0) ok = publish(nxt.v, nxt.e, nxt.r0, nxt.n) && load_k(nxt.r0, nxt.e);
+                        if (nxt.v >= 0) ok = publish(nxt.v, nxt.e, nxt.r0, nxt.n) && load_k(nxt.r0, nxt.e, nxt.n);
                     }
-                    if (ok) ok = load_codes(&tv, cur.r0 + t * TT, cur.e);
+                    if (ok) ok = load_codes(true, cur.r0 + t * TT, cur.e, cur.n - t * TT);
                 }
                 cur = nxt;
             }
@@ -576,7 +600,7 @@ decode_i8mma_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constan
         if (ok && v >= 0) ok = query_step(0);
         for (int k = 0; ok && v >= 0; k++) {
             const int nt = (n + TT - 1) / TT;
-            const int npc = start_s[e + 1] - start_s[e];
+            const bool whole = n == lens_s[e];      // the sequence lies in this CTA's range
 #pragma unroll
             for (int hl = 0; hl < HW; hl++) { mrun[hl] = -INFINITY; lsum[hl] = 0.f; }
 #pragma unroll
@@ -607,17 +631,17 @@ decode_i8mma_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constan
 #pragma unroll
             for (int hl = 0; hl < HW; hl++)
                 L[hl] = red[hl * 2] + red[(HW + hl) * 2] + red[(2 * HW + hl) * 2] + red[(3 * HW + hl) * 2];
-            float *dst = (npc == 1 ? p.out + (long long)e * HD : p.part_o + (long long)v * HD) + g * BW * 128 + t;
+            float *dst = (whole ? p.out + (long long)e * HD : p.part_o + (long long)v * HD) + g * BW * 128 + t;
 #pragma unroll
             for (int bl = 0; bl < BW; bl++) {
 #pragma unroll
                 for (int hh = 0; hh < HB; hh++) {
                     if (hh != half) continue;
                     const int hl = bl * HB + hh;
-                    dst[bl * 128] = npc == 1 ? oacc[bl] / L[hl] : oacc[bl];
+                    dst[bl * 128] = whole ? oacc[bl] / L[hl] : oacc[bl];
                 }
             }
-            if (npc > 1) {
+            if (!whole) {
 #pragma unroll
                 for (int hl = 0; hl < HW; hl++)
                     if (t == hl) {
@@ -644,27 +668,46 @@ decode_i8mma_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constan
     }
 }
 
-// Sequences of more than one piece: combine the pieces' partial (max, sum,
-// output) per head (base-2 maxima).  One CTA per sequence.
+// Sequences split over several CTAs' row ranges: combine the pieces' partial
+// (max, sum, output) per head (base-2 maxima).  One CTA per sequence; the
+// piece of sequence e in CTA c's range has slot c + e.
 template <int D>
 __global__ void __launch_bounds__(256)
 decode_i8mma_merge(const __grid_constant__ Params p)
 {
     constexpr int H = HD / D;
+    __shared__ int slots[kMaxGrid];
+    __shared__ int n_slots;
     const int e = blockIdx.x;
-    const long long v0 = p.starts[e];
-    const int npc = p.starts[e + 1] - (int)v0;
-    if (npc <= 1) return;                           // written by the main kernel
+    if (threadIdx.x == 0) {
+        const long long rows_all = p.starts[p.n_seq];
+        const long long s0 = p.starts[e], s1 = p.starts[e + 1];
+        auto first_row = [&](long long c) { return rows_all * c / p.grid; };
+        long long c = s0 * p.grid / rows_all;       // CTA holding row s0 (adjusted for rounding)
+        while (c + 1 < p.grid && first_row(c + 1) <= s0) c++;
+        while (c > 0 && first_row(c) > s0) c--;
+        int n = 0;
+        for (long long lo = first_row(c); c < p.grid && lo < s1; c++) {
+            const long long hi = first_row(c + 1);
+            if (hi > (lo > s0 ? lo : s0)) slots[n++] = (int)c + e;   // rows of e in this range
+            lo = hi;
+        }
+        n_slots = n;
+    }
+    __syncthreads();
+    const int n = n_slots;
+    if (n <= 1) return;                             // one range: written by the main kernel
     float *out = p.out + (long long)e * HD;
     for (int x = threadIdx.x; x < HD; x += blockDim.x) {
         const int h = x / D;
         float M = -INFINITY;
-        for (int q2 = 0; q2 < npc; q2++) M = fmaxf(M, p.part_ml[((v0 + q2) * H + h) * 2]);
+        for (int i = 0; i < n; i++) M = fmaxf(M, p.part_ml[((long long)slots[i] * H + h) * 2]);
         float L = 0.f, O = 0.f;
-        for (int q2 = 0; q2 < npc; q2++) {
-            const float f = ex2(p.part_ml[((v0 + q2) * H + h) * 2] - M);
-            L += p.part_ml[((v0 + q2) * H + h) * 2 + 1] * f;
-            O += p.part_o[(v0 + q2) * HD + x] * f;
+        for (int i = 0; i < n; i++) {
+            const long long sl = slots[i];
+            const float f = ex2(p.part_ml[(sl * H + h) * 2] - M);
+            L += p.part_ml[(sl * H + h) * 2 + 1] * f;
+            O += p.part_o[sl * HD + x] * f;
         }
         out[x] = O / L;
     }
@@ -696,12 +739,13 @@ static PFN_cuTensorMapEncodeTiled_v12000 i8_encode_fn() {
 // the 128-byte swizzle; scales: fp32, cols x 128 boxes, no swizzle).  Rows past
 // cap read as zeros.  Cached per (pointer, shape).
 static bool i8_map(CUtensorMap *m, const void *ptr, bool codes, int cols, long long cap, int n_seq,
-                   long long row_bytes) {
-    struct Entry { const void *ptr; bool codes; int cols; long long cap; int n_seq; long long rb; CUtensorMap map; };
-    static thread_local Entry cache[16];
+                   long long row_bytes, int box_rows = attn::dq::TT) {
+    struct Entry { const void *ptr; bool codes; int cols; long long cap; int n_seq; long long rb; int br; CUtensorMap map; };
+    static thread_local Entry cache[24];
     static thread_local int next = 0;
     for (auto &c : cache)
-        if (c.ptr == ptr && c.codes == codes && c.cols == cols && c.cap == cap && c.n_seq == n_seq && c.rb == row_bytes) {
+        if (c.ptr == ptr && c.codes == codes && c.cols == cols && c.cap == cap && c.n_seq == n_seq && c.rb == row_bytes &&
+            c.br == box_rows) {
             *m = c.map;
             return true;
         }
@@ -709,24 +753,16 @@ static bool i8_map(CUtensorMap *m, const void *ptr, bool codes, int cols, long l
     if (!fn) return false;
     cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)cap, (cuuint64_t)n_seq};
     cuuint64_t strides[2] = {(cuuint64_t)row_bytes, (cuuint64_t)(row_bytes * cap)};
-    cuuint32_t box[3] = {codes ? 128u : (cuuint32_t)cols, (cuuint32_t)attn::dq::TT, 1};
+    cuuint32_t box[3] = {codes ? 128u : (cuuint32_t)cols, (cuuint32_t)box_rows, 1};
     cuuint32_t estr[3] = {1, 1, 1};
     CUresult r = fn(m, codes ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3,
                     const_cast<void *>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                     codes ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return false;
-    cache[next] = Entry{ptr, codes, cols, cap, n_seq, row_bytes, *m};
-    next = (next + 1) % 16;
+    cache[next] = Entry{ptr, codes, cols, cap, n_seq, row_bytes, box_rows, *m};
+    next = (next + 1) % 24;
     return true;
-}
-
-// Rows per piece: a multiple of the 128-row tile, enough pieces for ~4 per SM
-// at the longest length, at most 512.
-static int i8mma_piece(int max_len, int n_seq) {
-    long long c = ((long long)max_len * n_seq + 4 * 148 - 1) / (4 * 148);
-    c = (c + 127) / 128 * 128;
-    return (int)std::max(128LL, std::min((long long)attn::dq::PT, c));
 }
 
 bool decode_i8mma_shape_ok(int heads, int head_dim, int kv_dtype) {
@@ -739,16 +775,18 @@ bool decode_i8mma_ok(const DecodeLaunch &L) {
     if (L.row_stride % 16 || L.row_stride < attn::dq::HD) return false;
     if (((uintptr_t)L.kbase | (uintptr_t)L.vbase | (uintptr_t)L.ksbase | (uintptr_t)L.vsbase | (uintptr_t)L.q) & 15)
         return false;
-    if (L.cap > (1LL << 31) || (long long)L.cap * L.n_seq * L.row_stride <= 0) return false;
+    if (L.cap > (1LL << 31) || (long long)L.max_len * L.n_seq >= (1LL << 31)) return false;   // int row indices
     return i8_encode_fn() != nullptr;
 }
 
+// Workspace: the row table, then one partial (max and sum per head, output
+// row) per slot cta + sequence.
 size_t decode_i8mma_ws_bytes(int n_seq, int heads, int head_dim, int max_len) {
-    const int piece = i8mma_piece(max_len, n_seq);
-    const long long n_items = (long long)n_seq * ((max_len + piece - 1) / piece);
-    size_t r = ((size_t)(n_seq + 2) * sizeof(int) + 255) / 256 * 256;              // piece table + counter
-    r += ((size_t)n_items * heads * 2 * sizeof(float) + 255) / 256 * 256;         // part_ml
-    r += ((size_t)n_items * heads * head_dim * sizeof(float) + 255) / 256 * 256;  // part_o
+    (void)max_len;
+    const long long slots = (long long)attn::dq::kMaxGrid + n_seq;
+    size_t r = ((size_t)(n_seq + 1) * sizeof(int) + 255) / 256 * 256;
+    r += ((size_t)slots * heads * 2 * sizeof(float) + 255) / 256 * 256;           // part_ml
+    r += ((size_t)slots * heads * head_dim * sizeof(float) + 255) / 256 * 256;    // part_o
     return r;
 }
 
@@ -757,26 +795,27 @@ static int launch_i8mma_t(const DecodeLaunch &L) {
     using namespace attn::dq;
     using Gm = Geo<D>;
     Params p;
-    p.piece = i8mma_piece(L.max_len, L.n_seq);
-    const int max_pieces = (L.max_len + p.piece - 1) / p.piece;
-    const long long n_items = (long long)L.n_seq * max_pieces;
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    p.grid = std::max(1, std::min(sms, kMaxGrid));
     p.n_seq = L.n_seq;
     p.max_len = L.max_len;
+    const long long slots = (long long)kMaxGrid + L.n_seq;
     char *ws = static_cast<char *>(L.ws);
-    const size_t t_bytes = ((size_t)(L.n_seq + 2) * sizeof(int) + 255) / 256 * 256;
-    const size_t ml_bytes = ((size_t)n_items * Gm::H * 2 * sizeof(float) + 255) / 256 * 256;
+    const size_t t_bytes = ((size_t)(L.n_seq + 1) * sizeof(int) + 255) / 256 * 256;
+    const size_t ml_bytes = ((size_t)slots * Gm::H * 2 * sizeof(float) + 255) / 256 * 256;
     p.starts = reinterpret_cast<int *>(ws);
-    p.counter = reinterpret_cast<unsigned *>(p.starts + L.n_seq + 1);
     p.part_ml = reinterpret_cast<float *>(ws + t_bytes);
     p.part_o = reinterpret_cast<float *>(ws + t_bytes + ml_bytes);
-    CUtensorMap mk, mv, mks, mvs;
+    CUtensorMap mk, mv, mk32, mv32, mks, mvs;
     if (!i8_map(&mk, L.kbase, true, HD, L.cap, L.n_seq, L.row_stride) ||
         !i8_map(&mv, L.vbase, true, HD, L.cap, L.n_seq, L.row_stride) ||
+        !i8_map(&mk32, L.kbase, true, HD, L.cap, L.n_seq, L.row_stride, 32) ||
+        !i8_map(&mv32, L.vbase, true, HD, L.cap, L.n_seq, L.row_stride, 32) ||
         !i8_map(&mks, L.ksbase, false, Gm::H, L.cap, L.n_seq, (long long)Gm::H * 4) ||
         !i8_map(&mvs, L.vsbase, false, Gm::H, L.cap, L.n_seq, (long long)Gm::H * 4))
         return set_error(ATTN_ERR_CUDA, "decode: cannot encode the cache tensor maps");
-    cudaError_t ce = cudaMemsetAsync(p.counter, 0, sizeof(unsigned), L.stream);
-    if (ce != cudaSuccess) return set_error(ATTN_ERR_CUDA, "decode: counter clear: %s", cudaGetErrorString(ce));
     p.q = L.q;
     p.lens = L.lens;
     p.out = L.out;
@@ -785,11 +824,7 @@ static int launch_i8mma_t(const DecodeLaunch &L) {
     const size_t smem = Gm::SMEM;
     if (!ensure_smem_attr((const void *)decode_i8mma_kernel<D>, smem))
         return set_error(ATTN_ERR_CUDA, "decode: cannot set shared-memory size");
-    int dev = 0, sms = 148;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const int grid = (int)std::max(1LL, std::min((long long)sms, n_items));
-    decode_i8mma_kernel<D><<<grid, kThreads, smem, L.stream>>>(mk, mv, mks, mvs, p);
+    decode_i8mma_kernel<D><<<p.grid, kThreads, smem, L.stream>>>(mk, mv, mk32, mv32, mks, mvs, p);
     int st = check_launch("decode_i8mma_kernel");
     if (st) return st;
     decode_i8mma_merge<D><<<L.n_seq, 256, 0, L.stream>>>(p);
