@@ -669,14 +669,17 @@ decode_i8mma_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constan
 }
 
 // Sequences split over several CTAs' row ranges: combine the pieces' partial
-// (max, sum, output) per head (base-2 maxima).  One CTA per sequence; the
-// piece of sequence e in CTA c's range has slot c + e.
+// (max, sum, output) per head (base-2 maxima).  Grid (sequence, quarter of
+// the row); the piece of sequence e in CTA c's range has slot c + e.  The
+// per-(piece, head) factors 2^(m_i - M) / L are made once in shared memory,
+// so each output is one pass of independent loads.
 template <int D>
 __global__ void __launch_bounds__(256)
 decode_i8mma_merge(const __grid_constant__ Params p)
 {
     constexpr int H = HD / D;
     __shared__ int slots[kMaxGrid];
+    __shared__ float fac[kMaxGrid][H];
     __shared__ int n_slots;
     const int e = blockIdx.x;
     if (threadIdx.x == 0) {
@@ -697,20 +700,24 @@ decode_i8mma_merge(const __grid_constant__ Params p)
     __syncthreads();
     const int n = n_slots;
     if (n <= 1) return;                             // one range: written by the main kernel
-    float *out = p.out + (long long)e * HD;
-    for (int x = threadIdx.x; x < HD; x += blockDim.x) {
-        const int h = x / D;
-        float M = -INFINITY;
+    if (threadIdx.x < H) {
+        const int h = threadIdx.x;
+        float M = -INFINITY, L = 0.f;
         for (int i = 0; i < n; i++) M = fmaxf(M, p.part_ml[((long long)slots[i] * H + h) * 2]);
-        float L = 0.f, O = 0.f;
         for (int i = 0; i < n; i++) {
-            const long long sl = slots[i];
-            const float f = ex2(p.part_ml[(sl * H + h) * 2] - M);
-            L += p.part_ml[(sl * H + h) * 2 + 1] * f;
-            O += p.part_o[sl * HD + x] * f;
+            const float f = ex2(p.part_ml[((long long)slots[i] * H + h) * 2] - M);
+            fac[i][h] = f;
+            L += p.part_ml[((long long)slots[i] * H + h) * 2 + 1] * f;
         }
-        out[x] = O / L;
+        const float inv = 1.f / L;
+        for (int i = 0; i < n; i++) fac[i][h] *= inv;
     }
+    __syncthreads();
+    const int x = blockIdx.y * 256 + threadIdx.x, h = x / D;
+    float O = 0.f;
+#pragma unroll 4
+    for (int i = 0; i < n; i++) O += p.part_o[(long long)slots[i] * HD + x] * fac[i][h];
+    p.out[(long long)e * HD + x] = O;
 }
 
 }  // namespace dq
@@ -827,7 +834,7 @@ static int launch_i8mma_t(const DecodeLaunch &L) {
     decode_i8mma_kernel<D><<<p.grid, kThreads, smem, L.stream>>>(mk, mv, mk32, mv32, mks, mvs, p);
     int st = check_launch("decode_i8mma_kernel");
     if (st) return st;
-    decode_i8mma_merge<D><<<L.n_seq, 256, 0, L.stream>>>(p);
+    decode_i8mma_merge<D><<<dim3(L.n_seq, HD / 256), 256, 0, L.stream>>>(p);
     return check_launch("decode_i8mma_merge");
 }
 

@@ -462,6 +462,16 @@ def test_int8_decode_signed_scales_and_zero_query(A, H, d):
         assert rel_err(out[s], ref) < F32_TOL, (s, lens[s])
 
 
+@pytest.mark.parametrize("H,d", [(16, 64), (8, 128)])
+def test_int8_decode_fewer_rows_than_sms(A, H, d):
+    """Fewer cache rows in all than SMs: most CTAs get an empty share, and a
+    sequence's rows are spread over several CTAs with empty ones between."""
+    lens = [1, 3, 2, 7, 1]
+    out, refs = _int8_decode_case(A, H, d, lens, 8, seed=160)
+    for s, ref in enumerate(refs):
+        assert rel_err(out[s], ref) < F32_TOL, (s, lens[s])
+
+
 def test_int8_stream_strided_rows(A):
     """Rows wider than H*d (per-row bulk copies instead of one copy per block)."""
     lens = [300, 1, 777]
