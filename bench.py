@@ -61,7 +61,7 @@ L2_BYTES = 126 * 2 ** 20
 # dram__bytes_read.sum + dram__bytes_write.sum per launch of the dominant
 # kernel, each from one ncu capture of that kernel at the config's size;
 # None where not captured
-TRAFFIC = {"c3-bf16": 51817984, "c4-f32": 2153309904, "c4-int8": 577940736, "c2": 51463168}
+TRAFFIC = {"c3-bf16": 51817984, "c4-f32": 2153309904, "c4-int8": 584853248, "c2": 51463168}
 
 
 def causal_flops(B, H, T, d):
@@ -260,6 +260,7 @@ class Workload:
             vc = torch.randn((n * cap, H * d), generator=g, device=dev)
             self.int8 = cfg["kv"] == "int8"
             if self.int8:
+                self.launches = 2           # the decode kernel and the kernel that merges split sequences
                 self.kc, self.ks = A.quantize_int8_t(kc, H)
                 self.vc, self.vs = A.quantize_int8_t(vc, H)
                 del kc, vc
