@@ -28,6 +28,11 @@
 //               the S row it read and P's low part to a separate TMEM block
 // TMEM (256 columns): S/Ph buffers [0,64) and [64,128), Pl [128,192), O
 // [192, 192+D).  An S buffer is reused once the PV that read its P finished.
+// Head dims 96 and 128: the split query tile would not fit in shared memory
+// next to a two-stage ring, so it lives in TMEM (Qh in columns [0,D), Ql in
+// [D,2D); the S products read their A operand from TMEM) and key tiles are
+// 32 rows; the splitters move each landed query tile from its shared-memory
+// staging buffer into TMEM (512 columns: Q parts, two S buffers, Pl, O).
 // Every mbarrier wait is bounded; a timeout records a code in the device
 // error word, raises a CTA-wide abort flag, and all roles fall through to the
 // teardown, which frees TMEM.
@@ -46,7 +51,6 @@ namespace ftf {
 using namespace sm100;
 
 constexpr int BM = 128;            // query rows per tile (TMEM lanes)
-constexpr int BN = 64;             // keys per tile
 constexpr int kThreads = 384;
 constexpr int kMaxCtas = 320;
 constexpr int kMaxItems = 32768;
@@ -54,21 +58,26 @@ constexpr int kLocalItems = 256;
 
 template <int D>
 struct Cfg {
+    static constexpr bool QT = D > 64;              // query parts in TMEM
+    static constexpr int BN = QT ? 32 : 64;         // keys per tile
     static constexpr int CH = D / 32;               // 128-byte column chunks of a row
     static constexpr int QB = BM * D * 4;           // one fp32 Q tile (high or low part)
     static constexpr int KB = BN * D * 4;           // one fp32 K or V tile
-    static constexpr int OFF_QH = 0, OFF_QL = QB;
-    static constexpr int OFF_ST = 2 * QB;           // stages: Kh, Kl, V raw then V^T low, V^T high
+    static constexpr int OFF_QH = 0, OFF_QL = QB;   // (TMEM mode: OFF_QH is the raw staging tile)
+    static constexpr int OFF_ST = QT ? QB : 2 * QB; // stages: Kh, Kl, V raw then V^T low, V^T high
     static constexpr int STAGE = 4 * KB;
     static constexpr int OFF_BAR = OFF_ST + 2 * STAGE;
     static constexpr int OFF_ITEMS = OFF_BAR + 256;
     static constexpr int SMEM = OFF_ITEMS + 4 * kLocalItems + 1024;
     static constexpr int CTAS = 2 * (SMEM + 1024) <= 228 * 1024 ? 2 : 1;
-    static constexpr int TM_S = 0, TM_PL = 128, TM_O = 192, TM_COLS = 256;
+    static constexpr int TM_QH = 0, TM_QL = D;      // TMEM mode only
+    static constexpr int TM_S = QT ? 2 * D : 0, TM_PL = TM_S + 2 * BN, TM_O = TM_PL + BN;
+    static constexpr int TM_COLS = QT ? 512 : 256;
     // per-thread registers after setmaxnreg: warpgroup 0, splitters, softmax
     // (two CTAs per SM: 384 x 80 at launch = 128 x (40 + 56 + 144); one CTA:
-    // 384 x 160 at launch >= 128 x (40 + 128 + 160))
-    static constexpr int REG_SPLIT = CTAS == 2 ? 56 : 128;
+    // 384 x 160 at launch >= 128 x (64 + 160 + 160))
+    static constexpr int REG_MMA = CTAS == 2 ? 40 : 64;
+    static constexpr int REG_SPLIT = CTAS == 2 ? 56 : 160;
     static constexpr int REG_SOFT = CTAS == 2 ? 144 : 160;
     static_assert(TM_O + D <= TM_COLS, "TMEM budget");
 };
@@ -83,7 +92,8 @@ enum {
     B_PF = 13,                     // P written (and O rescaled)
     B_OD = 14,                     // PV finished
     B_SPL = 15,                    // splitters: raw V read (before V^T overwrites it)
-    B_COUNT = 16
+    B_QC = 16,                     // TMEM mode: the staged raw query tile was read
+    B_COUNT = 17
 };
 
 struct Params {
@@ -92,7 +102,7 @@ struct Params {
     const float *v;                // V itself, for the first query row (see the epilogue)
     long long in_stride;
     long long out_stride;
-    int T, H, B, n_qt, n_items;
+    int T, H, B, n_qt, n_items, bn;   // bn: keys per tile
     float scale_log2;              // log2(e) / sqrt(d)
     int *err;
     int use_list;
@@ -111,12 +121,12 @@ __device__ __forceinline__ void split_item(const Params &p, int i, int &b, int &
     h = r % p.H;
     b = r / p.H;
 }
-__device__ __forceinline__ Item make_item(int b, int h, int qt, int T) {
+__device__ __forceinline__ Item make_item(int b, int h, int qt, int T, int bn) {
     Item it;
     it.b = b;
     it.h = h;
     it.q0 = qt * BM;
-    it.n_kv = (min(it.q0 + BM, T) + BN - 1) / BN;   // key tiles up to the diagonal
+    it.n_kv = (min(it.q0 + BM, T) + bn - 1) / bn;   // key tiles up to the diagonal
     return it;
 }
 __device__ __forceinline__ int item_of(const Params &p, int k) {
@@ -136,14 +146,14 @@ __device__ __forceinline__ bool next_item(const Params &p, const uint32_t *items
     if (n_local >= 0) {
         if (k >= n_local) return false;
         const uint32_t v = items_s[k];
-        it = make_item((int)(v & 0xfffu), (int)((v >> 12) & 0x3ffu), (int)(v >> 22), p.T);
+        it = make_item((int)(v & 0xfffu), (int)((v >> 12) & 0x3ffu), (int)(v >> 22), p.T, p.bn);
         return true;
     }
     const int id = item_of(p, k);
     if (id < 0) return false;
     int b, h, qt;
     split_item(p, id, b, h, qt);
-    it = make_item(b, h, qt, p.T);
+    it = make_item(b, h, qt, p.T, p.bn);
     return true;
 }
 
@@ -171,6 +181,7 @@ fwd_tf32_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
                 const __grid_constant__ CUtensorMap tv, const __grid_constant__ Params p)
 {
     using C = Cfg<D>;
+    constexpr int BN = C::BN;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
@@ -212,6 +223,7 @@ fwd_tf32_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
         mbar_init(BAR(B_PF), 128);
         mbar_init(BAR(B_OD), 1);
         mbar_init(BAR(B_SPL), 128);
+        mbar_init(BAR(B_QC), 128);
         *abort_flag = 0;
         fence_mbar_init();
     }
@@ -229,7 +241,7 @@ fwd_tf32_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
 
     // registers: see Cfg (each setmaxnreg inside its role's branch)
     if (warp < 8) {
-        if (warp < 4) regs_dec<40>();
+        if (warp < 4) regs_dec<C::REG_MMA>();
         if (warp == 0) {
             // -------------------------------------------------------- producer
             const bool leader = elect_one();
@@ -243,7 +255,7 @@ fwd_tf32_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
             for (int k = 0; ok; k++) {
                 Item it;
                 if (!next_item(p, items_s, n_local, k, it)) break;
-                if (k > 0 && !(ok = wait_w(B_QE, k - 1, 0x401))) break;
+                if (k > 0 && !(ok = wait_w(C::QT ? B_QC : B_QE, k - 1, 0x401))) break;
                 if (leader) {
                     mbar_arrive_expect_tx(BAR(B_QF), C::QB);
 #pragma unroll
@@ -283,18 +295,23 @@ fwd_tf32_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
                     if (t >= 2 && !(ok = wait_w(B_BF + sbuf, (t >> 1) - 1, 0x413))) break;
                     tc_fence_after();
                     const uint32_t kh = base + C::OFF_ST + st * C::STAGE, kl = kh + C::KB;
-                    const uint32_t d_t = tmem + C::TM_S + 64 * sbuf;
+                    const uint32_t d_t = tmem + C::TM_S + BN * sbuf;
                     if (leader) {
                         // K-step kk: chunk kk/4 (128-byte columns), +32 bytes within it
 #pragma unroll
                         for (int part = 0; part < 3; part++) {       // hh, hl, lh
                             const uint32_t qa = base + (part == 2 ? C::OFF_QL : C::OFF_QH);
+                            const uint32_t qt = tmem + (part == 2 ? C::TM_QL : C::TM_QH);
                             const uint32_t kb = part == 1 ? kl : kh;
 #pragma unroll
                             for (int kk = 0; kk < D / 8; kk++) {
-                                const uint64_t ad = sw128_desc(qa + (kk >> 2) * (BM * 128) + (kk & 3) * 32, 16, 1024);
                                 const uint64_t bd = sw128_desc(kb + (kk >> 2) * (BN * 128) + (kk & 3) * 32, 16, 1024);
-                                mma_tf32_ss(d_t, ad, bd, idS, (part > 0 || kk > 0));
+                                if constexpr (C::QT) {
+                                    mma_tf32_ts(d_t, qt + 8 * kk, bd, idS, (part > 0 || kk > 0));
+                                } else {
+                                    const uint64_t ad = sw128_desc(qa + (kk >> 2) * (BM * 128) + (kk & 3) * 32, 16, 1024);
+                                    mma_tf32_ss(d_t, ad, bd, idS, (part > 0 || kk > 0));
+                                }
                             }
                         }
                         mma_commit(BAR(B_SF + sbuf));
@@ -319,9 +336,9 @@ fwd_tf32_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
                     if (!(ok = wait_w(B_PF, t, 0x422))) break;
                     tc_fence_after();
                     const uint32_t vl = base + C::OFF_ST + st * C::STAGE + 2 * C::KB, vh = vl + C::KB;
-                    const uint32_t ph = tmem + C::TM_S + 64 * sbuf, pl = tmem + C::TM_PL;
+                    const uint32_t ph = tmem + C::TM_S + BN * sbuf, pl = tmem + C::TM_PL;
                     if (leader) {
-                        // V^T tile [D rows][64 keys] K-major: key chunk kk/4 (32 keys, D*128
+                        // V^T tile [D rows][BN keys] K-major: key chunk kk/4 (32 keys, D*128
                         // bytes apart), +32 bytes per 8-key step within it
 #pragma unroll
                         for (int part = 0; part < 3; part++) {       // hh, hl, lh
@@ -351,9 +368,40 @@ fwd_tf32_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
                 Item it;
                 if (!next_item(p, items_s, n_local, k, it)) break;
                 if (!(ok = wait_w(B_QF, k, 0x431))) break;
-                split_hi_lo(qh, ql, BM * D, tid, 128);
-                fence_async_smem();
-                mbar_arrive(BAR(B_QS));
+                if constexpr (C::QT) {
+                    // this warp's 32 query rows (its TMEM lane quadrant), 32 columns at a
+                    // time: staged raw values -> high and low parts in TMEM
+                    if (k > 0 && !(ok = wait_w(B_QE, k - 1, 0x434))) break;   // the last item's S products read Q
+                    tc_fence_after();
+                    const int quad = warp & 3, row = quad * 32 + lane;
+                    const uint32_t lb = (uint32_t)(quad * 32) << 16;
+#pragma unroll 1
+                    for (int c = 0; c < C::CH; c++) {
+                        uint32_t hi[32], lo[32];
+                        const uint8_t *src = sb + C::OFF_QH + c * (BM * 128) + row * 128;
+#pragma unroll
+                        for (int j = 0; j < 8; j++) {
+                            const float4 x = *reinterpret_cast<const float4 *>(src + ((j ^ (row & 7)) << 4));
+                            const float xv[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+                            for (int u = 0; u < 4; u++) {
+                                const uint32_t h = __float_as_uint(xv[u]) & 0xFFFFE000u;
+                                hi[4 * j + u] = h;
+                                lo[4 * j + u] = __float_as_uint(xv[u] - __uint_as_float(h));
+                            }
+                        }
+                        tmem_st32(tmem + lb + C::TM_QH + 32 * c, hi);
+                        tmem_st32(tmem + lb + C::TM_QL + 32 * c, lo);
+                    }
+                    tmem_wait_st();
+                    tc_fence_before();
+                    mbar_arrive(BAR(B_QC));
+                    mbar_arrive(BAR(B_QS));
+                } else {
+                    split_hi_lo(qh, ql, BM * D, tid, 128);
+                    fence_async_smem();
+                    mbar_arrive(BAR(B_QS));
+                }
                 for (int j = 0; j < it.n_kv; j++, t++) {
                     const int st = t & 1;
                     if (!(ok = wait_w(B_KVF + st, t >> 1, 0x432))) break;
@@ -405,31 +453,28 @@ fwd_tf32_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
             float m_run = -INFINITY, l_run = 0.f;
             for (int j = 0; j < it.n_kv; j++, t++) {
                 const int sbuf = t & 1;
-                const uint32_t tS = tmem + lane_base + C::TM_S + 64 * sbuf;
+                const uint32_t tS = tmem + lane_base + C::TM_S + BN * sbuf;
                 ok = mbar_wait(BAR(B_SF + sbuf), (t >> 1) & 1, abort_flag, p.err, 0x441);
                 if (!(ok = __all_sync(0xffffffffu, ok))) break;
                 tc_fence_after();
-                float s[64];
-                {
-                    uint32_t t0[32], t1[32];
-                    tmem_ld32(tS, t0);
-                    tmem_ld32(tS + 32, t1);
+                float s[BN];
+#pragma unroll
+                for (int h2 = 0; h2 < BN / 32; h2++) {
+                    uint32_t t0[32];
+                    tmem_ld32(tS + 32 * h2, t0);
                     tmem_wait_ld();
 #pragma unroll
-                    for (int c = 0; c < 32; c++) {
-                        s[c] = __uint_as_float(t0[c]);
-                        s[32 + c] = __uint_as_float(t1[c]);
-                    }
+                    for (int c = 0; c < 32; c++) s[32 * h2 + c] = __uint_as_float(t0[c]);
                 }
                 const int key0 = j * BN;
                 if (key0 + BN - 1 > it.q0 || key0 + BN > p.T) {   // tiles touching the diagonal or T
 #pragma unroll
-                    for (int c = 0; c < 64; c++)
+                    for (int c = 0; c < BN; c++)
                         if (key0 + c > qrow || key0 + c >= p.T) s[c] = -INFINITY;
                 }
                 float mx = -INFINITY;
 #pragma unroll
-                for (int c = 0; c < 64; c += 2) mx = max3(mx, s[c], s[c + 1]);
+                for (int c = 0; c < BN; c += 2) mx = max3(mx, s[c], s[c + 1]);
                 mx *= p.scale_log2;
                 float alpha = 1.f;
                 const bool grow = mx > m_run + 8.f;               // also true on the first tile
@@ -439,7 +484,7 @@ fwd_tf32_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
                     l_run *= alpha;
                 }
 #pragma unroll
-                for (int c = 0; c < 64; c++) {
+                for (int c = 0; c < BN; c++) {
                     s[c] = ex2(fmaf(s[c], p.scale_log2, -m_run));
                     l_run += s[c];
                 }
@@ -448,7 +493,7 @@ fwd_tf32_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
                 if (!(ok = __all_sync(0xffffffffu, ok))) break;
                 tc_fence_after();
 #pragma unroll
-                for (int h2 = 0; h2 < 2; h2++) {
+                for (int h2 = 0; h2 < BN / 32; h2++) {
                     uint32_t hi[32], lo[32];
 #pragma unroll
                     for (int c = 0; c < 32; c++) {
@@ -481,35 +526,30 @@ fwd_tf32_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
             ok = mbar_wait(BAR(B_OD), (t - 1) & 1, abort_flag, p.err, 0x443);
             if (!(ok = __all_sync(0xffffffffu, ok))) break;
             tc_fence_after();
-            float o[D];
+            // The first query row attends to key 0 alone: its output is V_0
+            // exactly (the products would leave a 2^-22 relative error, and a
+            // backward pass turns O_0 - V_0 into a nonzero gradient where the
+            // exact one is zero).
+            const float inv = qrow == 0 ? 1.f : 1.f / l_run;
+            float *dst = p.o + ((long long)it.b * p.T + qrow) * p.out_stride + (long long)it.h * D;
+            const float *v0 = p.v + (long long)it.b * p.T * p.in_stride + (long long)it.h * D;
 #pragma unroll
             for (int c0 = 0; c0 < D; c0 += 32) {
                 uint32_t tt[32];
                 tmem_ld32(tO + c0, tt);
+                tmem_wait_ld();
+                if (qrow < p.T) {
+                    float o[32];
 #pragma unroll
-                for (int c = 0; c < 32; c++) o[c0 + c] = __uint_as_float(tt[c]);
-            }
-            tmem_wait_ld();
-            tc_fence_before();
-            if (qrow < p.T) {
-                float inv = 1.f / l_run;
-                float *dst = p.o + ((long long)it.b * p.T + qrow) * p.out_stride + (long long)it.h * D;
-                if (qrow == 0) {
-                    // The first query row attends to key 0 alone: its output is V_0
-                    // exactly (the products would leave a 2^-22 relative error, and a
-                    // backward pass turns O_0 - V_0 into a nonzero gradient where the
-                    // exact one is zero).
-                    const float *src = p.v + (long long)it.b * p.T * p.in_stride + (long long)it.h * D;
+                    for (int c = 0; c < 32; c++) o[c] = qrow == 0 ? v0[c0 + c] : __uint_as_float(tt[c]) * inv;
 #pragma unroll
-                    for (int c = 0; c < D; c++) o[c] = src[c];
-                    inv = 1.f;
+                    for (int c = 0; c < 32; c += 4)
+                        *reinterpret_cast<float4 *>(dst + c0 + c) = make_float4(o[c], o[c + 1], o[c + 2], o[c + 3]);
                 }
-#pragma unroll
-                for (int c = 0; c < D; c += 4)
-                    *reinterpret_cast<float4 *>(dst + c) = make_float4(o[c] * inv, o[c + 1] * inv, o[c + 2] * inv,
-                                                                       o[c + 3] * inv);
-                if (p.lse) p.lse[((long long)it.b * p.H + it.h) * p.T + qrow] = (m_run + __log2f(l_run)) * kLn2;
             }
+            tc_fence_before();
+            if (qrow < p.T && p.lse)
+                p.lse[((long long)it.b * p.H + it.h) * p.T + qrow] = (m_run + __log2f(l_run)) * kLn2;
         }
     }
 
@@ -575,7 +615,8 @@ static bool cached_map_f32(CUtensorMap *m, const void *ptr, int cols, int T, int
 }
 
 bool fwd_tf32_sm100_supported(int D, long long in_stride, long long out_stride) {
-    return (D == 32 || D == 64) && in_stride % 4 == 0 && out_stride % 4 == 0 && encode_fn_t() != nullptr;
+    return (D == 32 || D == 64 || D == 96 || D == 128) && in_stride % 4 == 0 && out_stride % 4 == 0 &&
+           encode_fn_t() != nullptr;
 }
 
 static void lpt_schedule_tf32(const attn::ftf::Params &p, int ctas, std::vector<unsigned short> &out) {
@@ -586,7 +627,7 @@ static void lpt_schedule_tf32(const attn::ftf::Params &p, int ctas, std::vector<
     const int hb = p.H * p.B;
     for (int i = 0; i < p.n_items; i++) {
         const int qt = p.n_qt - 1 - i / hb;
-        const long long cost = 2LL * (qt + 1) + 2;      // key tiles + per-item overhead
+        const long long cost = (long long)(qt + 1) * BM / p.bn + 2;      // key tiles + per-item overhead
         auto [load, c] = heap.top();
         heap.pop();
         lists[c].push_back((unsigned short)i);
@@ -607,8 +648,8 @@ static int launch_tf32_t(const void *q, const void *k, const void *v, void *o, f
     using namespace attn::ftf;
     using Cg = Cfg<D>;
     CUtensorMap mq, mk, mv;
-    if (!cached_map_f32(&mq, q, H * D, T, B, in_stride, BM) || !cached_map_f32(&mk, k, H * D, T, B, in_stride, BN) ||
-        !cached_map_f32(&mv, v, H * D, T, B, in_stride, BN))
+    if (!cached_map_f32(&mq, q, H * D, T, B, in_stride, BM) || !cached_map_f32(&mk, k, H * D, T, B, in_stride, Cg::BN) ||
+        !cached_map_f32(&mv, v, H * D, T, B, in_stride, Cg::BN))
         return set_error(ATTN_ERR_CUDA, "3xTF32 forward: cuTensorMapEncodeTiled failed");
     int dev = 0;
     cudaGetDevice(&dev);
@@ -630,6 +671,7 @@ static int launch_tf32_t(const void *q, const void *k, const void *v, void *o, f
     p.B = B;
     p.n_qt = (T + BM - 1) / BM;
     p.n_items = p.n_qt * H * B;
+    p.bn = Cg::BN;
     p.scale_log2 = attn::kLog2e / sqrtf((float)D);
     p.err = err;
     const int ctas = std::max(1, std::min(std::min(Cg::CTAS * sm_count[dev], kMaxCtas), p.n_items));
@@ -637,9 +679,9 @@ static int launch_tf32_t(const void *q, const void *k, const void *v, void *o, f
     p.packable = B < 4096 && H < 1024 && p.n_qt < 1024;
     p.sched = nullptr;
     if (p.use_list) {
-        static unsigned short *sched_buf[128][2] = {{nullptr}};
-        static long long sched_key[128][2];
-        const int slot = D == 64;
+        static unsigned short *sched_buf[128][4] = {{nullptr}};
+        static long long sched_key[128][4];
+        const int slot = D / 32 - 1;
         const long long key = (((long long)T * 4096 + H) * 65536 + B) * 512 + ctas;
         if (!sched_buf[dev][slot]) {
             if (cudaMalloc(&sched_buf[dev][slot], (kMaxCtas + 1 + kMaxItems) * sizeof(unsigned short)) != cudaSuccess)
@@ -660,12 +702,12 @@ static int launch_tf32_t(const void *q, const void *k, const void *v, void *o, f
     const size_t smem = Cg::SMEM;
     if (!ensure_smem_attr((const void *)fwd_tf32_kernel<D>, smem))
         return set_error(ATTN_ERR_CUDA, "3xTF32 forward: cannot set shared-memory size");
-    static bool carveout_set[128][2] = {{false}};
-    if (!carveout_set[dev][D == 64]) {
+    static bool carveout_set[128][4] = {{false}};
+    if (!carveout_set[dev][D / 32 - 1]) {
         if (cudaFuncSetAttribute((const void *)fwd_tf32_kernel<D>, cudaFuncAttributePreferredSharedMemoryCarveout,
                                  100) != cudaSuccess)
             return set_error(ATTN_ERR_CUDA, "3xTF32 forward: cannot set the shared-memory carveout");
-        carveout_set[dev][D == 64] = true;
+        carveout_set[dev][D / 32 - 1] = true;
     }
     fwd_tf32_kernel<D><<<ctas, kThreads, smem, s>>>(mq, mk, mv, p);
     return check_launch("3xTF32 forward kernel");
@@ -679,6 +721,8 @@ int launch_fwd_tf32_sm100(int D, const void *q, const void *k, const void *v, vo
     switch (D) {
         case 32: return launch_tf32_t<32>(q, k, v, o, lse, in_stride, out_stride, B, H, T, err, s);
         case 64: return launch_tf32_t<64>(q, k, v, o, lse, in_stride, out_stride, B, H, T, err, s);
+        case 96: return launch_tf32_t<96>(q, k, v, o, lse, in_stride, out_stride, B, H, T, err, s);
+        case 128: return launch_tf32_t<128>(q, k, v, o, lse, in_stride, out_stride, B, H, T, err, s);
         default: return set_error(ATTN_ERR_UNSUPPORTED, "3xTF32 forward: head_dim %d", D);
     }
 }

@@ -60,7 +60,8 @@ def test_forward_f32_golden(A, name):
 
 
 @pytest.mark.parametrize("B,T,H,d", [(2, 130, 3, 32), (1, 200, 2, 64), (1, 77, 2, 96), (1, 129, 2, 128),
-                                     (1, 64, 1, 64), (3, 1, 2, 32), (1, 256, 4, 64)])
+                                     (1, 64, 1, 64), (3, 1, 2, 32), (1, 256, 4, 64), (2, 300, 3, 128),
+                                     (1, 515, 2, 96), (2, 1, 1, 128), (1, 33, 1, 96)])
 def test_forward_f32_vs_oracle(A, B, T, H, d):
     q, k, v = qkv(11 * T + d, B, T, H, d)
     ref, _, rlse = O.attn_forward(q, k, v, B, T, H, d)
