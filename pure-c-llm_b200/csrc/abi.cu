@@ -49,6 +49,11 @@ int launch_bwd_f32(int dtype, int D, const void *dout, const void *q, const void
                    int H, int T, cudaStream_t s);
 size_t bwd_f32_workspace_bytes(int B, int H, int T);
 bool bwd_bf16_sm100_supported(int D, long long in_stride, long long out_stride);
+bool bwd_tf32_sm100_supported(int D, long long in_stride, long long out_stride);
+int launch_bwd_tf32_sm100(int D, const void *dout, const void *q, const void *k, const void *v, const void *o,
+                          const float *lse, void *dq, void *dk, void *dv, int accumulate, void *ws,
+                          long long in_stride, long long out_stride, int B, int H, int T, int *err,
+                          cudaStream_t s);
 int launch_bwd_bf16_sm100(int D, const void *dout, const void *q, const void *k, const void *v, const void *o,
                           const float *lse, void *dq, void *dk, void *dv, int accumulate, void *ws,
                           long long in_stride, long long out_stride, int B, int H, int T, int *err,
@@ -221,6 +226,10 @@ int attn_bwd_ex(const attn_shape *s, int dtype, const void *dO, const void *Q, c
                          need, workspace_bytes);
     if (dtype == ATTN_BF16 && bwd_bf16_sm100_supported(s->head_dim, in_st, out_st))
         return launch_bwd_bf16_sm100(s->head_dim, dO, Q, K, V, O, lse, dQ, dK, dV, accumulate ? 1 : 0, workspace,
+                                     in_st, out_st, s->batch, s->heads, s->seq_len, device_error_ptr(),
+                                     reinterpret_cast<cudaStream_t>(stream));
+    if (dtype == ATTN_F32 && bwd_tf32_sm100_supported(s->head_dim, in_st, out_st))
+        return launch_bwd_tf32_sm100(s->head_dim, dO, Q, K, V, O, lse, dQ, dK, dV, accumulate ? 1 : 0, workspace,
                                      in_st, out_st, s->batch, s->heads, s->seq_len, device_error_ptr(),
                                      reinterpret_cast<cudaStream_t>(stream));
     return launch_bwd_f32(dtype, s->head_dim, dO, Q, K, V, O, lse, dQ, dK, dV, accumulate ? 1 : 0,
