@@ -248,7 +248,6 @@ bwd_tf32_kernel(const __grid_constant__ CUtensorMap m_a, const __grid_constant__
         }
     } else if (warp >= 4 && warp < 8) {
         // ------------------------------------------------------------ splitters
-        const int tid = threadIdx.x - 128;
         const int quad = warp & 3, row = quad * 32 + lane;
         const uint32_t lb = (uint32_t)(quad * 32) << 16;
         bool ok = wait_w(B_FXF, 0, 0x531);
@@ -292,9 +291,13 @@ bwd_tf32_kernel(const __grid_constant__ CUtensorMap m_a, const __grid_constant__
                 uint8_t *hi = s0 + (part ? 4 : 0) * C::SB, *lo = hi + C::SB;
                 uint8_t *th = hi + 2 * C::SB, *tl = hi + 3 * C::SB;
                 const bool transpose = KIND == 0 || part == 0;
+                // a warp instruction covers 4 rows x 8 columns: conflict-free both for
+                // the row-major reads and writes and for the transposed writes (the
+                // 16-byte units of 8 transposed rows x 4 words spread over all banks)
 #pragma unroll
                 for (int i = 0; i < PER; i++) {
-                    const int idx = tid + 128 * i, r = idx / D, col = idx % D;
+                    const int blk = (warp & 3) + 4 * i;            // block of 4 rows x 8 columns
+                    const int r = 4 * (blk % (BS / 4)) + (lane >> 3), col = 8 * (blk / (BS / 4)) + (lane & 7);
                     const int off = (col >> 5) * (BS * 128) + r * 128 + ((((col & 31) >> 2) ^ (r & 7)) << 4) +
                                     (col & 3) * 4;
                     const float x = *reinterpret_cast<const float *>(hi + off);
