@@ -38,6 +38,12 @@ using namespace sm100;
 constexpr int BT = 128;           // fixed rows per tile (TMEM lanes)
 constexpr int BS = 32;            // streamed rows per tile
 constexpr int kThreads = 384;
+// The tensor core's accumulation into TMEM is not round-to-nearest; over the
+// thousands of products a dK/dV/dQ row gathers at T = 4096 that drifts by
+// ~5e-5.  So the accumulators restart every kGroup streamed tiles and the
+// elementwise warpgroup adds each group's sums into fp32 running sums in
+// shared memory (in the fixed tiles' staging area, free once they are in TMEM).
+constexpr int kGroup = 4;
 
 template <int D>
 struct Cfg {
@@ -47,7 +53,9 @@ struct Cfg {
     // shared memory: two raw fixed tiles, 2 stages x (C hi, C lo, C^T hi, C^T lo,
     // D hi, D lo, D^T hi, D^T lo), 2 stages x row statistics (dkdv), barriers
     static constexpr int OFF_FA = 0, OFF_FB = FB;
-    static constexpr int OFF_ST = 2 * FB;
+    static constexpr int RS_PITCH = D + 1;          // floats per running-sum row (conflict-free columns)
+    static constexpr int RS_BYTES = 2 * BT * RS_PITCH * 4;    // dV and dK (dQ: the first half)
+    static constexpr int OFF_ST = ((2 * FB > RS_BYTES ? 2 * FB : RS_BYTES) + 1023) / 1024 * 1024;
     static constexpr int STAGE = 8 * SB;
     static constexpr int OFF_STATS = OFF_ST + 2 * STAGE;
     static constexpr int OFF_BAR = OFF_STATS + 2 * 2 * BS * 4;
@@ -62,7 +70,7 @@ struct Cfg {
 };
 
 // barrier slots
-enum { B_FXF = 0, B_FX, B_SF, B_SS = B_SF + 2, B_SE = B_SS + 2, B_XY = B_SE + 2, B_W, B_ACC, B_ST, B_COUNT };
+enum { B_FXF = 0, B_FX, B_SF, B_SS = B_SF + 2, B_SE = B_SS + 2, B_XY = B_SE + 2, B_W, B_ACC, B_ST, B_AF, B_COUNT };
 
 struct Params {
     float *out1, *out2;          // dkdv: dK, dV;  dq: dQ
@@ -75,16 +83,6 @@ struct Params {
 };
 
 __device__ __forceinline__ uint32_t hi_bits(float x) { return __float_as_uint(x) & 0xFFFFE000u; }
-
-// 32 lanes x 16 columns of 32-bit (load): thread t gets lane (base + t), columns [col, col+16)
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
-        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-        : "r"(taddr));
-}
 
 // KIND 0: dkdv, KIND 1: dq.  m_a/m_b: the fixed pair (128-row boxes), m_c/m_d:
 // the streamed pair (32-row boxes); 3-D {H*D, T, B} views, 32-float x rows
@@ -127,6 +125,7 @@ bwd_tf32_kernel(const __grid_constant__ CUtensorMap m_a, const __grid_constant__
         mbar_init(BAR(B_W), 128);
         mbar_init(BAR(B_ACC), 1);
         mbar_init(BAR(B_ST), 128);
+        mbar_init(BAR(B_AF), 128);
         *abort_flag = 0;
         fence_mbar_init();
     }
@@ -218,6 +217,8 @@ bwd_tf32_kernel(const __grid_constant__ CUtensorMap m_a, const __grid_constant__
         for (int it = 0; it < count; it++) {
             const int st = it & 1;
             if (!wait_w(B_W, it, 0x515)) break;
+            // a new group overwrites the accumulators: the previous group's sums were read
+            if (it >= kGroup && it % kGroup == 0 && !wait_w(B_AF, it / kGroup - 1, 0x516)) break;
             tc_fence_after();
             const uint32_t sbase = base + C::OFF_ST + st * C::STAGE;
             if (leader) {
@@ -237,7 +238,7 @@ bwd_tf32_kernel(const __grid_constant__ CUtensorMap m_a, const __grid_constant__
 #pragma unroll
                         for (int kk = 0; kk < BS / 8; kk++) {
                             const uint64_t bd = sw128_desc(tv + (kk & 3) * 32, 16, 1024);
-                            mma_tf32_ts(acc, wa + 8 * kk, bd, idAcc, (it > 0 || part > 0 || kk > 0));
+                            mma_tf32_ts(acc, wa + 8 * kk, bd, idAcc, (it % kGroup > 0 || part > 0 || kk > 0));
                         }
                     }
                 }
@@ -382,33 +383,43 @@ bwd_tf32_kernel(const __grid_constant__ CUtensorMap m_a, const __grid_constant__
             tmem_wait_st();
             tc_fence_before();
             mbar_arrive(BAR(B_W));
+            if (it % kGroup == kGroup - 1 || it == count - 1) {
+                // the group's sums -> fp32 running sums (this thread's row), then
+                // the accumulators are free for the next group
+                if (!(ok = wait_w(B_ACC, it, 0x545))) break;
+                tc_fence_after();
+                for (int a = 0; a < (KIND == 0 ? 2 : 1); a++) {
+                    float *rs = reinterpret_cast<float *>(sb + C::OFF_FA) + (a * BT + row) * C::RS_PITCH;
+#pragma unroll 1
+                    for (int c0 = 0; c0 < D; c0 += 16) {
+                        uint32_t acc[16];
+                        tmem_ld16(tmem + lb + (a ? C::TM_A2 : C::TM_A1) + c0, acc);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int c = 0; c < 16; c++)
+                            rs[c0 + c] = (it < kGroup ? 0.f : rs[c0 + c]) + __uint_as_float(acc[c]);
+                    }
+                }
+                tc_fence_before();
+                mbar_arrive(BAR(B_AF));
+            }
         }
-        // epilogue: accumulators -> global (fp32, optionally added to the output)
-        if (ok && count > 0) ok = mbar_wait(BAR(B_ACC), (count - 1) & 1, abort_flag, p.err, 0x544);
-        if (__all_sync(0xffffffffu, ok && count > 0)) {
-            tc_fence_after();
+        // epilogue: running sums -> global (fp32, optionally added to the output)
+        if (__all_sync(0xffffffffu, ok && count > 0) && grow_ < p.T) {
             for (int a = 0; a < (KIND == 0 ? 2 : 1); a++) {
                 // dkdv: a=0 -> dV (out2), a=1 -> dK (out1);  dq: dQ (out1)
                 float *outp = KIND == 0 ? (a == 0 ? p.out2 : p.out1) : p.out1;
                 float *dst = outp + ((long long)b * p.T + grow_) * p.out_stride + (long long)h * D;
+                const float *rs = reinterpret_cast<const float *>(sb + C::OFF_FA) + (a * BT + row) * C::RS_PITCH;
 #pragma unroll
-                for (int c0 = 0; c0 < D; c0 += 32) {
-                    uint32_t acc[32];
-                    tmem_ld32(tmem + lb + (a ? C::TM_A2 : C::TM_A1) + c0, acc);
-                    tmem_wait_ld();
-                    if (grow_ < p.T) {
-#pragma unroll
-                        for (int c = 0; c < 32; c += 4) {
-                            float4 v = make_float4(__uint_as_float(acc[c]), __uint_as_float(acc[c + 1]),
-                                                   __uint_as_float(acc[c + 2]), __uint_as_float(acc[c + 3]));
-                            float4 *d4 = reinterpret_cast<float4 *>(dst + c0 + c);
-                            if (p.accumulate) {
-                                const float4 o = *d4;
-                                v.x += o.x; v.y += o.y; v.z += o.z; v.w += o.w;
-                            }
-                            *d4 = v;
-                        }
+                for (int c = 0; c < D; c += 4) {
+                    float4 v = make_float4(rs[c], rs[c + 1], rs[c + 2], rs[c + 3]);
+                    float4 *d4 = reinterpret_cast<float4 *>(dst + c);
+                    if (p.accumulate) {
+                        const float4 o = *d4;
+                        v.x += o.x; v.y += o.y; v.z += o.z; v.w += o.w;
                     }
+                    *d4 = v;
                 }
             }
         }

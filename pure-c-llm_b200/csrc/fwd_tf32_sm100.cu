@@ -72,14 +72,23 @@ struct Cfg {
     static constexpr int CTAS = 2 * (SMEM + 1024) <= 228 * 1024 ? 2 : 1;
     static constexpr int TM_QH = 0, TM_QL = D;      // TMEM mode only
     static constexpr int TM_S = QT ? 2 * D : 0, TM_PL = TM_S + 2 * BN, TM_O = TM_PL + BN;
-    static constexpr int TM_COLS = QT ? 512 : 256;
+    // The tensor core's accumulation into TMEM is not round-to-nearest, and a
+    // row's O gathers many thousands of products: accumulated there over the
+    // whole key range, an all-positive V drifts by ~1e-5 at T = 1024.  So each
+    // key tile's PV starts a fresh sum (TM_O) and the softmax warpgroup adds it
+    // into the running output in fp32 -- in TMEM (TM_A) where the columns
+    // allow, else in registers (d 128).
+    static constexpr bool ACC_TMEM = TM_O + 2 * D <= (QT ? 512 : (D <= 32 ? 256 : 512));
+    static constexpr int TM_A = TM_O + D;
+    static constexpr int TM_COLS = QT || TM_A + D > 256 ? 512 : 256;
     // per-thread registers after setmaxnreg: warpgroup 0, splitters, softmax
     // (two CTAs per SM: 384 x 80 at launch = 128 x (40 + 56 + 144); one CTA:
     // 384 x 160 at launch >= 128 x (64 + 160 + 160))
     static constexpr int REG_MMA = CTAS == 2 ? 40 : 64;
     static constexpr int REG_SPLIT = CTAS == 2 ? 56 : 160;
     static constexpr int REG_SOFT = CTAS == 2 ? 144 : 160;
-    static_assert(TM_O + D <= TM_COLS, "TMEM budget");
+    static_assert(TM_O + D <= TM_COLS && (!ACC_TMEM || TM_A + D <= TM_COLS), "TMEM budget");
+    static_assert(TM_COLS * CTAS <= 512, "TMEM budget per SM");
 };
 
 enum {
@@ -347,7 +356,7 @@ fwd_tf32_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
 #pragma unroll
                             for (int kk = 0; kk < BN / 8; kk++) {
                                 const uint64_t bd = sw128_desc(vb + (kk >> 2) * (D * 128) + (kk & 3) * 32, 16, 1024);
-                                mma_tf32_ts(tmem + C::TM_O, pa + 8 * kk, bd, idO, (j > 0 || part > 0 || kk > 0));
+                                mma_tf32_ts(tmem + C::TM_O, pa + 8 * kk, bd, idO, (part > 0 || kk > 0));   // fresh per tile
                             }
                         }
                         mma_commit(BAR(B_OD));
@@ -444,6 +453,8 @@ fwd_tf32_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
         const int row = quad * 32 + lane;
         const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
         const uint32_t tPL = tmem + lane_base + C::TM_PL, tO = tmem + lane_base + C::TM_O;
+        const uint32_t tA = tmem + lane_base + C::TM_A;
+        float oacc[C::ACC_TMEM ? 1 : D];            // running output in registers (d 128)
         int t = 0;
         bool ok = true;
         for (int k = 0; ok; k++) {
@@ -451,6 +462,10 @@ fwd_tf32_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
             if (!next_item(p, items_s, n_local, k, it)) break;
             const int qrow = it.q0 + row;
             float m_run = -INFINITY, l_run = 0.f;
+            if constexpr (!C::ACC_TMEM) {
+#pragma unroll
+                for (int c = 0; c < D; c++) oacc[c] = 0.f;
+            }
             for (int j = 0; j < it.n_kv; j++, t++) {
                 const int sbuf = t & 1;
                 const uint32_t tS = tmem + lane_base + C::TM_S + BN * sbuf;
@@ -505,15 +520,30 @@ fwd_tf32_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
                     tmem_st32(tS + 32 * h2, hi);
                     tmem_st32(tPL + 32 * h2, lo);
                 }
-                if (__any_sync(0xffffffffu, j > 0 && grow)) {
-                    uint32_t o[32];
+                // running output = (running output + PV of the previous key tile) * alpha,
+                // in fp32 (the PV about to be issued overwrites TM_O)
+                if (j > 0) {
+                    if constexpr (C::ACC_TMEM) {
+#pragma unroll 1
+                        for (int c0 = 0; c0 < D; c0 += 16) {
+                            uint32_t pv[16], oa[16];
+                            tmem_ld16(tO + c0, pv);
+                            if (j > 1) tmem_ld16(tA + c0, oa);
+                            tmem_wait_ld();
 #pragma unroll
-                    for (int c0 = 0; c0 < D; c0 += 32) {
-                        tmem_ld32(tO + c0, o);
-                        tmem_wait_ld();
+                            for (int c = 0; c < 16; c++)
+                                oa[c] = __float_as_uint(((j > 1 ? __uint_as_float(oa[c]) : 0.f) + __uint_as_float(pv[c])) * alpha);
+                            tmem_st16(tA + c0, oa);
+                        }
+                    } else {
 #pragma unroll
-                        for (int c = 0; c < 32; c++) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
-                        tmem_st32(tO + c0, o);
+                        for (int c0 = 0; c0 < D; c0 += 16) {
+                            uint32_t pv[16];
+                            tmem_ld16(tO + c0, pv);
+                            tmem_wait_ld();
+#pragma unroll
+                            for (int c = 0; c < 16; c++) oacc[c0 + c] = (oacc[c0 + c] + __uint_as_float(pv[c])) * alpha;
+                        }
                     }
                 }
                 tmem_wait_st();
@@ -533,18 +563,36 @@ fwd_tf32_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
             const float inv = qrow == 0 ? 1.f : 1.f / l_run;
             float *dst = p.o + ((long long)it.b * p.T + qrow) * p.out_stride + (long long)it.h * D;
             const float *v0 = p.v + (long long)it.b * p.T * p.in_stride + (long long)it.h * D;
-#pragma unroll
-            for (int c0 = 0; c0 < D; c0 += 32) {
-                uint32_t tt[32];
-                tmem_ld32(tO + c0, tt);
-                tmem_wait_ld();
+            const bool more = it.n_kv > 1;         // a running output exists besides the last PV
+            auto out16 = [&](int c0, const uint32_t (&tt)[16], const float *acc) {
                 if (qrow < p.T) {
-                    float o[32];
+                    float o[16];
 #pragma unroll
-                    for (int c = 0; c < 32; c++) o[c] = qrow == 0 ? v0[c0 + c] : __uint_as_float(tt[c]) * inv;
+                    for (int c = 0; c < 16; c++) o[c] = qrow == 0 ? v0[c0 + c] : (acc[c] + __uint_as_float(tt[c])) * inv;
 #pragma unroll
-                    for (int c = 0; c < 32; c += 4)
+                    for (int c = 0; c < 16; c += 4)
                         *reinterpret_cast<float4 *>(dst + c0 + c) = make_float4(o[c], o[c + 1], o[c + 2], o[c + 3]);
+                }
+            };
+            if constexpr (C::ACC_TMEM) {
+#pragma unroll 1
+                for (int c0 = 0; c0 < D; c0 += 16) {
+                    uint32_t tt[16], oa[16];
+                    tmem_ld16(tO + c0, tt);
+                    if (more) tmem_ld16(tA + c0, oa);
+                    tmem_wait_ld();
+                    float acc[16];
+#pragma unroll
+                    for (int c = 0; c < 16; c++) acc[c] = more ? __uint_as_float(oa[c]) : 0.f;
+                    out16(c0, tt, acc);
+                }
+            } else {
+#pragma unroll
+                for (int c0 = 0; c0 < D; c0 += 16) {
+                    uint32_t tt[16];
+                    tmem_ld16(tO + c0, tt);
+                    tmem_wait_ld();
+                    out16(c0, tt, oacc + c0);
                 }
             }
             tc_fence_before();
