@@ -55,6 +55,7 @@ constexpr int kThreads = 384;
 constexpr int kMaxCtas = 320;
 constexpr int kMaxItems = 32768;
 constexpr int kLocalItems = 256;
+constexpr int kFold = 4;           // key tiles per fresh PV sum (see Cfg)
 
 template <int D>
 struct Cfg {
@@ -74,10 +75,10 @@ struct Cfg {
     static constexpr int TM_S = QT ? 2 * D : 0, TM_PL = TM_S + 2 * BN, TM_O = TM_PL + BN;
     // The tensor core's accumulation into TMEM is not round-to-nearest, and a
     // row's O gathers many thousands of products: accumulated there over the
-    // whole key range, an all-positive V drifts by ~1e-5 at T = 1024.  So each
-    // key tile's PV starts a fresh sum (TM_O) and the softmax warpgroup adds it
-    // into the running output in fp32 -- in TMEM (TM_A) where the columns
-    // allow, else in registers (d 128).
+    // whole key range, an all-positive V drifts by ~1e-5 at T = 1024.  So PV
+    // restarts its TMEM sum (TM_O) every kFold key tiles and the softmax
+    // warpgroup adds each group into the running output in fp32 -- in TMEM
+    // (TM_A) where the columns allow, else in registers (d 128).
     static constexpr bool ACC_TMEM = TM_O + 2 * D <= (QT ? 512 : (D <= 32 ? 256 : 512));
     static constexpr int TM_A = TM_O + D;
     static constexpr int TM_COLS = QT || TM_A + D > 256 ? 512 : 256;
@@ -356,7 +357,7 @@ fwd_tf32_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
 #pragma unroll
                             for (int kk = 0; kk < BN / 8; kk++) {
                                 const uint64_t bd = sw128_desc(vb + (kk >> 2) * (D * 128) + (kk & 3) * 32, 16, 1024);
-                                mma_tf32_ts(tmem + C::TM_O, pa + 8 * kk, bd, idO, (part > 0 || kk > 0));   // fresh per tile
+                                mma_tf32_ts(tmem + C::TM_O, pa + 8 * kk, bd, idO, (j % kFold > 0 || part > 0 || kk > 0));
                             }
                         }
                         mma_commit(BAR(B_OD));
@@ -520,29 +521,45 @@ fwd_tf32_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
                     tmem_st32(tS + 32 * h2, hi);
                     tmem_st32(tPL + 32 * h2, lo);
                 }
-                // running output = (running output + PV of the previous key tile) * alpha,
-                // in fp32 (the PV about to be issued overwrites TM_O)
-                if (j > 0) {
-                    if constexpr (C::ACC_TMEM) {
+                // Every kFold tiles the PV sum in TM_O is folded into the running output
+                // (fp32) before the next PV restarts it: running = (running + PV sum) *
+                // alpha.  In between, a grown max rescales the PV sum and the running
+                // output in place (warp-uniform: a warp rescales if any row needs it).
+                const bool fold = j > 0 && j % kFold == 0;
+                const bool have = j > kFold;           // a running output exists
+                const bool resc = !fold && j > 0 && __any_sync(0xffffffffu, grow);
+                if constexpr (C::ACC_TMEM) {
+                    if (fold || resc) {
 #pragma unroll 1
                         for (int c0 = 0; c0 < D; c0 += 16) {
                             uint32_t pv[16], oa[16];
                             tmem_ld16(tO + c0, pv);
-                            if (j > 1) tmem_ld16(tA + c0, oa);
+                            if (have) tmem_ld16(tA + c0, oa);
                             tmem_wait_ld();
 #pragma unroll
-                            for (int c = 0; c < 16; c++)
-                                oa[c] = __float_as_uint(((j > 1 ? __uint_as_float(oa[c]) : 0.f) + __uint_as_float(pv[c])) * alpha);
-                            tmem_st16(tA + c0, oa);
+                            for (int c = 0; c < 16; c++) {
+                                const float o = have ? __uint_as_float(oa[c]) : 0.f, v = __uint_as_float(pv[c]);
+                                oa[c] = __float_as_uint(fold ? (o + v) * alpha : o * alpha);
+                                pv[c] = __float_as_uint(v * alpha);
+                            }
+                            if (fold || have) tmem_st16(tA + c0, oa);
+                            if (resc) tmem_st16(tO + c0, pv);
                         }
-                    } else {
+                    }
+                } else {
+                    if (fold || resc) {
 #pragma unroll
                         for (int c0 = 0; c0 < D; c0 += 16) {
                             uint32_t pv[16];
                             tmem_ld16(tO + c0, pv);
                             tmem_wait_ld();
 #pragma unroll
-                            for (int c = 0; c < 16; c++) oacc[c0 + c] = (oacc[c0 + c] + __uint_as_float(pv[c])) * alpha;
+                            for (int c = 0; c < 16; c++) {
+                                const float v = __uint_as_float(pv[c]);
+                                oacc[c0 + c] = (oacc[c0 + c] + (fold ? v : 0.f)) * alpha;
+                                pv[c] = __float_as_uint(v * alpha);
+                            }
+                            if (resc) tmem_st16(tO + c0, pv);
                         }
                     }
                 }
@@ -563,7 +580,7 @@ fwd_tf32_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
             const float inv = qrow == 0 ? 1.f : 1.f / l_run;
             float *dst = p.o + ((long long)it.b * p.T + qrow) * p.out_stride + (long long)it.h * D;
             const float *v0 = p.v + (long long)it.b * p.T * p.in_stride + (long long)it.h * D;
-            const bool more = it.n_kv > 1;         // a running output exists besides the last PV
+            const bool more = it.n_kv > kFold;     // a running output exists besides the last PV sum
             auto out16 = [&](int c0, const uint32_t (&tt)[16], const float *acc) {
                 if (qrow < p.T) {
                     float o[16];
