@@ -40,10 +40,11 @@ constexpr int BS = 32;            // streamed rows per tile
 constexpr int kThreads = 384;
 // The tensor core's accumulation into TMEM is not round-to-nearest; over the
 // thousands of products a dK/dV/dQ row gathers at T = 4096 that drifts by
-// ~5e-5.  So the accumulators restart every kGroup streamed tiles and the
-// elementwise warpgroup adds each group's sums into fp32 running sums in
-// shared memory (in the fixed tiles' staging area, free once they are in TMEM).
-constexpr int kGroup = 4;
+// ~5e-5.  So the accumulators restart every kGroup streamed tiles (96
+// accumulation steps, ~4e-6 at worst) and the elementwise warpgroup adds each
+// group's sums into fp32 running sums in shared memory (in the fixed tiles'
+// staging area, free once they are in TMEM).
+constexpr int kGroup = 8;
 
 template <int D>
 struct Cfg {
