@@ -223,6 +223,7 @@ decode_i8mma_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constan
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    asm volatile("griddepcontrol.launch_dependents;");   // the merge kernel may be scheduled
     // this CTA's rows [row0, row1) of the concatenated sequences
     const long long rows_all = start_s[p.n_seq];
     const int row0 = (int)(rows_all * blockIdx.x / gridDim.x), row1 = (int)(rows_all * (blockIdx.x + 1) / gridDim.x);
@@ -682,6 +683,10 @@ decode_i8mma_merge(const __grid_constant__ Params p)
     __shared__ float fac[kMaxGrid][H];
     __shared__ int n_slots;
     const int e = blockIdx.x;
+    // launched as a programmatic dependent of the main kernel: its CTAs may start
+    // on SMs the main kernel has left; the partials are read only after the main
+    // grid completed and its writes are visible
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     if (threadIdx.x == 0) {
         const long long rows_all = p.starts[p.n_seq];
         const long long s0 = p.starts[e], s1 = p.starts[e + 1];
@@ -834,7 +839,17 @@ static int launch_i8mma_t(const DecodeLaunch &L) {
     decode_i8mma_kernel<D><<<p.grid, kThreads, smem, L.stream>>>(mk, mv, mk32, mv32, mks, mvs, p);
     int st = check_launch("decode_i8mma_kernel");
     if (st) return st;
-    decode_i8mma_merge<D><<<dim3(L.n_seq, HD / 256), 256, 0, L.stream>>>(p);
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = dim3(L.n_seq, HD / 256);
+    lc.blockDim = dim3(256);
+    lc.stream = L.stream;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    lc.attrs = at;
+    lc.numAttrs = 1;
+    const cudaError_t ce = cudaLaunchKernelEx(&lc, decode_i8mma_merge<D>, p);
+    if (ce != cudaSuccess) return set_error(ATTN_ERR_CUDA, "decode: merge launch: %s", cudaGetErrorString(ce));
     return check_launch("decode_i8mma_merge");
 }
 
