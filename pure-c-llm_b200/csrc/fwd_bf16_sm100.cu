@@ -10,7 +10,10 @@
 // the causal triangle's uneven item costs balance across SMs.  12 warps:
 //   warp 0      TMA producer: Q tiles into a double buffer (the next item's Q
 //               loads while the current item runs), K_j/V_j into a 4-stage
-//               ring that runs across item boundaries
+//               ring that runs across item boundaries, K and V on separate
+//               barriers (the S issuer needs only K).  The first item's Q and
+//               K_0 are requested during the set-up, by the thread that
+//               initialises the barriers.
 //   warps 1-3   MMA issuers, tcgen05.mma kind::f16 with fp32 accumulators in
 //               TMEM: warp 1 issues S_i = Q_i K_j^T for both query tiles (both
 //               operands in shared memory), warp 2 O_0 += P_0 V_j and warp 3
@@ -28,6 +31,9 @@
 // current one; that item's first PV waits until the warpgroup has read out
 // the previous O.
 //
+// Epilogue: each softmax warp stages its 32 normalised output rows in shared
+// memory (bf16, 128-byte swizzle) and writes them with one TMA store, which
+// also drops the rows past T.
 // TMEM: S0 cols [0,128), S1 [128,256), O0 [256,256+D), O1 [256+D, 256+2D),
 // P0 and P1 64 columns each after the O tiles.
 // Every mbarrier wait is bounded; a timeout records a code in the device
@@ -63,7 +69,8 @@ struct Cfg {
     static constexpr int OFF_Q = 0;                 // 2 buffers x 2 query tiles
     static constexpr int OFF_KV = 4 * Q_BYTES;
     static constexpr int STAGE_BYTES = 2 * KV_BYTES;
-    static constexpr int OFF_BAR = OFF_KV + kStages * STAGE_BYTES;
+    static constexpr int OFF_O = OFF_KV + kStages * STAGE_BYTES;   // 2 x 128 output rows, 128-byte swizzle
+    static constexpr int OFF_BAR = OFF_O + 2 * BM * D * 2;
     static constexpr int OFF_ITEMS = OFF_BAR + 256;     // kLocalItems packed items
     static constexpr int SMEM = OFF_ITEMS + 4 * 256 + 1024;
     static constexpr int TM_S0 = 0, TM_S1 = 128, TM_O0 = 256, TM_O1 = 256 + D;
@@ -76,9 +83,10 @@ struct Cfg {
 enum {
     B_QF = 0,                    // 2: query buffer loaded
     B_QE = 2,                    // 2: query buffer free (its last S finished)
-    B_KVF = 4,                   // kStages: key/value stage loaded
-    B_KVE = 4 + kStages,         // kStages: key/value stage free
-    B_SF = 4 + 2 * kStages,      // 2: S ready (per warpgroup)
+    B_KF = 4,                    // kStages: key tile of the stage loaded
+    B_VF = 4 + kStages,          // kStages: value tile of the stage loaded
+    B_KVE = 4 + 2 * kStages,     // kStages: key/value stage free
+    B_SF = 4 + 3 * kStages,      // 2: S ready (per warpgroup)
     B_SE = B_SF + 2,             // 2: S drained into registers
     B_PF = B_SE + 2,             // 2: P written (and O rescaled)
     B_OD = B_PF + 2,             // 2: PV finished
@@ -168,7 +176,8 @@ __device__ __forceinline__ bool next_item(const Params &p, const uint32_t *items
 template <int D>
 __global__ void __launch_bounds__(kThreads, 1)
 fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
-           const __grid_constant__ CUtensorMap tv, const __grid_constant__ Params p)
+           const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap to,
+           const __grid_constant__ Params p)
 {
     using C = Cfg<D>;
     static_assert(D == 64, "this kernel instance covers head_dim 64");
@@ -176,11 +185,12 @@ fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
     uint8_t *sb = smem_raw + (base - raw);
-    const uint32_t sQ = base + C::OFF_Q, sKV = base + C::OFF_KV;
+    const uint32_t sQ = base + C::OFF_Q, sKV = base + C::OFF_KV, sO = base + C::OFF_O;
     const uint32_t bar0 = base + C::OFF_BAR;
 #define BAR(i) (bar0 + 8u * (uint32_t)(i))
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sb + C::OFF_BAR + 192);
-    volatile int *abort_flag = reinterpret_cast<volatile int *>(sb + C::OFF_BAR + 196);
+    static_assert(8 * B_COUNT <= 224, "barrier area");
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sb + C::OFF_BAR + 224);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(sb + C::OFF_BAR + 228);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     uint32_t *items_s = reinterpret_cast<uint32_t *>(sb + C::OFF_ITEMS);
@@ -211,9 +221,25 @@ fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
             mbar_init(BAR(B_OD + i), 1);
             mbar_init(BAR(B_OF + i), 128);
         }
-        for (int s = 0; s < kStages; s++) { mbar_init(BAR(B_KVF + s), 1); mbar_init(BAR(B_KVE + s), 3); }
+        for (int s = 0; s < kStages; s++) {
+            mbar_init(BAR(B_KF + s), 1);
+            mbar_init(BAR(B_VF + s), 1);
+            mbar_init(BAR(B_KVE + s), 3);
+        }
         *abort_flag = 0;
         fence_mbar_init();
+        // Every CTA's first item is item blockIdx.x (both schedules deal the
+        // first items one per CTA, longest first), so its query tiles and first
+        // key tile start loading before the rest of the set-up and before the
+        // schedule is read.
+        const Item it = decode_item(p, (int)blockIdx.x);
+        prefetch_tmap(&tq);
+        prefetch_tmap(&tk);
+        mbar_arrive_expect_tx(BAR(B_QF), (it.has_q1 ? 2 : 1) * C::Q_BYTES);
+        tma_load_3d(sQ, &tq, BAR(B_QF), it.h * D, it.q0, it.b);
+        if (it.has_q1) tma_load_3d(sQ + C::Q_BYTES, &tq, BAR(B_QF), it.h * D, it.q0 + BM, it.b);
+        mbar_arrive_expect_tx(BAR(B_KF), C::KV_BYTES);
+        tma_load_3d(sKV, &tk, BAR(B_KF), it.h * D, 0, it.b);
     }
     if (warp == 0) {
         tmem_alloc(smem_u32(tmem_slot), C::TM_COLS);
@@ -233,11 +259,7 @@ fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
         // ------------------------------------------------------------ producer
         // warp-wide loop like the MMA issuer; the elected lane issues the copies
         const bool leader = elect_one();
-        if (leader) {
-            prefetch_tmap(&tq);
-            prefetch_tmap(&tk);
-            prefetch_tmap(&tv);
-        }
+        if (leader) prefetch_tmap(&tv);
         int g = 0;                                  // key/value tiles issued so far
         bool ok = true;
         for (int k = 0; ok; k++) {
@@ -248,7 +270,7 @@ fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
                 !(ok = __all_sync(0xffffffffu, mbar_wait(BAR(B_QE + qb), ((k >> 1) + 1) & 1, abort_flag, p.err, 0x201))))
                 break;
             const uint32_t qdst = sQ + qb * 2 * C::Q_BYTES;
-            if (leader) {
+            if (leader && k > 0) {                  // item 0's query tiles were issued at set-up
                 mbar_arrive_expect_tx(BAR(B_QF + qb), (it.has_q1 ? 2 : 1) * C::Q_BYTES);
                 tma_load_3d(qdst, &tq, BAR(B_QF + qb), it.h * D, it.q0, it.b);
                 if (it.has_q1) tma_load_3d(qdst + C::Q_BYTES, &tq, BAR(B_QF + qb), it.h * D, it.q0 + BM, it.b);
@@ -261,10 +283,13 @@ fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
                                                              p.err, 0x202))))
                     break;
                 if (leader) {
-                    mbar_arrive_expect_tx(BAR(B_KVF + st), 2 * C::KV_BYTES);
                     const uint32_t dst = sKV + st * C::STAGE_BYTES;
-                    tma_load_3d(dst, &tk, BAR(B_KVF + st), it.h * D, j * BN, it.b);
-                    tma_load_3d(dst + C::KV_BYTES, &tv, BAR(B_KVF + st), it.h * D, j * BN, it.b);
+                    if (g > 0) {                        // key tile 0 was issued at set-up
+                        mbar_arrive_expect_tx(BAR(B_KF + st), C::KV_BYTES);
+                        tma_load_3d(dst, &tk, BAR(B_KF + st), it.h * D, j * BN, it.b);
+                    }
+                    mbar_arrive_expect_tx(BAR(B_VF + st), C::KV_BYTES);
+                    tma_load_3d(dst + C::KV_BYTES, &tv, BAR(B_VF + st), it.h * D, j * BN, it.b);
                 }
                 __syncwarp();
             }
@@ -301,7 +326,7 @@ fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
                 if (!(ok = wait(B_QF + qb, k >> 1, 0x213))) break;
                 for (int j = 0; ok && j < it.n_kv; j++) {
                     const int st = (g + j) % kStages;
-                    if (!(ok = wait(B_KVF + st, (g + j) / kStages, 0x214))) break;
+                    if (!(ok = wait(B_KF + st, (g + j) / kStages, 0x214))) break;
                     // Descriptors of consecutive K-steps differ only in the
                     // start-address field, so each step adds a constant.
                     const uint64_t kd = sw128_desc(sKV + st * C::STAGE_BYTES, 16, 1024);
@@ -340,7 +365,7 @@ fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
                     const int st = (g + j) % kStages;
                     // the stage's load completing orders this release after the
                     // stage's previous use was released by all three issuers
-                    if (!(ok = wait(B_KVF + st, (g + j) / kStages, 0x215))) break;
+                    if (!(ok = wait(B_VF + st, (g + j) / kStages, 0x215))) break;
                     if (j >= n) {                                 // stage not used by this query tile
                         release(B_KVE + st, false);
                         continue;
@@ -493,22 +518,36 @@ fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
             tmem_wait_ld();
             tc_fence_before();
             mbar_arrive(BAR(B_OF + wg));             // the next item's first PV may overwrite O
-            const int qrow = qs + row;
-            if (qrow < p.T) {
+            // The warp stages its 32 output rows (bf16, 128-byte swizzle: the
+            // 16-byte chunk c of row r sits at chunk c ^ (r & 7)) and stores
+            // them with one TMA copy, which drops the rows past T.
+            {
                 const float inv = 1.f / l_run;
-                __nv_bfloat16 *dst = p.o + ((long long)it.b * p.T + qrow) * p.out_stride + (long long)it.h * D;
+                const uint32_t srow = sO + (uint32_t)(wg * BM + row) * 128u;
+                if (lane == 0) bulk_wait_read_all();     // the previous item's copy has read the rows
+                __syncwarp();
 #pragma unroll
-                for (int c = 0; c < D; c += 8) {
-                    uint4 v;
-                    v.x = pack_bf16(__uint_as_float(o[c + 0]) * inv, __uint_as_float(o[c + 1]) * inv);
-                    v.y = pack_bf16(__uint_as_float(o[c + 2]) * inv, __uint_as_float(o[c + 3]) * inv);
-                    v.z = pack_bf16(__uint_as_float(o[c + 4]) * inv, __uint_as_float(o[c + 5]) * inv);
-                    v.w = pack_bf16(__uint_as_float(o[c + 6]) * inv, __uint_as_float(o[c + 7]) * inv);
-                    *reinterpret_cast<uint4 *>(dst + c) = v;
+                for (int c = 0; c < 8; c++) {
+                    const uint32_t a = pack_bf16(__uint_as_float(o[8 * c + 0]) * inv, __uint_as_float(o[8 * c + 1]) * inv);
+                    const uint32_t b = pack_bf16(__uint_as_float(o[8 * c + 2]) * inv, __uint_as_float(o[8 * c + 3]) * inv);
+                    const uint32_t d = pack_bf16(__uint_as_float(o[8 * c + 4]) * inv, __uint_as_float(o[8 * c + 5]) * inv);
+                    const uint32_t e = pack_bf16(__uint_as_float(o[8 * c + 6]) * inv, __uint_as_float(o[8 * c + 7]) * inv);
+                    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};"
+                                 ::"r"(srow + ((uint32_t)(c ^ (row & 7)) << 4)), "r"(a), "r"(b), "r"(d), "r"(e)
+                                 : "memory");
                 }
-                if (p.lse) p.lse[((long long)it.b * p.H + it.h) * p.T + qrow] = (m_run + __log2f(l_run)) * kLn2;
+                fence_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    tma_store_3d(&to, sO + (uint32_t)(wg * BM + quad * 32) * 128u, it.h * D, qs + quad * 32, it.b);
+                    bulk_commit_group();
+                }
             }
+            const int qrow = qs + row;
+            if (qrow < p.T && p.lse)
+                p.lse[((long long)it.b * p.H + it.h) * p.T + qrow] = (m_run + __log2f(l_run)) * kLn2;
         }
+        if (lane == 0) bulk_wait_all();              // output copies complete before the CTA exits
     }
 
     // ---------------------------------------------------------------- teardown
@@ -549,12 +588,12 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 // 3-D view {columns, T, B} of a (B*T, stride) bf16 activation; 64 x 128 boxes
 // with the 128-byte swizzle the MMA descriptors expect.
-static bool make_map(CUtensorMap *m, const void *ptr, int cols, int T, int B, long long stride) {
+static bool make_map(CUtensorMap *m, const void *ptr, int cols, int T, int B, long long stride, int box_rows) {
     auto fn = encode_fn();
     if (!fn) return false;
     cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)T, (cuuint64_t)B};
     cuuint64_t strides[2] = {(cuuint64_t)stride * 2, (cuuint64_t)stride * 2 * T};
-    cuuint32_t box[3] = {64, 128, 1};
+    cuuint32_t box[3] = {64, (cuuint32_t)box_rows, 1};
     cuuint32_t estr[3] = {1, 1, 1};
     CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(ptr), dims, strides, box, estr,
                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -595,18 +634,19 @@ static void lpt_schedule(const attn::fa::Params &p, int ctas, std::vector<unsign
 
 // Tensor maps are cached per (pointer, shape): encoding one costs a driver
 // call, and training / benchmark loops reuse the same buffers every step.
-static bool cached_map(CUtensorMap *m, const void *ptr, int cols, int T, int B, long long stride) {
-    struct Entry { const void *ptr; int cols, T, B; long long stride; CUtensorMap map; };
-    static thread_local Entry cache[12];
+static bool cached_map(CUtensorMap *m, const void *ptr, int cols, int T, int B, long long stride,
+                       int box_rows = 128) {
+    struct Entry { const void *ptr; int cols, T, B; long long stride; int box_rows; CUtensorMap map; };
+    static thread_local Entry cache[16];
     static thread_local int next = 0;
     for (auto &e : cache)
-        if (e.ptr == ptr && e.cols == cols && e.T == T && e.B == B && e.stride == stride) {
+        if (e.ptr == ptr && e.cols == cols && e.T == T && e.B == B && e.stride == stride && e.box_rows == box_rows) {
             *m = e.map;
             return true;
         }
-    if (!make_map(m, ptr, cols, T, B, stride)) return false;
-    cache[next] = Entry{ptr, cols, T, B, stride, *m};
-    next = (next + 1) % 12;
+    if (!make_map(m, ptr, cols, T, B, stride, box_rows)) return false;
+    cache[next] = Entry{ptr, cols, T, B, stride, box_rows, *m};
+    next = (next + 1) % 16;
     return true;
 }
 
@@ -617,9 +657,9 @@ int launch_fwd_bf16_sm100(int D, const void *q, const void *k, const void *v, vo
     if (D != 64) return set_error(ATTN_ERR_UNSUPPORTED, "tcgen05 forward: head_dim %d", D);
     if (((uintptr_t)q | (uintptr_t)k | (uintptr_t)v | (uintptr_t)o) & 15)
         return set_error(ATTN_ERR_INVALID, "tcgen05 forward: tensors must be 16-byte aligned");
-    CUtensorMap tq, tk, tv;
+    CUtensorMap tq, tk, tv, to;
     if (!cached_map(&tq, q, H * D, T, B, in_stride) || !cached_map(&tk, k, H * D, T, B, in_stride) ||
-        !cached_map(&tv, v, H * D, T, B, in_stride))
+        !cached_map(&tv, v, H * D, T, B, in_stride) || !cached_map(&to, o, H * D, T, B, out_stride, 32))
         return set_error(ATTN_ERR_CUDA, "tcgen05 forward: cuTensorMapEncodeTiled failed");
     int dev = 0;
     cudaGetDevice(&dev);
@@ -671,7 +711,7 @@ int launch_fwd_bf16_sm100(int D, const void *q, const void *k, const void *v, vo
     const size_t smem = Cfg<64>::SMEM;
     if (!ensure_smem_attr((const void *)fwd_kernel<64>, smem))
         return set_error(ATTN_ERR_CUDA, "tcgen05 forward: cannot set shared-memory size");
-    fwd_kernel<64><<<ctas, kThreads, smem, s>>>(tq, tk, tv, p);
+    fwd_kernel<64><<<ctas, kThreads, smem, s>>>(tq, tk, tv, to, p);
     return check_launch("tcgen05 forward kernel");
 }
 
