@@ -61,7 +61,7 @@ L2_BYTES = 126 * 2 ** 20
 # dram__bytes_read.sum + dram__bytes_write.sum per launch of the dominant
 # kernel, each from one ncu capture of that kernel at the config's size (the
 # backward: its two main kernels together); None where not captured
-TRAFFIC = {"c3-bf16": 51817984, "c4-f32": 2153309904, "c4-int8": 584853248, "c2": 52355072,
+TRAFFIC = {"c3-bf16": 52874496, "c4-f32": 2153309904, "c4-int8": 584853248, "c2": 52355072,
            "c5-f32": 2047872256}
 
 
