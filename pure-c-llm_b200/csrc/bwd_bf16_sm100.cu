@@ -7,8 +7,14 @@
 // P is rebuilt from the forward's lse; the row statistics (lse in base 2, D)
 // come from the shared rowdot pre-pass into the workspace.
 //
-// Two deterministic kernels (no atomics), each one CTA per 128-row tile of one
-// (batch, head), 12 warps: warp 0 TMA producer; warps 1 and 2 MMA issuers
+// Two deterministic kernels (no atomics).  A unit is one 128-row tile of one
+// (batch, head); each kernel is persistent, one CTA per SM walking its units
+// in snake order over the units sorted by descending cost.  The fixed tiles
+// of a unit go into one of two buffers, so the next unit's load while the
+// current unit runs, and the streamed-tile ring and every barrier phase run
+// on across units; the accumulators pass to the next unit once the
+// elementwise warps have read them out.  12 warps: warp 0 TMA producer;
+// warps 1 and 2 MMA issuers
 // (warp 1 the S/dP products, warp 2 the accumulations; warp-converged loops,
 // the elected lane issues); warp 3 idle; warps 4-7 and 8-11 two elementwise
 // warpgroups, one thread per TMEM lane (= one row of the CTA's tile), the
@@ -27,6 +33,7 @@
 #include "common.cuh"
 #include "sm100.cuh"
 
+#include <algorithm>
 #include <cudaTypedefs.h>
 #include <type_traits>
 
@@ -50,14 +57,20 @@ constexpr int TILE_BYTES = BT * D * 2;        // one 128 x 64 bf16 tile (16 KB)
 constexpr int TM_X = 0, TM_Y = 128, TM_A1 = 256, TM_A2 = 320, TM_W1 = 384, TM_W2 = 448, TM_COLS = 512;
 
 // barrier slots
-enum { B_FIX = 0, B_SF = 1, B_SE = 1 + kStages, B_XY = 1 + 2 * kStages, B_XYE, B_W, B_ACC, B_ST, B_COUNT };
+//   FIX/FE: fixed tiles of a buffer loaded / free (their unit's last X/Y products done);
+//   SF/SE: streamed stage loaded / free; XY: X, Y of a tile ready; XYE: read;
+//   W: bf16 operands written; ACC: a tile's accumulations done; ST: statistics
+//   staged; AF: the unit's accumulators read out
+enum { B_FIX = 0, B_SF = 2, B_SE = 2 + kStages, B_XY = 2 + 2 * kStages, B_XYE, B_W, B_ACC, B_ST, B_FE, B_AF = B_FE + 2,
+       B_COUNT };
 static_assert(B_COUNT * 8 <= 128, "barrier area");
 
 struct Params {
     void *out1, *out2;           // dkdv: dK, dV;  dq: dQ
     const float *lse2, *dvec;    // [B][H][T]
     long long out_stride;
-    int T, H, accumulate;
+    int T, H, B, accumulate;
+    int n_units;                 // B * H * tiles; unit u: tile rank u / (B*H), batch and head from u % (B*H)
     float scale_log2;            // log2(e) / sqrt(d)
     float ds_scale;              // 1 / sqrt(d)
     int *err;
@@ -106,9 +119,9 @@ bwd_kernel(const __grid_constant__ CUtensorMap m_a, const __grid_constant__ CUte
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
     uint8_t *sb = smem_raw + (base - raw);
-    // layout: fixed A, fixed B, stages x (C, D), row statistics, barriers
-    const uint32_t sA = base, sB = base + TILE_BYTES, sST = base + 2 * TILE_BYTES;
-    const int OFF_STATS = 2 * TILE_BYTES + kStages * 2 * TILE_BYTES;     // kStages x 2 x 128 floats
+    // layout: 2 buffers x fixed (A, B), stages x (C, D), row statistics, barriers
+    const uint32_t sF = base, sST = base + 4 * TILE_BYTES;
+    const int OFF_STATS = 4 * TILE_BYTES + kStages * 2 * TILE_BYTES;     // kStages x 2 x 128 floats
     float *stats = reinterpret_cast<float *>(sb + OFF_STATS);
     const int OFF_BAR = OFF_STATS + kStages * 2 * BT * 4;
     const uint32_t bar0 = base + OFF_BAR;
@@ -118,21 +131,34 @@ bwd_kernel(const __grid_constant__ CUtensorMap m_a, const __grid_constant__ CUte
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n_t = (p.T + BT - 1) / BT;
-    const int h = blockIdx.x, b = blockIdx.y;
-    // dkdv: key tile kt = z (small kt has the most query tiles: issued first);
-    // dq: query tile qt = n_t-1-z (large qt has the most key tiles)
-    const int fixed = KIND == 0 ? (int)blockIdx.z : n_t - 1 - (int)blockIdx.z;
-    const int first = KIND == 0 ? fixed : 0;                  // streamed tile range
-    const int count = KIND == 0 ? n_t - fixed : fixed + 1;
+    // Persistent: the CTA walks units k = 0, 1, ... in rounds of gridDim.x,
+    // snake order (round k takes position blockIdx.x, or gridDim.x-1-blockIdx.x
+    // when k is odd), over units ordered by descending cost.  Unit u: tile rank
+    // z = u / (B*H); dkdv: key tile kt = z (small kt has the most query tiles);
+    // dq: query tile qt = n_t-1-z (large qt has the most key tiles).
+    struct Unit { int h, b, fixed, first, count; };
+    auto unit_of = [&](int k, Unit &un) -> bool {
+        const int G = (int)gridDim.x;
+        const int u = k * G + ((k & 1) ? G - 1 - (int)blockIdx.x : (int)blockIdx.x);
+        if (u >= p.n_units) return false;
+        const int hb = p.H * p.B, z = u / hb, r = u - z * hb;
+        un.h = r % p.H;
+        un.b = r / p.H;
+        un.fixed = KIND == 0 ? z : n_t - 1 - z;
+        un.first = KIND == 0 ? un.fixed : 0;                  // streamed tile range
+        un.count = KIND == 0 ? n_t - un.fixed : un.fixed + 1;
+        return true;
+    };
 
     if (threadIdx.x == 0) {
-        mbar_init(BAR(B_FIX), 1);
+        for (int f = 0; f < 2; f++) { mbar_init(BAR(B_FIX + f), 1); mbar_init(BAR(B_FE + f), 1); }
         for (int s = 0; s < kStages; s++) { mbar_init(BAR(B_SF + s), 1); mbar_init(BAR(B_SE + s), 1); }
         mbar_init(BAR(B_XY), 1);
         mbar_init(BAR(B_XYE), 256);
         mbar_init(BAR(B_W), 256);
         mbar_init(BAR(B_ACC), 1);
         mbar_init(BAR(B_ST), 256);
+        mbar_init(BAR(B_AF), 256);
         *abort_flag = 0;
         fence_mbar_init();
     }
@@ -156,18 +182,29 @@ bwd_kernel(const __grid_constant__ CUtensorMap m_a, const __grid_constant__ CUte
             prefetch_tmap(&m_b);
             prefetch_tmap(&m_c);
             prefetch_tmap(&m_d);
-            mbar_arrive_expect_tx(BAR(B_FIX), 2 * TILE_BYTES);
-            tma_load_3d(sA, &m_a, BAR(B_FIX), h * D, fixed * BT, b);
-            tma_load_3d(sB, &m_b, BAR(B_FIX), h * D, fixed * BT, b);
-            for (int it = 0; it < count; it++) {
-                const int st = it % kStages;
-                if (it >= kStages &&
-                    !mbar_wait(BAR(B_SE + st), ((it / kStages) + 1) & 1, abort_flag, p.err, 0x301))
+            int g = 0;                               // streamed tiles issued (all units)
+            bool ok = true;
+            Unit un;
+            for (int k = 0; ok && unit_of(k, un); k++) {
+                // fixed tiles of unit k go to buffer k & 1, free once unit k-2's
+                // last X/Y products completed
+                const int fb = k & 1;
+                if (k >= 2 && !(ok = mbar_wait(BAR(B_FE + fb), ((k >> 1) + 1) & 1, abort_flag, p.err, 0x302)))
                     break;
-                mbar_arrive_expect_tx(BAR(B_SF + st), 2 * TILE_BYTES);
-                const uint32_t dst = sST + st * 2 * TILE_BYTES;
-                tma_load_3d(dst, &m_c, BAR(B_SF + st), h * D, (first + it) * BT, b);
-                tma_load_3d(dst + TILE_BYTES, &m_d, BAR(B_SF + st), h * D, (first + it) * BT, b);
+                const uint32_t fdst = sF + fb * 2 * TILE_BYTES;
+                mbar_arrive_expect_tx(BAR(B_FIX + fb), 2 * TILE_BYTES);
+                tma_load_3d(fdst, &m_a, BAR(B_FIX + fb), un.h * D, un.fixed * BT, un.b);
+                tma_load_3d(fdst + TILE_BYTES, &m_b, BAR(B_FIX + fb), un.h * D, un.fixed * BT, un.b);
+                for (int it = 0; it < un.count; it++, g++) {
+                    const int st = g % kStages;
+                    if (g >= kStages &&
+                        !(ok = mbar_wait(BAR(B_SE + st), ((g / kStages) + 1) & 1, abort_flag, p.err, 0x301)))
+                        break;
+                    mbar_arrive_expect_tx(BAR(B_SF + st), 2 * TILE_BYTES);
+                    const uint32_t dst = sST + st * 2 * TILE_BYTES;
+                    tma_load_3d(dst, &m_c, BAR(B_SF + st), un.h * D, (un.first + it) * BT, un.b);
+                    tma_load_3d(dst + TILE_BYTES, &m_d, BAR(B_SF + st), un.h * D, (un.first + it) * BT, un.b);
+                }
             }
         }
     } else if (warp == 1 || warp == 2) {
@@ -180,24 +217,32 @@ bwd_kernel(const __grid_constant__ CUtensorMap m_a, const __grid_constant__ CUte
         if (warp == 1) {
             constexpr uint32_t idXY = idesc_bf16(BT, BT, 0, 0);    // both operands K-major (along d)
             // X, Y for streamed tile `it`:  dkdv: X = K Q^T, Y = V dO^T;  dq: X = Q K^T, Y = dO V^T
-            bool ok = wait(B_FIX, 0, 0x311);
-            for (int it = 0; ok && it < count; it++) {
-                if (!(ok = wait(B_SF + it % kStages, it / kStages, 0x312))) break;
-                if (it > 0 && !(ok = wait(B_XYE, it - 1, 0x314))) break;   // X/Y of the previous tile read
-                tc_fence_after();
-                const uint32_t stg = sST + (it % kStages) * 2 * TILE_BYTES;
-                const uint64_t fa = sw128_desc(sA, 16, 1024), fb = sw128_desc(sB, 16, 1024);
-                const uint64_t sc = sw128_desc(stg, 16, 1024), sd = sw128_desc(stg + TILE_BYTES, 16, 1024);
-                if (leader) {
+            int g = 0;
+            bool ok = true;
+            Unit un;
+            for (int k = 0; ok && unit_of(k, un); k++) {
+                const int fbuf = k & 1;
+                if (!(ok = wait(B_FIX + fbuf, k >> 1, 0x311))) break;
+                const uint32_t fsrc = sF + fbuf * 2 * TILE_BYTES;
+                const uint64_t fa = sw128_desc(fsrc, 16, 1024), fb = sw128_desc(fsrc + TILE_BYTES, 16, 1024);
+                for (int it = 0; it < un.count; it++, g++) {
+                    if (!(ok = wait(B_SF + g % kStages, g / kStages, 0x312))) break;
+                    if (g > 0 && !(ok = wait(B_XYE, g - 1, 0x314))) break;   // X/Y of the previous tile read
+                    tc_fence_after();
+                    const uint32_t stg = sST + (g % kStages) * 2 * TILE_BYTES;
+                    const uint64_t sc = sw128_desc(stg, 16, 1024), sd = sw128_desc(stg + TILE_BYTES, 16, 1024);
+                    if (leader) {
 #pragma unroll
-                    for (int kk = 0; kk < D / 16; kk++)
-                        mma_bf16_ss(tmem + TM_X, fa + 2 * kk, sc + 2 * kk, idXY, kk > 0);
+                        for (int kk = 0; kk < D / 16; kk++)
+                            mma_bf16_ss(tmem + TM_X, fa + 2 * kk, sc + 2 * kk, idXY, kk > 0);
 #pragma unroll
-                    for (int kk = 0; kk < D / 16; kk++)
-                        mma_bf16_ss(tmem + TM_Y, fb + 2 * kk, sd + 2 * kk, idXY, kk > 0);
-                    mma_commit(BAR(B_XY));
+                        for (int kk = 0; kk < D / 16; kk++)
+                            mma_bf16_ss(tmem + TM_Y, fb + 2 * kk, sd + 2 * kk, idXY, kk > 0);
+                        mma_commit(BAR(B_XY));
+                        if (it == un.count - 1) mma_commit(BAR(B_FE + fbuf));   // the unit's fixed tiles are free
+                    }
+                    __syncwarp();
                 }
-                __syncwarp();
             }
         } else {
             constexpr uint32_t idAcc = idesc_bf16(BT, D, 0, 1);    // A from TMEM, B MN-major
@@ -205,10 +250,17 @@ bwd_kernel(const __grid_constant__ CUtensorMap m_a, const __grid_constant__ CUte
             //   dq:   A1 (dQ) += W2 (dS) . K_j
             // (tile it's X/Y products finished before its W was written, so this
             // warp's commit alone frees the stage)
-            for (int it = 0; it < count; it++) {
-                if (!wait(B_W, it, 0x315)) break;
+            int g = 0;
+            bool ok = true;
+            Unit un;
+            for (int k = 0; ok && unit_of(k, un); k++)
+            for (int it = 0; it < un.count; it++, g++) {
+                // the unit's first accumulation overwrites the accumulators: the
+                // previous unit's have been read out
+                if (it == 0 && k > 0 && !(ok = wait(B_AF, k - 1, 0x316))) break;
+                if (!(ok = wait(B_W, g, 0x315))) break;
                 tc_fence_after();
-                const uint32_t stg = sST + (it % kStages) * 2 * TILE_BYTES;
+                const uint32_t stg = sST + (g % kStages) * 2 * TILE_BYTES;
                 if (leader) {
                     if (KIND == 0) {
                         const uint64_t dq_ = sw128_desc(stg, 16384, 1024);                 // Q_i, MN-major
@@ -226,7 +278,7 @@ bwd_kernel(const __grid_constant__ CUtensorMap m_a, const __grid_constant__ CUte
                             mma_bf16_ts(tmem + TM_A1, tmem + TM_W2 + kk * 8, dk + 128 * kk, idAcc, it > 0 || kk > 0);
                     }
                     mma_commit(BAR(B_ACC));
-                    mma_commit(BAR(B_SE + it % kStages));     // streamed stage free
+                    mma_commit(BAR(B_SE + g % kStages));      // streamed stage free
                 }
                 __syncwarp();
             }
@@ -238,125 +290,134 @@ bwd_kernel(const __grid_constant__ CUtensorMap m_a, const __grid_constant__ CUte
         const int quad = warp & 3;
         const int row = quad * 32 + lane;            // TMEM lane = row of the CTA's fixed tile
         const uint32_t lb = (uint32_t)(quad * 32) << 16;
-        const long long bh = ((long long)b * p.H + h) * p.T;
-        const int grow_ = fixed * BT + row;          // global row index of this thread
-        float my_nl2 = 0.f, my_ndd = 0.f;            // dq: this query row's -lse2 and -D / sqrt(d)
-        if (KIND == 1 && grow_ < p.T) {
-            my_nl2 = -__ldg(p.lse2 + bh + grow_);
-            my_ndd = -__ldg(p.dvec + bh + grow_) * p.ds_scale;
-        }
         const uint64_t scale2 = f2(p.scale_log2, p.scale_log2), ds2 = f2(p.ds_scale, p.ds_scale);
         bool ok = true;
-        for (int it = 0; it < count; it++) {
-            const int tcol = first + it;             // streamed tile index
-            float *st_l = stats + (it % kStages) * 2 * BT;   // dkdv: lse2 / D of the query columns
-            if (KIND == 0) {
-                if (half == 0) {                     // staged as -lse2 and -D / sqrt(d)
-                    const int q = tcol * BT + row;
-                    st_l[row] = q < p.T ? -__ldg(p.lse2 + bh + q) : 0.f;
-                    st_l[BT + row] = q < p.T ? -__ldg(p.dvec + bh + q) * p.ds_scale : 0.f;
-                }
-                // the statistics are in shared memory before anyone reads them (an
-                // mbarrier with a bounded wait, so a warp that gave up on an earlier
-                // wait cannot leave the others blocked here)
-                mbar_arrive(BAR(B_ST));
-                if (!__all_sync(0xffffffffu, mbar_wait(BAR(B_ST), it & 1, abort_flag, p.err, 0x323))) {
-                    ok = false;
-                    break;
-                }
+        int g = 0;                                   // streamed tiles (all units)
+        Unit un;
+        for (int k = 0; ok && unit_of(k, un); k++) {
+            const int h = un.h, b = un.b, fixed = un.fixed, first = un.first, count = un.count;
+            const long long bh = ((long long)b * p.H + h) * p.T;
+            const int grow_ = fixed * BT + row;          // global row index of this thread
+            float my_nl2 = 0.f, my_ndd = 0.f;            // dq: this query row's -lse2 and -D / sqrt(d)
+            if (KIND == 1 && grow_ < p.T) {
+                my_nl2 = -__ldg(p.lse2 + bh + grow_);
+                my_ndd = -__ldg(p.dvec + bh + grow_) * p.ds_scale;
             }
-            ok = mbar_wait(BAR(B_XY), it & 1, abort_flag, p.err, 0x321);
-            if (it > 0 && ok) ok = mbar_wait(BAR(B_ACC), (it - 1) & 1, abort_flag, p.err, 0x322);
+            for (int it = 0; it < count; it++, g++) {
+                const int tcol = first + it;             // streamed tile index
+                float *st_l = stats + (g % kStages) * 2 * BT;   // dkdv: lse2 / D of the query columns
+                if (KIND == 0) {
+                    if (half == 0) {                     // staged as -lse2 and -D / sqrt(d)
+                        const int q = tcol * BT + row;
+                        st_l[row] = q < p.T ? -__ldg(p.lse2 + bh + q) : 0.f;
+                        st_l[BT + row] = q < p.T ? -__ldg(p.dvec + bh + q) * p.ds_scale : 0.f;
+                    }
+                    // the statistics are in shared memory before anyone reads them (an
+                    // mbarrier with a bounded wait, so a warp that gave up on an earlier
+                    // wait cannot leave the others blocked here)
+                    mbar_arrive(BAR(B_ST));
+                    if (!__all_sync(0xffffffffu, mbar_wait(BAR(B_ST), g & 1, abort_flag, p.err, 0x323))) {
+                        ok = false;
+                        break;
+                    }
+                }
+                ok = mbar_wait(BAR(B_XY), g & 1, abort_flag, p.err, 0x321);
+                if (g > 0 && ok) ok = mbar_wait(BAR(B_ACC), (g - 1) & 1, abort_flag, p.err, 0x322);
+                if (!(ok = __all_sync(0xffffffffu, ok))) break;
+                tc_fence_after();
+                const bool diag = (tcol == fixed);
+                // this half's 64 columns of X and Y in one round trip
+                uint32_t xs[64], ys[64];
+    #pragma unroll
+                for (int q2 = 0; q2 < 2; q2++) {
+                    uint32_t t0[32], t1[32];
+                    tmem_ld32(tmem + lb + TM_X + 64 * half + 32 * q2, t0);
+                    tmem_ld32(tmem + lb + TM_Y + 64 * half + 32 * q2, t1);
+    #pragma unroll
+                    for (int c = 0; c < 32; c++) {
+                        xs[32 * q2 + c] = t0[c];
+                        ys[32 * q2 + c] = t1[c];
+                    }
+                }
+                tmem_wait_ld();
+                tc_fence_before();
+                mbar_arrive(BAR(B_XYE));                 // X and Y read: the next products may start
+                // P = 2^(S scale - lse2), dS = P (dP - D) / sqrt(d), pairwise on f32x2;
+                // the mask (diagonal tile, or key/query columns past T) only where needed
+                const bool need_mask = diag || (KIND == 0 && tcol * BT + BT > p.T);
+                auto tile = [&](auto masked_tag) {
+                    constexpr bool MASKED = decltype(masked_tag)::value;
+    #pragma unroll
+                    for (int q2 = 0; q2 < 2; q2++) {
+                        uint32_t wp[16], wd[16];
+    #pragma unroll
+                        for (int c = 0; c < 32; c += 2) {
+                            const int cc = 32 * q2 + c;      // column within this half
+                            const int col = 64 * half + cc;
+                            uint64_t nl2, ndd;
+                            if (KIND == 0) {                 // row = key, col = query
+                                nl2 = *reinterpret_cast<const uint64_t *>(st_l + col);
+                                ndd = *reinterpret_cast<const uint64_t *>(st_l + BT + col);
+                            } else {                         // row = query, col = key
+                                nl2 = f2(my_nl2, my_nl2);
+                                ndd = f2(my_ndd, my_ndd);
+                            }
+                            const uint64_t xa2 = fma2(f2(__uint_as_float(xs[cc]), __uint_as_float(xs[cc + 1])), scale2, nl2);
+                            // kPolyPairs of every 8 pairs on the FMA pipe, the rest on MUFU
+                            float pv[2];
+                            if (((cc >> 1) & 7) < kPolyPairs) {
+                                f2_split(exp2_poly2(xa2), pv[0], pv[1]);
+                            } else {
+                                float a0, a1;
+                                f2_split(xa2, a0, a1);
+                                pv[0] = ex2(a0);
+                                pv[1] = ex2(a1);
+                            }
+                            if (MASKED) {
+    #pragma unroll
+                                for (int u = 0; u < 2; u++) {
+                                    const int cu = col + u;
+                                    const bool m = KIND == 0 ? ((diag && cu < row) || (tcol * BT + cu >= p.T))
+                                                             : (diag && cu > row);
+                                    if (m) pv[u] = 0.f;
+                                }
+                            }
+                            const uint64_t pv2 = f2(pv[0], pv[1]);
+                            const uint64_t t2 = fma2(f2(__uint_as_float(ys[cc]), __uint_as_float(ys[cc + 1])), ds2, ndd);
+                            float d0, d1;
+                            f2_split(fma2(pv2, t2, 0ull), d0, d1);
+                            wp[c / 2] = pack_bf16(pv[0], pv[1]);
+                            wd[c / 2] = pack_bf16(d0, d1);
+                        }
+                        if (KIND == 0) tmem_st16(tmem + lb + TM_W1 + 32 * half + 16 * q2, wp);
+                        tmem_st16(tmem + lb + TM_W2 + 32 * half + 16 * q2, wd);
+                    }
+                };
+                if (need_mask) tile(std::true_type{});
+                else tile(std::false_type{});
+                tmem_wait_st();
+                tc_fence_before();
+                mbar_arrive(BAR(B_W));
+            }
+            if (!ok) break;
+            // epilogue: this half's 32 columns of each accumulator -> global; the
+            // accumulators are released to the next unit as soon as they are read
+            ok = mbar_wait(BAR(B_ACC), (g - 1) & 1, abort_flag, p.err, 0x324);
             if (!(ok = __all_sync(0xffffffffu, ok))) break;
             tc_fence_after();
-            const bool diag = (tcol == fixed);
-            // this half's 64 columns of X and Y in one round trip
-            uint32_t xs[64], ys[64];
-#pragma unroll
-            for (int q2 = 0; q2 < 2; q2++) {
-                uint32_t t0[32], t1[32];
-                tmem_ld32(tmem + lb + TM_X + 64 * half + 32 * q2, t0);
-                tmem_ld32(tmem + lb + TM_Y + 64 * half + 32 * q2, t1);
-#pragma unroll
-                for (int c = 0; c < 32; c++) {
-                    xs[32 * q2 + c] = t0[c];
-                    ys[32 * q2 + c] = t1[c];
-                }
-            }
+            uint32_t acc[2][32];
+            tmem_ld32(tmem + lb + TM_A1 + 32 * half, acc[0]);
+            if (KIND == 0) tmem_ld32(tmem + lb + TM_A2 + 32 * half, acc[1]);
             tmem_wait_ld();
             tc_fence_before();
-            mbar_arrive(BAR(B_XYE));                 // X and Y read: the next products may start
-            // P = 2^(S scale - lse2), dS = P (dP - D) / sqrt(d), pairwise on f32x2;
-            // the mask (diagonal tile, or key/query columns past T) only where needed
-            const bool need_mask = diag || (KIND == 0 && tcol * BT + BT > p.T);
-            auto tile = [&](auto masked_tag) {
-                constexpr bool MASKED = decltype(masked_tag)::value;
-#pragma unroll
-                for (int q2 = 0; q2 < 2; q2++) {
-                    uint32_t wp[16], wd[16];
-#pragma unroll
-                    for (int c = 0; c < 32; c += 2) {
-                        const int cc = 32 * q2 + c;      // column within this half
-                        const int col = 64 * half + cc;
-                        uint64_t nl2, ndd;
-                        if (KIND == 0) {                 // row = key, col = query
-                            nl2 = *reinterpret_cast<const uint64_t *>(st_l + col);
-                            ndd = *reinterpret_cast<const uint64_t *>(st_l + BT + col);
-                        } else {                         // row = query, col = key
-                            nl2 = f2(my_nl2, my_nl2);
-                            ndd = f2(my_ndd, my_ndd);
-                        }
-                        const uint64_t xa2 = fma2(f2(__uint_as_float(xs[cc]), __uint_as_float(xs[cc + 1])), scale2, nl2);
-                        // kPolyPairs of every 8 pairs on the FMA pipe, the rest on MUFU
-                        float pv[2];
-                        if (((cc >> 1) & 7) < kPolyPairs) {
-                            f2_split(exp2_poly2(xa2), pv[0], pv[1]);
-                        } else {
-                            float a0, a1;
-                            f2_split(xa2, a0, a1);
-                            pv[0] = ex2(a0);
-                            pv[1] = ex2(a1);
-                        }
-                        if (MASKED) {
-#pragma unroll
-                            for (int u = 0; u < 2; u++) {
-                                const int cu = col + u;
-                                const bool m = KIND == 0 ? ((diag && cu < row) || (tcol * BT + cu >= p.T))
-                                                         : (diag && cu > row);
-                                if (m) pv[u] = 0.f;
-                            }
-                        }
-                        const uint64_t pv2 = f2(pv[0], pv[1]);
-                        const uint64_t t2 = fma2(f2(__uint_as_float(ys[cc]), __uint_as_float(ys[cc + 1])), ds2, ndd);
-                        float d0, d1;
-                        f2_split(fma2(pv2, t2, 0ull), d0, d1);
-                        wp[c / 2] = pack_bf16(pv[0], pv[1]);
-                        wd[c / 2] = pack_bf16(d0, d1);
-                    }
-                    if (KIND == 0) tmem_st16(tmem + lb + TM_W1 + 32 * half + 16 * q2, wp);
-                    tmem_st16(tmem + lb + TM_W2 + 32 * half + 16 * q2, wd);
-                }
-            };
-            if (need_mask) tile(std::true_type{});
-            else tile(std::false_type{});
-            tmem_wait_st();
-            tc_fence_before();
-            mbar_arrive(BAR(B_W));
-        }
-        // epilogue: this half's 32 columns of each accumulator -> global
-        if (ok && count > 0) ok = mbar_wait(BAR(B_ACC), (count - 1) & 1, abort_flag, p.err, 0x323);
-        if (__all_sync(0xffffffffu, ok && count > 0)) {
-            tc_fence_after();
-            for (int a = 0; a < (KIND == 0 ? 2 : 1); a++) {
-                uint32_t acc[32];
-                tmem_ld32(tmem + lb + (a ? TM_A2 : TM_A1) + 32 * half, acc);
-                tmem_wait_ld();
-                if (grow_ < p.T) {
+            mbar_arrive(BAR(B_AF));
+            if (grow_ < p.T) {
+                for (int a = 0; a < (KIND == 0 ? 2 : 1); a++) {
                     // dkdv: a=0 -> dV (out2), a=1 -> dK (out1);  dq: dQ (out1)
                     void *outp = KIND == 0 ? (a == 0 ? p.out2 : p.out1) : p.out1;
                     __nv_bfloat16 *dst = static_cast<__nv_bfloat16 *>(outp) +
                                          ((long long)b * p.T + grow_) * p.out_stride + (long long)h * D + 32 * half;
-                    store_row_bf16<32>(dst, acc, p.accumulate != 0);
+                    store_row_bf16<32>(dst, acc[a], p.accumulate != 0);
                 }
             }
         }
@@ -375,7 +436,7 @@ bwd_kernel(const __grid_constant__ CUtensorMap m_a, const __grid_constant__ CUte
 }
 
 constexpr int smem_bytes() {
-    return 2 * TILE_BYTES + kStages * 2 * TILE_BYTES + kStages * 2 * BT * 4 + 256 + 1024;
+    return 4 * TILE_BYTES + kStages * 2 * TILE_BYTES + kStages * 2 * BT * 4 + 256 + 1024;
 }
 
 }  // namespace fab
@@ -451,6 +512,7 @@ int launch_bwd_bf16_sm100(int D, const void *dout, const void *q, const void *k,
     p.out_stride = out_stride;
     p.T = T;
     p.H = H;
+    p.B = B;
     p.accumulate = accumulate;
     p.scale_log2 = attn::kLog2e / sqrtf((float)D);
     p.ds_scale = 1.0f / sqrtf((float)D);
@@ -459,7 +521,16 @@ int launch_bwd_bf16_sm100(int D, const void *dout, const void *q, const void *k,
     if (!ensure_smem_attr((const void *)bwd_kernel<0>, smem) || !ensure_smem_attr((const void *)bwd_kernel<1>, smem))
         return set_error(ATTN_ERR_CUDA, "tcgen05 backward: cannot set shared-memory size");
     const int n_t = (T + BT - 1) / BT;
-    dim3 grid(H, B, n_t);
+    const long long n_units = (long long)B * H * n_t;
+    if (n_units > (1LL << 30)) return set_error(ATTN_ERR_INVALID, "tcgen05 backward: too many tiles");
+    p.n_units = (int)n_units;
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    static int sm_count[128] = {0};
+    if (dev < 0 || dev >= 128) return set_error(ATTN_ERR_INVALID, "tcgen05 backward: device %d", dev);
+    if (!sm_count[dev] && cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess)
+        sm_count[dev] = sms;
+    const int grid = (int)std::min<long long>(sm_count[dev] ? sm_count[dev] : 148, n_units);   // persistent
     p.out1 = dk;
     p.out2 = dv;
     bwd_kernel<0><<<grid, kThreads, smem, s>>>(mk, mv, mq, mdo, p);     // fixed K, V; streamed Q, dO
