@@ -62,7 +62,7 @@ L2_BYTES = 126 * 2 ** 20
 # kernel, each from one ncu capture of that kernel at the config's size (the
 # backward: its two main kernels together); None where not captured
 TRAFFIC = {"c3-bf16": 52874496, "c4-f32": 2153309904, "c4-int8": 584853248, "c2": 52355072,
-           "c5-f32": 2047872256}
+           "c5-f32": 2047872256, "c5-bf16": 458164992, "c3-f32": 131287552}
 
 
 def causal_flops(B, H, T, d):
