@@ -84,10 +84,14 @@ struct Cfg {
     static constexpr int TM_COLS = QT || TM_A + D > 256 ? 512 : 256;
     // per-thread registers after setmaxnreg: warpgroup 0, splitters, softmax
     // (two CTAs per SM: 384 x 80 at launch = 128 x (40 + 56 + 144); one CTA:
-    // 384 x 160 at launch >= 128 x (64 + 160 + 160))
+    // 384 x 168 at launch >= 128 x (64 + 160 + 232), or 128 x (64 + 200 + 232)
+    // at d = 96).  ptxas allocates each role's code within its budget, so
+    // these are the sizes at which the roles compile without spills.
     static constexpr int REG_MMA = CTAS == 2 ? 40 : 64;
-    static constexpr int REG_SPLIT = CTAS == 2 ? 56 : 160;
-    static constexpr int REG_SOFT = CTAS == 2 ? 144 : 160;
+    static constexpr int REG_SPLIT = CTAS == 2 ? 56 : (D == 96 ? 200 : 160);
+    static constexpr int REG_SOFT = CTAS == 2 ? 144 : 232;
+    static_assert(CTAS == 2 ? REG_MMA + REG_SPLIT + REG_SOFT <= 3 * 80 : REG_MMA + REG_SPLIT + REG_SOFT <= 3 * 168,
+                  "register split exceeds the launch allocation");
     static_assert(TM_O + D <= TM_COLS && (!ACC_TMEM || TM_A + D <= TM_COLS), "TMEM budget");
     static_assert(TM_COLS * CTAS <= 512, "TMEM budget per SM");
 };
@@ -369,7 +373,8 @@ fwd_tf32_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
             }
         } else if (warp >= 4) {
             // -------------------------------------------------------- splitters
-            regs_dec<C::REG_SPLIT>();
+            if constexpr (C::REG_SPLIT > 168) regs_inc<C::REG_SPLIT>();   // d = 96 (launched with 168)
+            else regs_dec<C::REG_SPLIT>();
             const int tid = threadIdx.x - 128;
             float *qh = reinterpret_cast<float *>(sb + C::OFF_QH), *ql = reinterpret_cast<float *>(sb + C::OFF_QL);
             int t = 0;
@@ -449,7 +454,7 @@ fwd_tf32_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
         }
     } else {
         // ------------------------------------------------------------ softmax
-        if (C::CTAS == 2) regs_inc<C::REG_SOFT>();   // (one CTA per SM: the launch allocation suffices)
+        regs_inc<C::REG_SOFT>();
         const int quad = warp & 3;
         const int row = quad * 32 + lane;
         const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
