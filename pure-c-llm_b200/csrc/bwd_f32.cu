@@ -50,6 +50,53 @@ __global__ void bwd_rowdot_kernel(const BwdParams p)
     }
 }
 
+// The same statistics, one block per 32 consecutive rows of one (batch, head):
+// 8 threads per row, each reading D/8 contiguous elements of O and dO with
+// 8-byte loads (a row's 8 threads cover it in one contiguous segment), a
+// 3-step shuffle sum, and coalesced writes of the 32 rows' D and lse2 (which
+// are laid out [B][H][T]).  Needs 8-byte aligned rows.
+template <typename T, int D>
+__global__ void __launch_bounds__(256) bwd_rowdot_tile_kernel(const BwdParams p)
+{
+    static_assert(D % 32 == 0, "8 threads x a multiple of 4 elements per row");
+    constexpr int EP = D / 8;                        // elements per thread
+    const int row = threadIdx.x >> 3, part = threadIdx.x & 7;
+    const int t = (int)blockIdx.x * 32 + row, h = (int)blockIdx.y, b = (int)blockIdx.z;
+    float acc = 0.f;
+    if (t < p.T) {
+        const long long bt = (long long)b * p.T + t;
+        const T *o = static_cast<const T *>(p.o) + bt * p.out_stride + (long long)h * D + part * EP;
+        const T *g = static_cast<const T *>(p.dout) + bt * p.in_stride + (long long)h * D + part * EP;
+        if constexpr (sizeof(T) == 4) {
+#pragma unroll
+            for (int c = 0; c < EP; c += 2) {
+                const float2 x = __ldg(reinterpret_cast<const float2 *>(o + c));
+                const float2 y = __ldg(reinterpret_cast<const float2 *>(g + c));
+                acc = fmaf(x.x, y.x, acc);
+                acc = fmaf(x.y, y.y, acc);
+            }
+        } else {
+#pragma unroll
+            for (int c = 0; c < EP; c += 4) {           // 4 bf16 = two 32-bit words
+                const uint2 x = __ldg(reinterpret_cast<const uint2 *>(o + c));
+                const uint2 y = __ldg(reinterpret_cast<const uint2 *>(g + c));
+                acc = fmaf(__uint_as_float(x.x << 16), __uint_as_float(y.x << 16), acc);
+                acc = fmaf(__uint_as_float(x.x & 0xffff0000u), __uint_as_float(y.x & 0xffff0000u), acc);
+                acc = fmaf(__uint_as_float(x.y << 16), __uint_as_float(y.y << 16), acc);
+                acc = fmaf(__uint_as_float(x.y & 0xffff0000u), __uint_as_float(y.y & 0xffff0000u), acc);
+            }
+        }
+    }
+    acc += __shfl_xor_sync(0xffffffffu, acc, 4);
+    acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+    acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+    if (part == 0 && t < p.T) {
+        const long long r = ((long long)b * p.H + h) * p.T + t;
+        p.dvec[r] = acc;
+        p.lse2[r] = p.lse[r] * kLog2e;
+    }
+}
+
 template <int D> struct BwdCfg {
     static constexpr int NBUF = D <= 96 ? 2 : 1;   // double-buffer streamed tiles when smem allows
 };
@@ -289,6 +336,22 @@ namespace attn_host {
 
 bool ensure_smem_attr(const void *func, size_t bytes);
 
+// Row statistics through the tiled kernel when the rows are 8-byte aligned,
+// else through the warp-per-row kernel.
+template <typename T, int D>
+static int launch_rowdot_t(const attn::BwdParams &p, cudaStream_t s) {
+    const bool aligned = ((((uintptr_t)p.o | (uintptr_t)p.dout) & 7) == 0) &&
+                         (p.in_stride * (long long)sizeof(T)) % 8 == 0 && (p.out_stride * (long long)sizeof(T)) % 8 == 0;
+    if (aligned && p.H <= 65535 && p.B <= 65535) {
+        const dim3 grid((unsigned)((p.T + 31) / 32), (unsigned)p.H, (unsigned)p.B);
+        attn::bwd_rowdot_tile_kernel<T, D><<<grid, 256, 0, s>>>(p);
+    } else {
+        const long long rows = (long long)p.B * p.T * p.H;
+        attn::bwd_rowdot_kernel<T, D><<<(unsigned)((rows + 7) / 8), 256, 0, s>>>(p);
+    }
+    return check_launch("bwd_rowdot_kernel");
+}
+
 // Row statistics for any backward: lse2 = lse * log2(e) and D = dO . O per
 // (b, h, t), into the workspace (shared with the tensor-core backward).
 int launch_bwd_rowdot(int dtype, int D, const void *o, const void *dout, const float *lse, float *ws,
@@ -299,17 +362,14 @@ int launch_bwd_rowdot(int dtype, int D, const void *o, const void *dout, const f
     p.dvec = ws + (long long)B * H * T;
     p.in_stride = in_stride; p.out_stride = out_stride;
     p.B = B; p.H = H; p.T = T;
-    const long long rows = (long long)B * T * H;
-    const unsigned grid = (unsigned)((rows + 7) / 8);
     const bool bf = dtype == ATTN_BF16;
     switch (D) {
-        case 32: bf ? attn::bwd_rowdot_kernel<__nv_bfloat16, 32><<<grid, 256, 0, s>>>(p) : attn::bwd_rowdot_kernel<float, 32><<<grid, 256, 0, s>>>(p); break;
-        case 64: bf ? attn::bwd_rowdot_kernel<__nv_bfloat16, 64><<<grid, 256, 0, s>>>(p) : attn::bwd_rowdot_kernel<float, 64><<<grid, 256, 0, s>>>(p); break;
-        case 96: bf ? attn::bwd_rowdot_kernel<__nv_bfloat16, 96><<<grid, 256, 0, s>>>(p) : attn::bwd_rowdot_kernel<float, 96><<<grid, 256, 0, s>>>(p); break;
-        case 128: bf ? attn::bwd_rowdot_kernel<__nv_bfloat16, 128><<<grid, 256, 0, s>>>(p) : attn::bwd_rowdot_kernel<float, 128><<<grid, 256, 0, s>>>(p); break;
+        case 32: return bf ? launch_rowdot_t<__nv_bfloat16, 32>(p, s) : launch_rowdot_t<float, 32>(p, s);
+        case 64: return bf ? launch_rowdot_t<__nv_bfloat16, 64>(p, s) : launch_rowdot_t<float, 64>(p, s);
+        case 96: return bf ? launch_rowdot_t<__nv_bfloat16, 96>(p, s) : launch_rowdot_t<float, 96>(p, s);
+        case 128: return bf ? launch_rowdot_t<__nv_bfloat16, 128>(p, s) : launch_rowdot_t<float, 128>(p, s);
         default: return set_error(ATTN_ERR_UNSUPPORTED, "bwd: head_dim %d", D);
     }
-    return check_launch("bwd_rowdot_kernel");
 }
 
 size_t bwd_f32_workspace_bytes(int B, int H, int T) {
@@ -326,9 +386,7 @@ static int launch_bwd_f32_t(const attn::BwdParams &p, cudaStream_t s) {
     if (!ensure_smem_attr((const void *)bwd_dkdv_kernel<T, D>, smem_kv) ||
         !ensure_smem_attr((const void *)bwd_dq_kernel<T, D>, smem_q))
         return set_error(ATTN_ERR_CUDA, "bwd_f32: cannot set shared-memory size");
-    const long long rows = (long long)p.B * p.T * p.H;
-    bwd_rowdot_kernel<T, D><<<(unsigned)((rows + 7) / 8), 256, 0, s>>>(p);
-    int st = check_launch("bwd_rowdot_kernel");
+    int st = launch_rowdot_t<T, D>(p, s);
     if (st) return st;
     dim3 grid((p.T + kFBM - 1) / kFBM, p.H, p.B);
     bwd_dkdv_kernel<T, D><<<grid, kFThreads, smem_kv, s>>>(p);
