@@ -168,6 +168,44 @@ def test_backward_bf16_vs_fp32_oracle(A, B, T, H, d):
     assert rel_err(host(dv), rv) < BF16_BWD_TOL
 
 
+@pytest.mark.parametrize("dt,pad_in,pad_out", [("f32", 4, 8), ("bf16", 4, 12)])
+def test_backward_padded_rows(A, dt, pad_in, pad_out):
+    """Rows wider than H*d (strides a multiple of 4 elements, as the C ABI
+    requires; at bf16 an input stride that is not a multiple of 8 keeps the
+    call off the tensor-core kernels): the row statistics and the gradients
+    read and write only the first H*d columns of each row."""
+    import torch
+    B, T, H, d = 1, 130, 2, 32
+    q, k, v = qkv(23, B, T, H, d)
+    do = synth.normal(24, (B * T, H * d))
+    tdt, code, tol = (torch.float32, A.F32, F32_TOL) if dt == "f32" else (torch.bfloat16, A.BF16, BF16_BWD_TOL)
+    if dt == "bf16":
+        q, k, v, do = (bf16_round(x) for x in (q, k, v, do))
+    _, probs, _ = O.attn_forward(q, k, v, B, T, H, d, want_probs=True)
+    rq, rk, rv = O.attn_backward(do, q, k, v, probs, B, T, H, d)
+    wi, wo = H * d + pad_in, H * d + pad_out
+
+    def padded(x, w):
+        t = torch.zeros((B * T, w), dtype=tdt, device="cuda")
+        t[:, :H * d] = torch.as_tensor(x, device="cuda").to(tdt)
+        return t
+
+    qd, kd, vd, gd = (padded(x, wi) for x in (q, k, v, do))
+    od = torch.zeros((B * T, wo), dtype=tdt, device="cuda")
+    lse = torch.zeros(B * H * T, device="cuda")
+    shape = A.Shape(B, H, T, d, wi, wo)
+    A.fwd_ex(shape, code, qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), od.data_ptr(), lse.data_ptr())
+    grads = [torch.zeros((B * T, wo), dtype=tdt, device="cuda") for _ in range(3)]
+    ws_bytes = A.bwd_workspace_bytes(shape, code)
+    ws = torch.zeros(ws_bytes, dtype=torch.uint8, device="cuda")
+    A.bwd_ex(shape, code, gd.data_ptr(), qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), od.data_ptr(), lse.data_ptr(),
+             grads[0].data_ptr(), grads[1].data_ptr(), grads[2].data_ptr(), 0, ws.data_ptr(), ws_bytes)
+    torch.cuda.synchronize()
+    for g, r in zip(grads, (rq, rk, rv)):
+        assert rel_err(host(g[:, :H * d]), r) < tol
+        assert not (g[:, H * d:] != 0).any()     # the padding columns stay untouched
+
+
 def test_backward_deterministic_and_workspace_check(A):
     import torch
     q, k, v = qkv(8, 1, 150, 2, 64)
