@@ -328,13 +328,16 @@ class Workload:
     def setup_e2e(self):
         torch = self.torch
         kind = self.cfg["kind"]
-        self.e2e_pipe = kind in ("fwd", "bwd")
+        self.e2e_pipe = kind in ("fwd", "bwd", "ragged")
         if self.e2e_pipe:
             # Every step copies its inputs in from pinned host memory and its
             # results out; consecutive steps overlap (H2D, the call and D2H on
             # three streams) over two sets of device and host buffers.
-            self.e2e_in = ["q", "k", "v"] + (["do", "o", "lse"] if kind == "bwd" else [])
-            self.e2e_out = ["o"] if kind == "fwd" else ["dq", "dk", "dv"]
+            if kind == "ragged":                     # the query rows in, the outputs back
+                self.e2e_in, self.e2e_out = ["q"], ["o"]
+            else:
+                self.e2e_in = ["q", "k", "v"] + (["do", "o", "lse"] if kind == "bwd" else [])
+                self.e2e_out = ["o"] if kind == "fwd" else ["dq", "dk", "dv"]
             base = {a: getattr(self, a) for a in self.e2e_in + self.e2e_out}
             self.e2e_sets = [base, {a: torch.empty_like(t) for a, t in base.items()}]
             for a in self.e2e_in:                    # both sets hold the same input values
