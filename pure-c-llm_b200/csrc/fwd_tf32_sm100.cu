@@ -83,13 +83,13 @@ struct Cfg {
     static constexpr int TM_A = TM_O + D;
     static constexpr int TM_COLS = QT || TM_A + D > 256 ? 512 : 256;
     // per-thread registers after setmaxnreg: warpgroup 0, splitters, softmax
-    // (two CTAs per SM: 384 x 80 at launch = 128 x (40 + 56 + 144); one CTA:
+    // (two CTAs per SM: 384 x 80 at launch = 128 x (32 + 56 + 152); one CTA:
     // 384 x 168 at launch >= 128 x (64 + 160 + 232), or 128 x (64 + 200 + 232)
     // at d = 96).  ptxas allocates each role's code within its budget, so
     // these are the sizes at which the roles compile without spills.
-    static constexpr int REG_MMA = CTAS == 2 ? 40 : 64;
+    static constexpr int REG_MMA = CTAS == 2 ? 32 : 64;
     static constexpr int REG_SPLIT = CTAS == 2 ? 56 : (D == 96 ? 200 : 160);
-    static constexpr int REG_SOFT = CTAS == 2 ? 144 : 232;
+    static constexpr int REG_SOFT = CTAS == 2 ? 152 : 232;
     static_assert(CTAS == 2 ? REG_MMA + REG_SPLIT + REG_SOFT <= 3 * 80 : REG_MMA + REG_SPLIT + REG_SOFT <= 3 * 168,
                   "register split exceeds the launch allocation");
     static_assert(TM_O + D <= TM_COLS && (!ACC_TMEM || TM_A + D <= TM_COLS), "TMEM budget");
