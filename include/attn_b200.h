@@ -47,8 +47,10 @@ enum {
     ATTN_ERR_CUDA = 3,         /* a CUDA runtime/driver call failed            */
     ATTN_ERR_NOMEM = 4,        /* device allocation failed                     */
     ATTN_ERR_WORKSPACE = 5,    /* caller workspace smaller than required       */
-    ATTN_ERR_DEVICE = 6        /* a kernel reported an internal error (bounded
+    ATTN_ERR_DEVICE = 6,       /* a kernel reported an internal error (bounded
                                   wait expired); see attn_device_error()       */
+    ATTN_ERR_COMM = 7          /* a collective failed or a group wait timed
+                                  out; the group has been torn down           */
 };
 
 /* element types of activations / caches */
@@ -236,6 +238,100 @@ ATTN_API int attn_shard_lpt(const int *lens, int n_seq, int heads, int world,
 ATTN_API int attn_gather_permute(const void *staging, void *out, int world, int batch,
                         int seq_len, int heads, int head_dim, int dtype,
                         attn_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Multi-GPU groups (no counterpart in the reference, whose trainer drives one
+ * GPU from one host process, train_kaggle.cu:346).  NCCL over NVLink is used
+ * only to gather outputs for callers that need them whole; the attention
+ * itself needs no collective.  NCCL is loaded at run time (libnccl.so.2, or
+ * the path in $ATTN_NCCL_LIB); NCCL_NVLS_ENABLE defaults to 0.  One group per
+ * process.
+ * ---------------------------------------------------------------------- */
+/* One host thread drives devices 0..ngpus-1 (ncclCommInitAll); use
+ * attn_fwd_multi / attn_decode_multi. */
+ATTN_API int attn_init(int ngpus);
+/* One process per GPU: rank 0 makes a 128-byte id, the caller hands it to
+ * every rank, and each joins with attn_init_rank on `device` (-1: the current
+ * device); then use the ordinary entry points on the rank's share and
+ * attn_gather_split / attn_gather_rows. */
+ATTN_API int attn_get_unique_id(unsigned char id[128]);
+ATTN_API int attn_init_rank(int nranks, int rank, int device, const unsigned char id[128]);
+/* Destroys the group's communicators (after the caller's work on them is done). */
+ATTN_API int attn_finalize(void);
+/* Ranks in the group, 0 when there is none. */
+ATTN_API int attn_group_size(void);
+/* Host-side watchdog: waits until every listed stream is idle, polling the
+ * communicators' asynchronous errors.  On a communicator error, or when the
+ * streams are still busy after timeout_ms, it aborts every communicator
+ * (ncclCommAbort), removes the group and returns ATTN_ERR_COMM. */
+ATTN_API int attn_group_sync(const attn_stream_t *streams, int n_streams, int timeout_ms);
+
+/* A rank's share of the (batch x head) units: nb x nh ranks tile the batch and
+ * head ranges evenly, with as many ranks along the batch as divide it (whole
+ * batches keep a rank's rows contiguous).  Rank r holds batches
+ * [batch0, batch0 + batch) and heads [head0, head0 + heads). */
+typedef struct {
+    int batch0, batch, head0, heads;
+    int nb, nh;
+} attn_split;
+ATTN_API int attn_split_plan(int batch, int heads, int nranks, int rank, attn_split *out);
+
+/* Bytes of workspace attn_gather_split / attn_fwd_multi need per rank for a
+ * gather of this shape (0 when the split is by whole batches). */
+ATTN_API size_t attn_gather_workspace_bytes(const attn_shape *s, int dtype, int nranks);
+/* One-process-per-rank group: `local` is this rank's forward output, dense
+ * (batch*T rows of heads*d, its split of `s`, the full shape); writes the
+ * whole (B*T, H*d) output `out` on every rank (all-gather, then a permute
+ * kernel when ranks split the heads). */
+ATTN_API int attn_gather_split(const attn_shape *s, int dtype, const void *local, void *out,
+                               void *workspace, size_t workspace_bytes, attn_stream_t stream);
+
+/* Ragged decode across ranks: each rank decodes its own sequences (for
+ * example by attn_shard_lpt with heads = 1) into `local`, max_local rows of
+ * row_bytes (a multiple of 16).  attn_gather_rows all-gathers every rank's
+ * max_local rows and writes row i of the gathered [nranks][max_local] block to
+ * out row order[i] (a DEVICE array; < 0 skips padding).  order == NULL: the
+ * gathered block is the output (n_out = nranks * max_local). */
+ATTN_API size_t attn_gather_rows_workspace_bytes(int max_local, size_t row_bytes, int nranks);
+ATTN_API int attn_gather_rows(const void *local, int max_local, size_t row_bytes, const int *order,
+                              int n_out, void *out, void *workspace, size_t workspace_bytes,
+                              attn_stream_t stream);
+
+/* attn_init group, one host thread: device g holds the full-size inputs
+ * q[g], k[g], v[g] (shape `s`) and runs its split (attn_split_plan with
+ * rank g) into o[g] at the split's rows and columns; lse[g] (may be NULL)
+ * receives its split's [batch][heads][T] statistics.  gather = 1 completes
+ * o[g] on every device (NCCL all-gather on streams[g]; dense output rows
+ * needed); ws[g] / ws_bytes[g] as attn_gather_workspace_bytes. */
+ATTN_API int attn_fwd_multi(const attn_shape *s, int dtype, const void *const *q,
+                            const void *const *k, const void *const *v, void *const *o,
+                            float *const *lse, int gather, void *const *ws,
+                            const size_t *ws_bytes, const attn_stream_t *streams);
+/* attn_init group, one host thread: device g decodes its own sequences
+ * (shapes[g], its caches and lens, out[g] with max_local rows); gather = 1
+ * then writes every device's rows into out_full[g] (n_total rows, 16-byte
+ * aligned) by order[g] (as attn_gather_rows), with ws[g] of
+ * attn_gather_rows_workspace_bytes(max_local, H*d*4, ngpus) bytes. */
+ATTN_API int attn_decode_multi(const attn_decode_shape *shapes, const float *const *q,
+                               const void *const *kcache, const void *const *vcache,
+                               const float *const *kscale, const float *const *vscale,
+                               const int *const *lens, float *const *out, int gather,
+                               int max_local, const int *const *order, int n_total,
+                               float *const *out_full, void *const *ws,
+                               const size_t *ws_bytes, const attn_stream_t *streams);
+
+/* ------------------------------------------------------------------------
+ * Test hook (no counterpart in the reference)
+ * ---------------------------------------------------------------------- */
+/* The next `launches` fp32 decode calls served by the single-pass decode
+ * kernel (few sequences, small total cache) make one of its warps wait on a
+ * barrier that nothing arrives at, bounded by `limit_cycles` SM cycles
+ * (>= 1000).  The wait runs out and the kernel takes its timeout path: it
+ * records code 0x32f in the device error word (attn_device_error), stops,
+ * lets the copies it has in flight land, and returns; the call's output is
+ * undefined and later calls run normally.  For tests of failure detection:
+ * no GPU fault is involved. */
+ATTN_API int attn_debug_decode_timeout(int launches, long long limit_cycles);
 
 #ifdef __cplusplus
 }

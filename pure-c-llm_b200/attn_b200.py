@@ -13,7 +13,7 @@ import os
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libattn_b200.so")
 
-OK, ERR_INVALID, ERR_UNSUPPORTED, ERR_CUDA, ERR_NOMEM, ERR_WORKSPACE, ERR_DEVICE = range(7)
+OK, ERR_INVALID, ERR_UNSUPPORTED, ERR_CUDA, ERR_NOMEM, ERR_WORKSPACE, ERR_DEVICE, ERR_COMM = range(8)
 F32, BF16, I8 = 0, 1, 2
 MAX_LAYERS = 64
 STATIC_SCRATCH_BYTES = 4 << 20      # ATTN_DECODE_STATIC_SCRATCH_BYTES
@@ -49,6 +49,11 @@ class KVCache(ctypes.Structure):
                 ("kscale", ctypes.c_void_p * MAX_LAYERS), ("vscale", ctypes.c_void_p * MAX_LAYERS)]
 
 
+class Split(ctypes.Structure):
+    _fields_ = [("batch0", ctypes.c_int), ("batch", ctypes.c_int), ("head0", ctypes.c_int),
+                ("heads", ctypes.c_int), ("nb", ctypes.c_int), ("nh", ctypes.c_int)]
+
+
 P = ctypes.c_void_p
 I = ctypes.c_int
 LL = ctypes.c_longlong
@@ -77,6 +82,20 @@ SIGNATURES = {
     "attn_shard_range": (I, [LL, I, I, ctypes.POINTER(LL), ctypes.POINTER(LL)]),
     "attn_shard_lpt": (I, [P, I, I, I, P, P]),
     "attn_gather_permute": (I, [P, P, I, I, I, I, I, I, P]),
+    "attn_debug_decode_timeout": (I, [I, LL]),
+    "attn_init": (I, [I]),
+    "attn_get_unique_id": (I, [P]),
+    "attn_init_rank": (I, [I, I, I, P]),
+    "attn_finalize": (I, []),
+    "attn_group_size": (I, []),
+    "attn_group_sync": (I, [P, I, I]),
+    "attn_split_plan": (I, [I, I, I, I, ctypes.POINTER(Split)]),
+    "attn_gather_workspace_bytes": (SZ, [ctypes.POINTER(Shape), I, I]),
+    "attn_gather_split": (I, [ctypes.POINTER(Shape), I, P, P, P, SZ, P]),
+    "attn_gather_rows_workspace_bytes": (SZ, [I, SZ, I]),
+    "attn_gather_rows": (I, [P, I, SZ, P, I, P, P, SZ, P]),
+    "attn_fwd_multi": (I, [ctypes.POINTER(Shape), I, P, P, P, P, P, I, P, P, P]),
+    "attn_decode_multi": (I, [ctypes.POINTER(DecodeShape), P, P, P, P, P, P, P, I, I, P, I, P, P, P, P]),
 }
 for _name, (_res, _args) in SIGNATURES.items():
     _f = getattr(lib, _name)
@@ -121,6 +140,12 @@ def shard_range(n_units: int, world: int, rank: int):
     b, e = LL(), LL()
     check(lib.attn_shard_range(n_units, world, rank, ctypes.byref(b), ctypes.byref(e)))
     return b.value, e.value
+
+
+def split_plan(batch: int, heads: int, nranks: int, rank: int) -> Split:
+    sp = Split()
+    check(lib.attn_split_plan(batch, heads, nranks, rank, ctypes.byref(sp)))
+    return sp
 
 
 def shard_lpt(lens, heads: int, world: int):

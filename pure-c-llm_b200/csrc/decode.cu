@@ -552,6 +552,7 @@ size_t decode_stream_ws_bytes(int n_seq, int heads, int head_dim, int max_len);
 bool decode_stream_shape_ok(int heads, int head_dim, int kv_dtype);
 size_t decode_i8mma_ws_bytes(int n_seq, int heads, int head_dim, int max_len);
 bool decode_i8mma_shape_ok(int heads, int head_dim, int kv_dtype);
+size_t decode_ring_ws_bytes(int n_seq, int heads, int head_dim);
 
 static size_t decode_split_ws_bytes(int n_seq, int heads, int head_dim, int max_len, int kv_dtype) {
     if (rows_i8_ok(heads, head_dim, kv_dtype)) {
@@ -580,6 +581,7 @@ static size_t decode_split_ws_bytes(int n_seq, int heads, int head_dim, int max_
 // split kernels.
 size_t decode_workspace_bytes(int n_seq, int heads, int head_dim, int max_len, int kv_dtype) {
     size_t b = decode_split_ws_bytes(n_seq, heads, head_dim, max_len, kv_dtype);
+    if (kv_dtype == ATTN_F32) b = std::max(b, decode_ring_ws_bytes(n_seq, heads, head_dim));
     if (decode_stream_shape_ok(heads, head_dim, kv_dtype))
         b = std::max(b, decode_stream_ws_bytes(n_seq, heads, head_dim, max_len));
     if (decode_i8mma_shape_ok(heads, head_dim, kv_dtype))
@@ -676,8 +678,12 @@ int launch_decode_stream(const DecodeLaunch &L);
 bool decode_i8mma_ok(const DecodeLaunch &L);
 int launch_decode_i8mma(const DecodeLaunch &L);
 
+bool decode_ring_ok(const DecodeLaunch &L);
+int launch_decode_ring(const DecodeLaunch &L);
+
 int launch_decode(const DecodeLaunch &L) {
     const bool i8 = L.kv_dtype == ATTN_I8;
+    if (decode_ring_ok(L)) return launch_decode_ring(L);
     if (decode_i8mma_ok(L)) return launch_decode_i8mma(L);
     if (decode_stream_ok(L)) return launch_decode_stream(L);
     if (rows_i8_ok(L.heads, L.head_dim, L.kv_dtype)) return launch_rows_i8(L);

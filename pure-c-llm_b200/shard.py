@@ -1,53 +1,71 @@
-"""Multi-GPU partition of the attention work by (batch x head) units.
+"""Python client of the library's multi-GPU entry points (one process per GPU).
 
-One process per GPU (torch.distributed supplies ranks and NCCL).  Attention
-has no cross-unit exchange, so the compute path needs no collective: each
-rank runs the kernels on its own head slice.  Only a caller that needs the
-whole output gets one all-gather, into a [world][B][T][H/world][d] staging
-buffer, followed by attn_gather_permute into the (B*T, H*d) layout.
-
-The split plans come from the C ABI (attn_shard_range for contiguous head or
-unit ranges, attn_shard_lpt for ragged decode units weighted by cache length).
+The split and the gathers live in the C library (csrc/group.cu):
+attn_split_plan says which (batch x head) units a rank computes,
+attn_shard_lpt balances ragged decode sequences, attn_init_rank joins the
+library's own NCCL communicator, and attn_gather_split / attn_gather_rows
+assemble whole outputs.  This module only moves the 128-byte communicator id
+between ranks (over whatever torch.distributed group the caller already
+has) and wraps tensors as pointers for the tests and the benchmark.
 """
+import ctypes
+
 import numpy as np
 
 import attn_b200 as A
 
 
-def head_range(heads: int, world: int, rank: int):
-    """Heads [h0, h1) of this rank; equal slices when world divides heads."""
-    return A.shard_range(heads, world, rank)
+def split(B: int, H: int, world: int, rank: int) -> A.Split:
+    return A.split_plan(B, H, world, rank)
 
 
-def permute_staging_np(staging, world, B, T, H, d):
-    """numpy mirror of attn_gather_permute: [G][B][T][H/G][d] -> (B*T, H*d)."""
-    s = np.asarray(staging).reshape(world, B, T, H // world, d)
-    return s.transpose(1, 2, 0, 3, 4).reshape(B * T, H * d)
-
-
-def forward_head_shard(q, k, v, B, H, T, d, world, rank):
-    """Runs this rank's head slice on the GPU; returns the compact (B*T, Hr*d)
-    output and lse [B][Hr][T].  q/k/v are this rank's full-width CUDA tensors."""
-    import torch
-    h0, h1 = head_range(H, world, rank)
-    hn = h1 - h0
-    out = torch.empty((B * T, hn * d), dtype=q.dtype, device=q.device)
-    lse = torch.empty(B * hn * T, dtype=torch.float32, device=q.device)
-    shape = A.Shape(B, hn, T, d, q.stride(0), hn * d)
-    esz = q.element_size()
-    off = h0 * d * esz
-    A.fwd_ex(shape, A.BF16 if esz == 2 else A.F32, q.data_ptr() + off, k.data_ptr() + off, v.data_ptr() + off,
-             out.data_ptr(), lse.data_ptr(), torch.cuda.current_stream().cuda_stream)
-    return out, lse
-
-
-def gather_heads(local_out, B, H, T, d, world, group=None):
-    """All-gathers equal head shards and permutes them to (B*T, H*d)."""
+def init_group(rank: int, world: int, device: int):
+    """Joins the library's NCCL group: rank 0 makes the id, torch.distributed
+    broadcasts it (any backend), every rank calls attn_init_rank."""
     import torch
     import torch.distributed as dist
-    rows, cols = local_out.shape
-    staging = torch.empty((world * rows, cols), dtype=local_out.dtype, device=local_out.device)
-    dist.all_gather_into_tensor(staging, local_out.contiguous(), group=group)
-    if staging.is_cuda:
-        return A.gather_permute_t(staging.reshape(-1, d), world, B, T, H, d)
-    return torch.from_numpy(permute_staging_np(staging.numpy(), world, B, T, H, d))
+    uid = (ctypes.c_ubyte * 128)()
+    if rank == 0:
+        A.check(A.lib.attn_get_unique_id(uid))
+    backend = dist.get_backend()
+    t = torch.tensor(list(bytes(uid)), dtype=torch.uint8,
+                     device=f"cuda:{device}" if backend == "nccl" else "cpu")
+    dist.broadcast(t, 0)
+    uid = (ctypes.c_ubyte * 128)(*t.cpu().tolist())
+    A.check(A.lib.attn_init_rank(world, rank, device, uid))
+
+
+def local_inputs(full, sp: A.Split, T: int, d: int):
+    """This rank's compact (batch*T, heads*d) slice of a full (B*T, H*d) tensor."""
+    rows = slice(sp.batch0 * T, (sp.batch0 + sp.batch) * T)
+    cols = slice(sp.head0 * d, (sp.head0 + sp.heads) * d)
+    return full[rows, cols].contiguous()
+
+
+def gather_split(local, B: int, H: int, T: int, d: int, out=None, stream=None):
+    """Whole (B*T, H*d) output on every rank from each rank's compact split."""
+    import torch
+    dt = A.BF16 if local.dtype == torch.bfloat16 else A.F32
+    shape = A.Shape(B, H, T, d, 0, 0)
+    out = torch.empty((B * T, H * d), dtype=local.dtype, device=local.device) if out is None else out
+    nbytes = A.lib.attn_gather_workspace_bytes(ctypes.byref(shape), dt, A.lib.attn_group_size())
+    ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=local.device)
+    s = torch.cuda.current_stream().cuda_stream if stream is None else stream
+    A.check(A.lib.attn_gather_split(ctypes.byref(shape), dt, local.data_ptr(), out.data_ptr(), ws.data_ptr(),
+                                    nbytes, s))
+    return out
+
+
+def permute_grid_np(staging, plans, B, T, H, d):
+    """numpy mirror of the gather's permute: staging [nranks][batch*T][heads*d]
+    (rank r's compact split) -> (B*T, H*d)."""
+    out = np.empty((B * T, H * d), dtype=staging.dtype)
+    for r, p in enumerate(plans):
+        out[p.batch0 * T:(p.batch0 + p.batch) * T, p.head0 * d:(p.head0 + p.heads) * d] = staging[r]
+    return out
+
+
+def lpt_sequences(lens, world: int):
+    """Sequences per rank (attn_shard_lpt with one unit per sequence)."""
+    ranks, load = A.shard_lpt(lens, 1, world)
+    return [np.flatnonzero(ranks == r) for r in range(world)], load

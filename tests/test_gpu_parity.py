@@ -272,8 +272,11 @@ def test_cached_attention_golden(A, name):
         assert rel_err(host(out), z["out"][i]) < F32_TOL
 
 
+# (24, 32, ...) and d 96 take the split kernels, the others the single-pass
+# kernel for small calls; (16, 64, 8, 3000) splits one sequence over ~40 CTAs.
 @pytest.mark.parametrize("H,d,n_seq,max_len", [(16, 64, 8, 3000), (16, 32, 5, 700), (4, 128, 3, 1500),
-                                               (2, 96, 4, 257), (16, 64, 2, 1)])
+                                               (2, 96, 4, 257), (16, 64, 2, 1), (24, 32, 3, 500),
+                                               (8, 128, 1, 5000), (1, 32, 200, 37)])
 def test_ragged_decode_f32_vs_oracle(A, H, d, n_seq, max_len):
     import torch
     lens = synth.uniform_int(H * d + n_seq, n_seq, 1, max_len)
@@ -375,6 +378,60 @@ def test_decode_caller_workspace_and_reuse(A):
     assert np.array_equal(outs[0], outs[1]) and np.array_equal(outs[1], outs[2])
     ref = O.cached_attention(q[1], kc[max_len:2 * max_len], vc[max_len:2 * max_len], int(lens[1]) - 1, H, d)
     assert rel_err(outs[0][1], ref) < F32_TOL
+
+
+def test_decode_padded_rows_and_dirty_workspace(A):
+    """Cache rows padded past H*d (row copies one by one) and a caller workspace
+    full of stale bytes: the merge tickets carry the call's generation, so old
+    contents never count."""
+    import torch
+    H, d, n_seq, max_len, pad = 16, 32, 3, 900, 16
+    lens = synth.uniform_int(77, n_seq, 1, max_len)
+    lens[1] = max_len
+    kc = synth.normal(91, (n_seq * max_len, H * d + pad))
+    vc = synth.normal(92, (n_seq * max_len, H * d + pad))
+    q = synth.normal(93, (n_seq, H * d))
+    kd, vd = dev(kc)[:, :H * d], dev(vc)[:, :H * d]
+    shape = A.DecodeShape(n_seq, H, d, A.F32, H * d + pad, max_len, max_len)
+    ws = torch.full((A.decode_workspace_bytes(shape),), 0xFF, dtype=torch.uint8, device="cuda")
+    for _ in range(2):
+        out = A.decode_t(dev(q), kd, vd, dev(lens), H, max_len, max_len, workspace=ws)
+        torch.cuda.synchronize()
+        for s_ in range(n_seq):
+            ref = O.cached_attention(q[s_], kc[s_ * max_len:(s_ + 1) * max_len, :H * d],
+                                     vc[s_ * max_len:(s_ + 1) * max_len, :H * d], int(lens[s_]) - 1, H, d)
+            assert rel_err(host(out)[s_], ref) < F32_TOL, s_
+        ws.random_(0, 256)
+
+
+def test_decode_bounded_wait_timeout_path(A):
+    """Failure detection without a fault: a test hook makes one warp of the
+    single-pass decode kernel wait on a barrier nothing arrives at.  The
+    bounded wait runs out, the kernel records its code in the device error
+    word, lets its in-flight copies land and returns; the next call is
+    correct and leaves the error word clear."""
+    import torch
+    H, d, n_seq, max_len = 16, 32, 16, 640
+    lens = np.full(n_seq, max_len, np.int32)
+    kc = synth.normal(94, (n_seq * max_len, H * d))
+    vc = synth.normal(95, (n_seq * max_len, H * d))
+    q = synth.normal(96, (n_seq, H * d))
+    qd, kd, vd, ld = dev(q), dev(kc), dev(vc), dev(lens)
+    code = ctypes.c_int()
+    A.check(A.lib.attn_device_error(0, ctypes.byref(code)))       # clear
+    A.check(A.lib.attn_debug_decode_timeout(1, 200000))
+    A.decode_t(qd, kd, vd, ld, H, max_len, max_len)
+    torch.cuda.synchronize()
+    A.check(A.lib.attn_device_error(0, ctypes.byref(code)))
+    assert code.value == 0x32f
+    out = A.decode_t(qd, kd, vd, ld, H, max_len, max_len)
+    torch.cuda.synchronize()
+    A.check(A.lib.attn_device_error(0, ctypes.byref(code)))
+    assert code.value == 0
+    for s_ in (0, 7, 15):
+        ref = O.cached_attention(q[s_], kc[s_ * max_len:(s_ + 1) * max_len], vc[s_ * max_len:(s_ + 1) * max_len],
+                                 max_len - 1, H, d)
+        assert rel_err(host(out)[s_], ref) < F32_TOL
 
 
 def test_decode_bad_length_sets_device_error_word(A):
