@@ -192,6 +192,29 @@ ATTN_API int attn_cached_attention(const float *q, const float *kcache, const fl
                           float *out, int pos, int heads, int head_dim,
                           long long row_stride, attn_stream_t stream);
 
+/* cached_attention (transformer.c:203-248) with its own argument list and
+ * HOST pointers: a drop-in for the call at transformer.c:266 (forward_block).
+ * q, out: H*d floats; kcache/vcache: the caller's host cache, T_MAX rows of
+ * H*d floats (transformer.h:35-38 shapes, or attn_set_decode_macro_shape);
+ * `scores` is accepted and unused.  The library keeps a device mirror of each
+ * (kcache, vcache) pair and copies over only the rows it has not seen -- the
+ * generator writes row `pos` before attending (transformer.c:256-264) -- then
+ * decodes on the GPU and writes `out` before returning.  A call with a pos
+ * below the mirrored length re-sends rows from pos on; rows below pos must not
+ * change once sent.  Exits(1) with a message on failure. */
+ATTN_API void attn_cached_attention_host(const float *q, const float *kcache, const float *vcache,
+                                         float *out, float *scores, int pos);
+/* Shapes of attn_cached_attention_host (defaults: transformer.h:35-38,
+ * N_HEADS 16, D_HEAD 96, T_MAX 512; rows of heads*head_dim floats). */
+ATTN_API int attn_set_decode_macro_shape(int heads, int head_dim, int t_max);
+/* The same with explicit shapes and a status (generate.c:130-152 works with
+ * run-time dims: H, DH, row stride D, BLK rows). */
+ATTN_API int attn_cached_attention_host_ex(const float *q, const float *kcache, const float *vcache,
+                                           float *out, int pos, int heads, int head_dim,
+                                           long long row_stride, int cap);
+/* Frees the device mirror of a host cache pair. */
+ATTN_API int attn_host_cache_release(const float *kcache, const float *vcache);
+
 /* INT8 quantiser for caches: the reference's symmetric absmax scheme
  * (gemm_bench.c:225-236: amax floored at 1e-8, scale = amax/127,
  * q = lroundf(x/scale) clamped to +-127) applied per (row, head).

@@ -83,6 +83,10 @@ SIGNATURES = {
     "attn_shard_lpt": (I, [P, I, I, I, P, P]),
     "attn_gather_permute": (I, [P, P, I, I, I, I, I, I, P]),
     "attn_debug_decode_timeout": (I, [I, LL]),
+    "attn_cached_attention_host": (None, [P, P, P, P, P, I]),
+    "attn_set_decode_macro_shape": (I, [I, I, I]),
+    "attn_cached_attention_host_ex": (I, [P, P, P, P, I, I, I, LL, I]),
+    "attn_host_cache_release": (I, [P, P]),
     "attn_init": (I, [I]),
     "attn_get_unique_id": (I, [P]),
     "attn_init_rank": (I, [I, I, I, P]),

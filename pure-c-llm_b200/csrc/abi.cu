@@ -7,7 +7,9 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <functional>
 #include <map>
+#include <tuple>
 #include <mutex>
 #include <queue>
 #include <utility>
@@ -95,6 +97,71 @@ bool ensure_smem_attr(const void *func, size_t bytes) {
     if (cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) != cudaSuccess)
         return false;
     done[key] = bytes;
+    return true;
+}
+
+// Per-device cache of the persistent kernels' schedules (per-CTA item lists),
+// one immutable device buffer per (kernel, shape) key.  A buffer is written
+// once, synchronously on a private stream, before its first use and never
+// again, so calls of different shapes may overlap on any streams.  The first
+// call of a new shape allocates and uploads (keep it out of stream capture).
+// After kMaxSchedules shapes on a device, the callers fall back to their
+// list-free static schedule.
+const unsigned short *schedule_get(int kernel_tag, long long key,
+                                   const std::function<void(std::vector<unsigned short> &)> &build) {
+    constexpr size_t kMaxSchedules = 256;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+    static std::map<std::tuple<int, int, long long>, unsigned short *> cache;
+    static std::map<int, cudaStream_t> upload_stream;
+    std::lock_guard<std::mutex> lk(g_mu);
+    const auto k = std::make_tuple(dev, kernel_tag, key);
+    auto it = cache.find(k);
+    if (it != cache.end()) return it->second;
+    if (cache.size() >= kMaxSchedules * 8) return nullptr;
+    size_t on_dev = 0;
+    for (auto &e : cache) on_dev += std::get<0>(e.first) == dev;
+    if (on_dev >= kMaxSchedules) return nullptr;
+    std::vector<unsigned short> h;
+    build(h);
+    cudaStream_t &us = upload_stream[dev];
+    if (!us && cudaStreamCreateWithFlags(&us, cudaStreamNonBlocking) != cudaSuccess) return nullptr;
+    unsigned short *d = nullptr;
+    if (cudaMalloc(&d, h.size() * sizeof(unsigned short)) != cudaSuccess) return nullptr;
+    if (cudaMemcpyAsync(d, h.data(), h.size() * sizeof(unsigned short), cudaMemcpyHostToDevice, us) != cudaSuccess ||
+        cudaStreamSynchronize(us) != cudaSuccess) {
+        cudaFree(d);
+        return nullptr;
+    }
+    cache[k] = d;
+    return d;
+}
+
+// SM count of the current device, cached.
+int sm_count_here() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+    static std::map<int, int> counts;
+    std::lock_guard<std::mutex> lk(g_mu);
+    auto it = counts.find(dev);
+    if (it != counts.end()) return it->second;
+    int sms = 148;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    counts[dev] = sms;
+    return sms;
+}
+
+// Sets a kernel's preferred shared-memory carveout once per device.
+bool ensure_carveout(const void *func, int percent) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return false;
+    static std::map<std::pair<const void *, int>, int> done;
+    std::lock_guard<std::mutex> lk(g_mu);
+    auto key = std::make_pair(func, dev);
+    if (done.count(key)) return true;
+    if (cudaFuncSetAttribute(func, cudaFuncAttributePreferredSharedMemoryCarveout, percent) != cudaSuccess)
+        return false;
+    done[key] = percent;
     return true;
 }
 
@@ -238,6 +305,14 @@ int attn_bwd_ex(const attn_shape *s, int dtype, const void *dO, const void *Q, c
 }
 
 // ---- macro-shaped drop-ins (gpu_kernels.h:67-72) ---------------------------
+}  // extern "C"
+namespace attn_host {
+void dropin_fwd(const float *Q, const float *K, const float *V, float *att, float *probs);
+void dropin_bwd(float *dQ, float *dK, float *dV, float *scratch, const float *dAtt, const float *Q,
+                const float *K, const float *V, const float *probs);
+}  // namespace attn_host
+extern "C" {
+
 static attn_shape g_macro = {ATTN_B_SIZE, ATTN_N_HEADS, ATTN_T_SIZE, ATTN_D_HEAD, 0, 0};
 
 int attn_set_macro_shape(int batch, int heads, int seq_len, int head_dim) {
@@ -259,6 +334,22 @@ static void die_on(int st, const char *where) {
 }
 
 void attn_fwd(const float *Q, const float *K, const float *V, float *att, float *probs) {
+    attn_host::dropin_fwd(Q, K, V, att, probs);
+}
+
+void attn_bwd(float *dQ, float *dK, float *dV, float *scratch, const float *dAtt, const float *Q,
+              const float *K, const float *V, const float *probs) {
+    attn_host::dropin_bwd(dQ, dK, dV, scratch, dAtt, Q, K, V, probs);
+}
+
+}  // extern "C"
+
+namespace attn_host {
+
+// Bodies of the drop-ins, shared by the C symbols above and the C++-linkage
+// symbols of abi_cxx.cu (train_kaggle.cu and gpu_kernels.h are compiled as
+// CUDA C++, so an unchanged trainer references the mangled names).
+void dropin_fwd(const float *Q, const float *K, const float *V, float *att, float *probs) {
     const attn_shape &s = g_macro;
     if (s.seq_len < s.head_dim + 1) die_on(set_error(ATTN_ERR_UNSUPPORTED, "T < d+1"), "attn_fwd");
     // probs layout: [lse: B*H*T][copy of att: B*T*H*d]
@@ -270,8 +361,8 @@ void attn_fwd(const float *Q, const float *K, const float *V, float *att, float 
     if (e != cudaSuccess) die_on(set_error(ATTN_ERR_CUDA, "%s", cudaGetErrorString(e)), "attn_fwd");
 }
 
-void attn_bwd(float *dQ, float *dK, float *dV, float *scratch, const float *dAtt, const float *Q,
-              const float *K, const float *V, const float *probs) {
+void dropin_bwd(float *dQ, float *dK, float *dV, float *scratch, const float *dAtt, const float *Q,
+                const float *K, const float *V, const float *probs) {
     const attn_shape &s = g_macro;
     const float *lse = probs;
     const float *ocopy = probs + (size_t)s.batch * s.heads * s.seq_len;
@@ -279,6 +370,10 @@ void attn_bwd(float *dQ, float *dK, float *dV, float *scratch, const float *dAtt
     die_on(attn_bwd_ex(&s, ATTN_F32, dAtt, Q, K, V, ocopy, lse, dQ, dK, dV, 0, scratch, ws_bytes, nullptr),
            "attn_bwd");
 }
+
+}  // namespace attn_host
+
+extern "C" {
 
 // ---------------------------------------------------------------------------
 // decode

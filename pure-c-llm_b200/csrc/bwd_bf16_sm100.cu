@@ -34,6 +34,8 @@
 #include "sm100.cuh"
 
 #include <algorithm>
+#include <functional>
+#include <vector>
 #include <cudaTypedefs.h>
 #include <type_traits>
 
@@ -448,6 +450,10 @@ constexpr int smem_bytes() {
 namespace attn_host {
 
 bool ensure_smem_attr(const void *func, size_t bytes);
+const unsigned short *schedule_get(int kernel_tag, long long key,
+                                   const std::function<void(std::vector<unsigned short> &)> &build);
+int sm_count_here();
+bool ensure_carveout(const void *func, int percent);
 int launch_bwd_rowdot(int dtype, int D, const void *o, const void *dout, const float *lse, float *ws,
                       long long in_stride, long long out_stride, int B, int H, int T, cudaStream_t s);
 
@@ -524,13 +530,7 @@ int launch_bwd_bf16_sm100(int D, const void *dout, const void *q, const void *k,
     const long long n_units = (long long)B * H * n_t;
     if (n_units > (1LL << 30)) return set_error(ATTN_ERR_INVALID, "tcgen05 backward: too many tiles");
     p.n_units = (int)n_units;
-    int dev = 0, sms = 148;
-    cudaGetDevice(&dev);
-    static int sm_count[128] = {0};
-    if (dev < 0 || dev >= 128) return set_error(ATTN_ERR_INVALID, "tcgen05 backward: device %d", dev);
-    if (!sm_count[dev] && cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess)
-        sm_count[dev] = sms;
-    const int grid = (int)std::min<long long>(sm_count[dev] ? sm_count[dev] : 148, n_units);   // persistent
+    const int grid = (int)std::min<long long>(sm_count_here(), n_units);   // persistent
     p.out1 = dk;
     p.out2 = dv;
     bwd_kernel<0><<<grid, kThreads, smem, s>>>(mk, mv, mq, mdo, p);     // fixed K, V; streamed Q, dO

@@ -43,6 +43,7 @@
 #include "sm100.cuh"
 
 #include <algorithm>
+#include <functional>
 #include <cudaTypedefs.h>
 #include <vector>
 
@@ -573,6 +574,10 @@ fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
 namespace attn_host {
 
 bool ensure_smem_attr(const void *func, size_t bytes);
+const unsigned short *schedule_get(int kernel_tag, long long key,
+                                   const std::function<void(std::vector<unsigned short> &)> &build);
+int sm_count_here();
+bool ensure_carveout(const void *func, int percent);
 
 static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -661,18 +666,8 @@ int launch_fwd_bf16_sm100(int D, const void *q, const void *k, const void *v, vo
     if (!cached_map(&tq, q, H * D, T, B, in_stride) || !cached_map(&tk, k, H * D, T, B, in_stride) ||
         !cached_map(&tv, v, H * D, T, B, in_stride) || !cached_map(&to, o, H * D, T, B, out_stride, 32))
         return set_error(ATTN_ERR_CUDA, "tcgen05 forward: cuTensorMapEncodeTiled failed");
-    int dev = 0;
-    cudaGetDevice(&dev);
-    static int sm_count[128] = {0};
-    if (dev < 0 || dev >= 128) return set_error(ATTN_ERR_INVALID, "tcgen05 forward: device %d", dev);
-    if (!sm_count[dev]) {
-        int sms = 148;
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        sm_count[dev] = sms;
-    }
-    // The per-CTA item lists live in a small per-device buffer, rewritten only
-    // when the shape or the CTA count changes (calls on one device are
-    // expected to come from one host thread, like the reference's trainer).
+    // The per-CTA item lists live in an immutable per-(shape, CTA count)
+    // device buffer from the library's schedule cache.
     Params p;
     p.o = static_cast<__nv_bfloat16 *>(o);
     p.lse = lse;
@@ -684,29 +679,14 @@ int launch_fwd_bf16_sm100(int D, const void *q, const void *k, const void *v, vo
     p.n_items = p.n_pairs * H * B;
     p.scale_log2 = attn::kLog2e / sqrtf((float)D);
     p.err = err;
-    const int ctas = std::max(1, std::min(std::min(sm_count[dev], kMaxCtas), p.n_items));
+    const int ctas = std::max(1, std::min(std::min(sm_count_here(), kMaxCtas), p.n_items));
     p.use_list = p.n_items <= kMaxItems;
     p.packable = B < 4096 && H < 1024 && p.n_pairs < 1024;
     p.sched = nullptr;
     if (p.use_list) {
-        static unsigned short *sched_buf[128] = {nullptr};
-        static long long sched_key[128];
         const long long key = (((long long)T * 4096 + H) * 65536 + B) * 256 + ctas;
-        if (!sched_buf[dev]) {
-            if (cudaMalloc(&sched_buf[dev], (kMaxCtas + 1 + kMaxItems) * sizeof(unsigned short)) != cudaSuccess)
-                return set_error(ATTN_ERR_NOMEM, "tcgen05 forward: cannot allocate the schedule buffer");
-            sched_key[dev] = -1;
-        }
-        if (key != sched_key[dev]) {
-            std::vector<unsigned short> h;
-            lpt_schedule(p, ctas, h);
-            if (cudaMemcpyAsync(sched_buf[dev], h.data(), h.size() * sizeof(unsigned short),
-                                cudaMemcpyHostToDevice, s) != cudaSuccess ||
-                cudaStreamSynchronize(s) != cudaSuccess)
-                return set_error(ATTN_ERR_CUDA, "tcgen05 forward: schedule upload failed");
-            sched_key[dev] = key;
-        }
-        p.sched = sched_buf[dev];
+        p.sched = schedule_get(1, key, [&](std::vector<unsigned short> &h) { lpt_schedule(p, ctas, h); });
+        p.use_list = p.sched != nullptr;            // a full cache: the list-free static schedule
     }
     const size_t smem = Cfg<64>::SMEM;
     if (!ensure_smem_attr((const void *)fwd_kernel<64>, smem))

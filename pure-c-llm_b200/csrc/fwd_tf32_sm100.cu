@@ -645,6 +645,10 @@ fwd_tf32_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
 namespace attn_host {
 
 bool ensure_smem_attr(const void *func, size_t bytes);
+const unsigned short *schedule_get(int kernel_tag, long long key,
+                                   const std::function<void(std::vector<unsigned short> &)> &build);
+int sm_count_here();
+bool ensure_carveout(const void *func, int percent);
 
 static PFN_cuTensorMapEncodeTiled_v12000 encode_fn_t() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -721,15 +725,6 @@ static int launch_tf32_t(const void *q, const void *k, const void *v, void *o, f
     if (!cached_map_f32(&mq, q, H * D, T, B, in_stride, BM) || !cached_map_f32(&mk, k, H * D, T, B, in_stride, Cg::BN) ||
         !cached_map_f32(&mv, v, H * D, T, B, in_stride, Cg::BN))
         return set_error(ATTN_ERR_CUDA, "3xTF32 forward: cuTensorMapEncodeTiled failed");
-    int dev = 0;
-    cudaGetDevice(&dev);
-    static int sm_count[128] = {0};
-    if (dev < 0 || dev >= 128) return set_error(ATTN_ERR_INVALID, "3xTF32 forward: device %d", dev);
-    if (!sm_count[dev]) {
-        int sms = 148;
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        sm_count[dev] = sms;
-    }
     Params p;
     p.o = static_cast<float *>(o);
     p.lse = lse;
@@ -744,41 +739,20 @@ static int launch_tf32_t(const void *q, const void *k, const void *v, void *o, f
     p.bn = Cg::BN;
     p.scale_log2 = attn::kLog2e / sqrtf((float)D);
     p.err = err;
-    const int ctas = std::max(1, std::min(std::min(Cg::CTAS * sm_count[dev], kMaxCtas), p.n_items));
+    const int ctas = std::max(1, std::min(std::min(Cg::CTAS * sm_count_here(), kMaxCtas), p.n_items));
     p.use_list = p.n_items <= kMaxItems;
     p.packable = B < 4096 && H < 1024 && p.n_qt < 1024;
     p.sched = nullptr;
     if (p.use_list) {
-        static unsigned short *sched_buf[128][4] = {{nullptr}};
-        static long long sched_key[128][4];
-        const int slot = D / 32 - 1;
         const long long key = (((long long)T * 4096 + H) * 65536 + B) * 512 + ctas;
-        if (!sched_buf[dev][slot]) {
-            if (cudaMalloc(&sched_buf[dev][slot], (kMaxCtas + 1 + kMaxItems) * sizeof(unsigned short)) != cudaSuccess)
-                return set_error(ATTN_ERR_NOMEM, "3xTF32 forward: cannot allocate the schedule buffer");
-            sched_key[dev][slot] = -1;
-        }
-        if (key != sched_key[dev][slot]) {
-            std::vector<unsigned short> h;
-            lpt_schedule_tf32(p, ctas, h);
-            if (cudaMemcpyAsync(sched_buf[dev][slot], h.data(), h.size() * sizeof(unsigned short),
-                                cudaMemcpyHostToDevice, s) != cudaSuccess ||
-                cudaStreamSynchronize(s) != cudaSuccess)
-                return set_error(ATTN_ERR_CUDA, "3xTF32 forward: schedule upload failed");
-            sched_key[dev][slot] = key;
-        }
-        p.sched = sched_buf[dev][slot];
+        p.sched = schedule_get(100 + D, key, [&](std::vector<unsigned short> &h) { lpt_schedule_tf32(p, ctas, h); });
+        p.use_list = p.sched != nullptr;            // a full cache: the list-free static schedule
     }
     const size_t smem = Cg::SMEM;
     if (!ensure_smem_attr((const void *)fwd_tf32_kernel<D>, smem))
         return set_error(ATTN_ERR_CUDA, "3xTF32 forward: cannot set shared-memory size");
-    static bool carveout_set[128][4] = {{false}};
-    if (!carveout_set[dev][D / 32 - 1]) {
-        if (cudaFuncSetAttribute((const void *)fwd_tf32_kernel<D>, cudaFuncAttributePreferredSharedMemoryCarveout,
-                                 100) != cudaSuccess)
-            return set_error(ATTN_ERR_CUDA, "3xTF32 forward: cannot set the shared-memory carveout");
-        carveout_set[dev][D / 32 - 1] = true;
-    }
+    if (!ensure_carveout((const void *)fwd_tf32_kernel<D>, 100))
+        return set_error(ATTN_ERR_CUDA, "3xTF32 forward: cannot set the shared-memory carveout");
     fwd_tf32_kernel<D><<<ctas, kThreads, smem, s>>>(mq, mk, mv, p);
     return check_launch("3xTF32 forward kernel");
 }

@@ -43,18 +43,24 @@ def test_static_scratch_decode_matches_workspace_decode(cuda, kv_name):
     kv = A.I8 if kv_name == "int8" else A.F32
     shape, q, kc, vc, ks, vs, lens = _case(A, kv, 1000 + kv)
     assert A.decode_workspace_bytes(shape) <= A.STATIC_SCRATCH_BYTES
+    # the regular entry point with a caller workspace (not the library's own)
+    ws_bytes = A.decode_workspace_bytes(shape)
+    ws = torch.zeros(ws_bytes, dtype=torch.uint8, device="cuda")
     ref = torch.empty_like(q)
     A.decode_ex(shape, q.data_ptr(), kc.data_ptr(), vc.data_ptr(), ks.data_ptr() if ks is not None else None,
-                vs.data_ptr() if vs is not None else None, lens.data_ptr(), ref.data_ptr())
+                vs.data_ptr() if vs is not None else None, lens.data_ptr(), ref.data_ptr(), ws.data_ptr(), ws_bytes)
     torch.cuda.synchronize()
     ref_h = ref.cpu().numpy()
-    for _ in range(2):                                # two calls in a row share the scratch
-        out = torch.full_like(q, float("nan"))
+    outs = [torch.full_like(q, float("nan")) for _ in range(2)]
+    for i, out in enumerate(outs):                    # two calls in a row share the scratch
+        free0 = torch.cuda.mem_get_info()[0]
         A.check(A.lib.attn_decode_static_ex(ctypes.byref(shape), q.data_ptr(), kc.data_ptr(), vc.data_ptr(),
                                             ks.data_ptr() if ks is not None else None,
                                             vs.data_ptr() if vs is not None else None,
                                             lens.data_ptr(), out.data_ptr(), None))
         torch.cuda.synchronize()
+        if i == 1:                                    # after the first call has loaded the kernels
+            assert torch.cuda.mem_get_info()[0] == free0, "the static entry point took device memory"
         out_h = out.cpu().numpy()
         assert np.isfinite(out_h).all()
         assert rel_err(out_h, ref_h) < F32_TOL
