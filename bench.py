@@ -14,8 +14,10 @@ measurements for every config:
 --config <key> runs one of them alone.
 
 A step is one call of the path over one batch of synthetic input that is
-already resident in HBM; its device time comes from CUDA events around the
-call on the launching stream.  No step starts L2-warm: when one step's
+already resident in HBM.  The K timed steps run back to back on the launching
+stream between two CUDA events, queued behind a device sleep long enough for
+the host to enqueue them all, so the interval holds the steps and the gaps
+between their kernels but not the host's enqueue.  No step starts L2-warm: when one step's
 working set is below 2 x L2, the step's device tensors are rotated over
 enough copies that together they exceed it.
 
@@ -602,27 +604,31 @@ def measure(key, args, ctx):
             dist.barrier(device_ids=[local])
 
     with torch.cuda.stream(stream):
+        t_host = time.perf_counter()
         for _ in range(args.warmup):
             wl.step(stream.cuda_stream)
+        t_host = (time.perf_counter() - t_host) / args.warmup     # host seconds to enqueue one step
         stream.synchronize()
-        starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-        ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         barrier()
         torch.cuda.synchronize()
+        # The K steps run back to back behind one device sleep long enough for
+        # the host to enqueue all of them, so that the timed interval holds the
+        # steps and the gaps between their kernels, not the host's enqueue.
+        sleep_s = min(0.05, 2e-4 + 4.0 * t_host * args.steps)
         with Clocks(local) as clk:
             t_wall = time.perf_counter()
+            torch.cuda._sleep(int(sleep_s * 2.0e9))               # cycles at up to 2 GHz
+            e_start.record(stream)
             for i in range(args.steps):
-                # ~50 us of device sleep ahead of the start event, so that the
-                # host's enqueue of the call is not inside the timed interval
-                torch.cuda._sleep(100000)
-                starts[i].record(stream)
                 wl.step(stream.cuda_stream)
-                ends[i].record(stream)
+            e_end.record(stream)
+            t_enq = time.perf_counter() - t_wall
             stream.synchronize()
             barrier()
             torch.cuda.synchronize()
             t_wall = time.perf_counter() - t_wall
-        total_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
+        total_ms = e_start.elapsed_time(e_end)
         # the gather alone (every rank takes the same collective steps)
         gather_ms = 0.0
         if wl.gather_ok:
@@ -693,7 +699,11 @@ def measure(key, args, ctx):
                             "l2": (f"inputs larger than L2: {n_sets} rotated copies of the step's tensors "
                                    f"({n_sets} x {wl.working_set / 2**20:.0f} MiB)") if n_sets > 1
                                   else "inputs larger than L2 (working set > 2 x L2)",
-                            "wall_s_timed": round(t_wall, 4)},
+                            "wall_s_timed": round(t_wall, 4),
+                            "timing": (f"{args.steps} steps back to back between two CUDA events, queued behind a "
+                                       f"{sleep_s * 1e3:.2f} ms device sleep; the host enqueued them in "
+                                       f"{t_enq * 1e3:.2f} ms"),
+                            "host_ahead_of_device": bool(t_enq < sleep_s)},
             "roofline": {"bound": bound, "achieved": round(achieved, 2), "peak": peak, "unit": punit,
                          "frac": round(achieved / peak, 4), "traffic": traffic, "traffic_capture": tinfo,
                          "peak_source": f"{pk['src']} ({'bf16_tflops burst' if bound == 'tensor' else 'hbm_gbs'})",

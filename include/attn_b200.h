@@ -346,8 +346,9 @@ ATTN_API int attn_decode_multi(const attn_decode_shape *shapes, const float *con
 /* ------------------------------------------------------------------------
  * Test hook (no counterpart in the reference)
  * ---------------------------------------------------------------------- */
-/* The next `launches` fp32 decode calls served by the single-pass decode
- * kernel (few sequences, small total cache) make one of its warps wait on a
+/* The next `launches` fp32 decode calls served by the TMA-ring decode kernel
+ * (fp32 calls of up to 256 sequences and 256 MB of cache that are too large
+ * for the one-CTA-per-head kernel) make one of its warps wait on a
  * barrier that nothing arrives at, bounded by `limit_cycles` SM cycles
  * (>= 1000).  The wait runs out and the kernel takes its timeout path: it
  * records code 0x32f in the device error word (attn_device_error), stops,

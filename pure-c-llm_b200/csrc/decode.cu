@@ -680,9 +680,12 @@ int launch_decode_i8mma(const DecodeLaunch &L);
 
 bool decode_ring_ok(const DecodeLaunch &L);
 int launch_decode_ring(const DecodeLaunch &L);
+bool decode_head_ok(const DecodeLaunch &L);
+int launch_decode_head(const DecodeLaunch &L);
 
 int launch_decode(const DecodeLaunch &L) {
     const bool i8 = L.kv_dtype == ATTN_I8;
+    if (decode_head_ok(L)) return launch_decode_head(L);
     if (decode_ring_ok(L)) return launch_decode_ring(L);
     if (decode_i8mma_ok(L)) return launch_decode_i8mma(L);
     if (decode_stream_ok(L)) return launch_decode_stream(L);

@@ -1,30 +1,29 @@
-// decode_ring.cu -- KV-cached decode attention over an fp32 cache for calls
-// whose total cache traffic is small (the 16-layer generator step), as one
-// persistent, one-pass, TMA-fed kernel (sm_100a).
+// decode_ring.cu -- KV-cached decode attention over an fp32 cache for
+// mid-size calls (up to 256 sequences and 256 MB of cache, too large for the
+// one-CTA-per-(sequence, head) kernel of decode_head.cu), as one persistent,
+// one-pass, TMA-fed kernel (sm_100a).
 //
 // Semantics: cached_attention, transformer.c:203-248 -- for every head, one
 // query row scores cache rows 0..len-1 with (q . k_j) / sqrt(d), softmaxes
 // them and sums the value rows.
 //
-// Why a separate kernel: a generator step reads only ~40 MB (16 layers x
-// ~600 rows x 2 KB x K,V), about 6 us at the HBM roof, so the time goes to
-// latency: a launch, the first bytes' round trip, and any pass that waits on
-// another.  This kernel therefore
-//   * splits the concatenated rows of all sequences evenly over one CTA per
-//     SM (a CTA's range covers one or two sequences), so every SM streams the
-//     same number of bytes and no second wave exists;
-//   * streams whole token rows (all heads, contiguous in memory) of K and V
-//     together with cp.async.bulk into a ring of ~32 KB stages, so at kernel
-//     start ~190 KB per SM -- most of the SM's share -- is requested at once;
-//     the query row travels with the first stage of each piece;
-//   * consumes each stage in one pass: warp h owns head h, scores the stage's
-//     rows with a transposing butterfly reduction (each lane ends up owning
-//     one row's score), keeps an online softmax (running max moved only when
-//     a score exceeds it by more than 2^8), and accumulates the value rows;
-//   * merges a sequence split over several CTAs in the CTA that finishes it
-//     last: per (sequence, head) a 64-bit ticket holds (call generation,
+// Design:
+//   * the concatenated rows of all sequences are split evenly over one CTA
+//     per SM, so every SM streams the same number of bytes and no second
+//     wave exists;
+//   * whole token rows (all heads, contiguous in memory) of K and V stream
+//     with cp.async.bulk into a ring of ~32 KB stages, most of the SM's share
+//     requested at once; the query row travels with the first stage of each
+//     piece;
+//   * each stage is consumed in one pass: warp h owns head h, scores the
+//     stage's rows with a transposing butterfly reduction (each lane ends up
+//     owning one row's score), keeps an online softmax (running max moved
+//     only when a score exceeds it by more than 2^8) and accumulates the
+//     value rows;
+//   * a sequence split over several CTAs is merged by the CTA that finishes
+//     it last: per (sequence, head) a 64-bit ticket holds (call generation,
 //     count), so tickets need no clearing between calls and the call is a
-//     single launch.
+//     single launch; the merge issues its loads together.
 // Every mbarrier wait is bounded; a timeout records a code in the device error
 // word and raises a CTA-wide abort flag, after which the producer waits
 // (bounded) for the bulk copies it has in flight before the CTA exits.
@@ -402,18 +401,46 @@ decode_ring_kernel(const __grid_constant__ Params p)
         last = __shfl_sync(0xffffffffu, last, 0);
         if (!last) continue;
         __threadfence();
+        // Merge this head's pieces.  Their loads go out together: the lanes
+        // take 32 pieces' statistics at a time, then every lane issues 8
+        // pieces' output loads before using any of them.
+        const float2 *pml = reinterpret_cast<const float2 *>(p.part_ml);
         float M = -INFINITY;
-        for (int cc = c_first; cc <= c_last; cc++) M = fmaxf(M, __ldcg(p.part_ml + ((cc + e) * (long long)H + h) * 2));
+        for (int c0 = c_first; c0 <= c_last; c0 += 32) {
+            const int cc = c0 + lane;
+            const float mv = cc <= c_last ? __ldcg(pml + (cc + e) * (long long)H + h).x : -INFINITY;
+            M = fmaxf(M, mv);
+        }
+#pragma unroll
+        for (int o2 = 16; o2 > 0; o2 >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o2));
         float L = 0.f, acc[DL];
 #pragma unroll
         for (int i = 0; i < DL; i++) acc[i] = 0.f;
-        for (int cc = c_first; cc <= c_last; cc++) {
-            const float *pm = p.part_ml + ((cc + e) * (long long)H + h) * 2;
-            const float f = ex2(__ldcg(pm) - M);
-            L += __ldcg(pm + 1) * f;
-            const float *pp = p.part_o + (cc + e) * (long long)HD + col;
+        for (int c0 = c_first; c0 <= c_last; c0 += 32) {
+            const int cc = c0 + lane;
+            float2 ml = make_float2(-INFINITY, 0.f);
+            if (cc <= c_last) ml = __ldcg(pml + (cc + e) * (long long)H + h);
+            const float f = ml.x == -INFINITY ? 0.f : ex2(ml.x - M);
+            float lf = ml.y * f;
 #pragma unroll
-            for (int i = 0; i < DL; i++) acc[i] = fmaf(__ldcg(pp + i), f, acc[i]);
+            for (int o2 = 16; o2 > 0; o2 >>= 1) lf += __shfl_xor_sync(0xffffffffu, lf, o2);
+            L += lf;
+            const int n = min(32, c_last - c0 + 1);
+            for (int j0 = 0; j0 < n; j0 += 8) {
+                float v[8][DL];
+#pragma unroll
+                for (int u = 0; u < 8; u++) {
+                    const float *pp = p.part_o + (c0 + j0 + u + e) * (long long)HD + col;
+#pragma unroll
+                    for (int i = 0; i < DL; i++) v[u][i] = j0 + u < n ? __ldcg(pp + i) : 0.f;
+                }
+#pragma unroll
+                for (int u = 0; u < 8; u++) {
+                    const float fu = __shfl_sync(0xffffffffu, f, (j0 + u) & 31);
+#pragma unroll
+                    for (int i = 0; i < DL; i++) acc[i] = fmaf(v[u][i], fu, acc[i]);
+                }
+            }
         }
         const float inv = 1.f / L;
 #pragma unroll
