@@ -151,7 +151,9 @@ ATTN_API size_t attn_decode_workspace_bytes(const attn_decode_shape *s);
  *     (ATTN_F32) or int8 codes (ATTN_I8).
  *   kscale/vscale: ATTN_I8 only, fp32 [(s*cap + r)*H + h] (NULL for fp32).
  * workspace may be NULL: the library then uses a buffer of its own per
- * device (allocated on first use). */
+ * device (allocated on first use); calls that use that buffer must not
+ * overlap on the GPU (order them on one stream, or give each stream its own
+ * workspace). */
 ATTN_API int attn_decode_ex(const attn_decode_shape *s, const float *q,
                    const void *kcache, const void *vcache,
                    const float *kscale, const float *vscale,
@@ -187,7 +189,8 @@ ATTN_API int attn_decode_static_ex(const attn_decode_shape *s, const float *q,
 
 /* cached_attention (transformer.c:203) with device pointers: one token of one
  * layer, attends rows 0..pos.  Writes out (H*d).  Uses the library's own
- * workspace.  Returns a status. */
+ * workspace, so calls must not overlap on the GPU with other calls that use
+ * it.  Returns a status. */
 ATTN_API int attn_cached_attention(const float *q, const float *kcache, const float *vcache,
                           float *out, int pos, int heads, int head_dim,
                           long long row_stride, attn_stream_t stream);

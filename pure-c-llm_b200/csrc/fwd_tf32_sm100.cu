@@ -85,8 +85,10 @@ struct Cfg {
     // per-thread registers after setmaxnreg: warpgroup 0, splitters, softmax
     // (two CTAs per SM: 384 x 80 at launch = 128 x (32 + 56 + 152); one CTA:
     // 384 x 168 at launch >= 128 x (64 + 160 + 232), or 128 x (64 + 200 + 232)
-    // at d = 96).  ptxas allocates each role's code within its budget, so
-    // these are the sizes at which the roles compile without spills.
+    // at d = 96).  ptxas allocates each role's code within its budget: with
+    // one CTA per SM these budgets compile without spills; at d = 32 (two
+    // CTAs per SM) no split of the 240 registers does, and 32/56/152 leaves
+    // the fewest (80 bytes, against 136 for 40/56/144), which ran fastest.
     static constexpr int REG_MMA = CTAS == 2 ? 32 : 64;
     static constexpr int REG_SPLIT = CTAS == 2 ? 56 : (D == 96 ? 200 : 160);
     static constexpr int REG_SOFT = CTAS == 2 ? 152 : 232;
