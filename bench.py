@@ -72,8 +72,14 @@ CONFIGS = {
                    workload="C5 causal backward fp32 B4 H16 T4096 d64"),
     "c5-bf16": dict(kind="bwd", B=4, H=16, T=4096, d=64, dtype="bf16",
                     workload="C5 causal backward bf16 B4 H16 T4096 d64"),
+    # not a BASELINE config: the reference GPU trainer's own attention call pair
+    # (gpu_kernels.h:17-31 shape) through the drop-in symbols, beside the
+    # reference's own cuBLAS attention at that shape
+    "trainer": dict(kind="train", B=4, H=12, T=1024, d=128, dtype="f32",
+                    workload="the reference GPU trainer's attention: attn_fwd + attn_bwd drop-ins at "
+                             "gpu_kernels.h's shape B4 H12 T1024 d128, fp32"),
 }
-ORDER = ["c3-bf16", "c1", "c2", "c3-f32", "c4-f32", "c4-int8", "c5-f32", "c5-bf16"]
+ORDER = ["c3-bf16", "c1", "c2", "c3-f32", "c4-f32", "c4-int8", "c5-f32", "c5-bf16", "trainer"]
 HEADLINE = "c3-bf16"
 METRIC = "causal-attn prefill TFLOP/s & KV-decode HBM GB/s per B200 at 1/2/4/8 GPUs"
 L2_BYTES = 126 * 2 ** 20
@@ -86,16 +92,16 @@ def causal_flops(B, H, T, d):
 
 
 def metric_of(cfg):
-    return {"fwd": "causal-attn prefill TFLOP/s", "bwd": "causal-attn backward TFLOP/s"}.get(
-        cfg["kind"], "KV-decode HBM GB/s")
+    return {"fwd": "causal-attn prefill TFLOP/s", "bwd": "causal-attn backward TFLOP/s",
+            "train": "causal-attn forward+backward TFLOP/s"}.get(cfg["kind"], "KV-decode HBM GB/s")
 
 
 def unit_of(cfg):
-    return "TFLOP/s" if cfg["kind"] in ("fwd", "bwd") else "GB/s"
+    return "TFLOP/s" if cfg["kind"] in ("fwd", "bwd", "train") else "GB/s"
 
 
 def dtype_of(cfg):
-    if cfg["kind"] in ("fwd", "bwd"):
+    if cfg["kind"] in ("fwd", "bwd", "train"):
         return cfg["dtype"]
     return "f32 (int8 cache)" if cfg.get("kv") == "int8" else "f32"
 
@@ -201,19 +207,20 @@ class CpuSample:
         self.O, self.cfg = O, cfg
         self.cores = _host_threads()
         kind = cfg["kind"]
-        if kind in ("fwd", "bwd"):
+        if kind in ("fwd", "bwd", "train"):
             B, H, T, d = 1, cfg["H"], cfg["T"], cfg["d"]
             if kind == "bwd":
                 T = min(T, 1024)
             self.args = (B, T, H, d)
             self.q, self.k, self.v = (synth.normal(s, (B * T, H * d), 0, 0.5) for s in (1, 2, 3))
-            if kind == "bwd":
+            if kind in ("bwd", "train"):
                 self.do = synth.normal(4, (B * T, H * d))
                 _, self.probs = O.ref_attention_forward(self.q, self.k, self.v, B, T, H, d)
-            self.work = causal_flops(B, H, T, d) * (2 if kind == "bwd" else 1) / 1e12
+            self.work = causal_flops(B, H, T, d) * {"fwd": 1, "bwd": 2, "train": 3}[kind] / 1e12
             self.unit = "TFLOP/s"
-            self.sample = (f"reference train.c attention_{'backward' if kind == 'bwd' else 'forward'} "
-                           f"B={B} H={H} T={T} d={d} (one batch row of the workload)")
+            what = {"fwd": "attention_forward", "bwd": "attention_backward",
+                    "train": "attention_forward + attention_backward"}[kind]
+            self.sample = f"reference train.c {what} B={B} H={H} T={T} d={d} (one batch row of the workload)"
             return
         H, d = cfg["H"], cfg["d"]
         if kind == "decode":
@@ -244,6 +251,10 @@ class CpuSample:
         elif c["kind"] == "bwd":
             B, T, H, d = self.args
             O.ref_attention_backward(self.do, self.q, self.k, self.v, self.probs, B, T, H, d)
+        elif c["kind"] == "train":
+            B, T, H, d = self.args
+            _, probs = O.ref_attention_forward(self.q, self.k, self.v, B, T, H, d)
+            O.ref_attention_backward(self.do, self.q, self.k, self.v, probs, B, T, H, d)
         else:
             for n in self.lens:
                 O.ref_cached_attention(self.qv, self.kc, self.vc, n - 1, c["H"], c["d"], self.t_max)
@@ -273,9 +284,9 @@ class Workload:
         self.rank, self.world = rank, world
         kind = cfg["kind"]
         g = torch.Generator(device=dev).manual_seed(1234 + rank)
-        self.gather_ok = world > 1 and kind != "bwd"
+        self.gather_ok = world > 1 and kind in ("fwd", "decode", "ragged")
         self.gather_launches = 0
-        if kind in ("fwd", "bwd"):
+        if kind in ("fwd", "bwd", "train"):
             B, H, T, d = cfg["B"], cfg["H"], cfg["T"], cfg["d"]
             self.sp = sp = A.split_plan(B, H, world, rank)
             Bl, Hl = sp.batch, sp.heads
@@ -292,6 +303,20 @@ class Workload:
             self.total_work = causal_flops(B, H, T, d)
             self.launches = 1
             self.in_names, self.out_names = ["q", "k", "v"], ["o"]
+            if kind == "train":
+                # the drop-ins take their shape from the macro-shape setting and run
+                # on the legacy default stream; probs and scratch are the trainer's
+                # B*H*T*T-float buffers (train_kaggle.cu:128, 138)
+                A.check(A.lib.attn_set_macro_shape(Bl, Hl, T, d))
+                self.do = mk(1.0)
+                self.dq, self.dk, self.dv = (torch.empty_like(self.q) for _ in range(3))
+                self.probs = torch.empty(Bl * Hl * T * T, device=dev)
+                self.scratch = torch.empty(Bl * Hl * T * T, device=dev)
+                self.work *= 3
+                self.total_work *= 3
+                self.launches = 4                    # forward; row-dot pre-pass, dK/dV and dQ kernels
+                self.in_names = ["q", "k", "v", "do"]
+                self.out_names = ["o", "dq", "dk", "dv"]
             if kind == "bwd":
                 self.do = mk(1.0)
                 A.fwd_ex(self.shape, self.dtype_code, self.q.data_ptr(), self.k.data_ptr(), self.v.data_ptr(),
@@ -304,7 +329,7 @@ class Workload:
                 self.launches = 3                    # row-dot pre-pass, dK/dV kernel, dQ kernel
                 self.in_names = ["q", "k", "v", "do", "o", "lse"]
                 self.out_names = ["dq", "dk", "dv"]
-            if self.gather_ok:
+            if self.gather_ok and kind == "fwd":
                 self.full = torch.empty((B * T, H * d), dtype=dt, device=dev)
                 self.g_bytes = A.lib.attn_gather_workspace_bytes(ctypes.byref(self.full_shape), self.dtype_code, world)
                 self.g_ws = torch.empty(max(self.g_bytes, 256), dtype=torch.uint8, device=dev)
@@ -373,19 +398,20 @@ class Workload:
                 self.order = torch.from_numpy(order.reshape(-1)).to(dev)
                 self.full = torch.empty((n, H * d), device=dev)
             self.local_desc = f"{nl} of {n} sequences (LPT by length), {int(lens_h.sum())} of {int(lens_all.sum())} rows"
-        if self.gather_ok and kind != "fwd":
+        if self.gather_ok and kind in ("decode", "ragged"):
             self.g_bytes = A.lib.attn_gather_rows_workspace_bytes(self.max_local, self.row_bytes, world)
             self.g_ws = torch.empty(max(self.g_bytes, 256), dtype=torch.uint8, device=dev)
             self.gather_launches = 1 if kind == "ragged" else 0
         self.working_set = self.work if kind in ("decode", "ragged") else \
             sum(getattr(self, a).numel() * getattr(self, a).element_size() for a in self.in_names + self.out_names)
+        self.legacy_stream = kind == "train"     # the drop-ins run on the legacy default stream
 
     def unit_is_tflops(self):
-        return self.cfg["kind"] in ("fwd", "bwd")
+        return self.cfg["kind"] in ("fwd", "bwd", "train")
 
     # device tensors a step reads or writes, per kind (the rotated input sets)
     _ROT = {"fwd": ("q", "k", "v", "o", "lse"), "bwd": ("q", "k", "v", "o", "lse", "do", "dq", "dk", "dv"),
-            "decode": ("kc", "vc", "kp", "vp"), "ragged": ()}
+            "train": ("q", "k", "v", "o", "do", "dq", "dk", "dv"), "decode": ("kc", "vc", "kp", "vp"), "ragged": ()}
 
     def rotate_inputs(self, n):
         """Keeps n copies of the step's device tensors and cycles through them,
@@ -416,6 +442,13 @@ class Workload:
             A.bwd_ex(self.shape, self.dtype_code, self.do.data_ptr(), self.q.data_ptr(), self.k.data_ptr(),
                      self.v.data_ptr(), self.o.data_ptr(), self.lse.data_ptr(), self.dq.data_ptr(),
                      self.dk.data_ptr(), self.dv.data_ptr(), 0, self.ws.data_ptr(), self.ws_bytes, stream)
+        elif kind == "train":
+            P = ctypes.c_void_p
+            A.lib.attn_fwd(P(self.q.data_ptr()), P(self.k.data_ptr()), P(self.v.data_ptr()), P(self.o.data_ptr()),
+                           P(self.probs.data_ptr()))
+            A.lib.attn_bwd(P(self.dq.data_ptr()), P(self.dk.data_ptr()), P(self.dv.data_ptr()),
+                           P(self.scratch.data_ptr()), P(self.do.data_ptr()), P(self.q.data_ptr()),
+                           P(self.k.data_ptr()), P(self.v.data_ptr()), P(self.probs.data_ptr()))
         elif kind == "decode":
             s = self.step_idx % c["steps"]
             self.step_idx += 1
@@ -443,7 +476,7 @@ class Workload:
     def setup_e2e(self):
         torch = self.torch
         kind = self.cfg["kind"]
-        self.e2e_pipe = kind in ("fwd", "bwd", "ragged")
+        self.e2e_pipe = kind in ("fwd", "bwd", "train", "ragged")
         gather = self.gather_ok
         if self.e2e_pipe:
             # Every step copies its inputs in from pinned host memory and its
@@ -560,14 +593,20 @@ def gpu_baseline(key, args, ctx, wl):
             fwd()
             dq, dk, dv = (torch.empty_like(q) for _ in range(3))
             scratch = torch.empty_like(probs)
-            call = lambda: L.refgpu_attn_bwd(P(dq.data_ptr()), P(dk.data_ptr()), P(dv.data_ptr()),
-                                             P(scratch.data_ptr()), P(wl.do.data_ptr()), P(q.data_ptr()),
-                                             P(k.data_ptr()), P(v.data_ptr()), P(probs.data_ptr()))
+            bwd = lambda: L.refgpu_attn_bwd(P(dq.data_ptr()), P(dk.data_ptr()), P(dv.data_ptr()),
+                                            P(scratch.data_ptr()), P(wl.do.data_ptr()), P(q.data_ptr()),
+                                            P(k.data_ptr()), P(v.data_ptr()), P(probs.data_ptr()))
+            if cfg["kind"] == "train":                # the trainer's call pair
+                call = lambda: (fwd(), bwd())
+            else:
+                call = bwd
             saved, wl.sets = getattr(wl, "sets", None), None
             wl.step(0)                                 # ours on the same inputs (default stream)
             wl.sets = saved
             got, theirs = [wl.dq, wl.dk, wl.dv], [dq, dk, dv]
-            flops = 2 * causal_flops(B, H, T, d)
+            if cfg["kind"] == "train":
+                got, theirs = got + [wl.o], theirs + [att]
+            flops = (3 if cfg["kind"] == "train" else 2) * causal_flops(B, H, T, d)
         for _ in range(args.warmup):
             call()
         torch.cuda.synchronize(dev)
@@ -580,8 +619,9 @@ def gpu_baseline(key, args, ctx, wl):
     ms = e0.elapsed_time(e1) / args.steps
     diff = max(float(((a - b).abs().max() / b.abs().max().clamp_min(1e-6)).item()) for a, b in zip(got, theirs))
     return {"value": round(flops / (ms / 1e3) / 1e12, 3), "unit": "TFLOP/s", "ms_per_step": round(ms, 4),
-            "kind": "reference GPU path: gpu_kernels.cu attn_%s (cuBLAS SGEMM over the full T x T scores + its "
-                    "softmax kernels), built from its sources for sm_100a" % cfg["kind"],
+            "kind": "reference GPU path: gpu_kernels.cu %s (cuBLAS SGEMM over the full T x T scores + its "
+                    "softmax kernels), built from its sources for sm_100a"
+                    % {"fwd": "attn_fwd", "bwd": "attn_bwd", "train": "attn_fwd + attn_bwd"}[cfg["kind"]],
             "max_rel_diff_vs_ours": diff}
 
 
@@ -591,7 +631,7 @@ def measure(key, args, ctx):
     world, rank, local, dev = ctx["world"], ctx["rank"], ctx["local"], ctx["dev"]
     cfg = CONFIGS[key]
     wl = Workload(cfg, A, torch, dev, rank, world)
-    stream = torch.cuda.Stream(device=dev)
+    stream = torch.cuda.default_stream(dev) if wl.legacy_stream else torch.cuda.Stream(device=dev)
     # Inputs larger than L2 between timed steps: when one step's working set is
     # below 2 x L2, the step's tensors are rotated over enough copies.
     ws = max(1, int(wl.working_set))
@@ -665,7 +705,7 @@ def measure(key, args, ctx):
 
     h2d_all = wl.h2d_bytes
     gpu_base = None
-    if world == 1 and cfg["kind"] in ("fwd", "bwd") and cfg["dtype"] == "f32" and not args.no_gpu_baseline:
+    if world == 1 and cfg["kind"] in ("fwd", "bwd", "train") and cfg["dtype"] == "f32" and not args.no_gpu_baseline:
         gpu_base = gpu_baseline(key, args, ctx, wl)
     if world > 1:
         t = torch.tensor([total_ms, e2e_ms, gather_ms], dtype=torch.float64, device=dev)
@@ -848,7 +888,8 @@ def config_block(key, world):
     return {"workload": cfg["workload"], "config_key": key,
             "split": "none (one GPU)" if world == 1 else
             {"fwd": "(batch x head) units, attn_split_plan", "bwd": "(batch x head) units, attn_split_plan",
-             "decode": "layers", "ragged": "sequences, LPT by length"}[cfg["kind"]]}
+             "train": "(batch x head) units, attn_split_plan", "decode": "layers",
+             "ragged": "sequences, LPT by length"}[cfg["kind"]]}
 
 
 if __name__ == "__main__":

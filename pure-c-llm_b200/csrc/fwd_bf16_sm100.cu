@@ -128,6 +128,15 @@ __device__ __forceinline__ Item decode_item(const Params &p, int i) {
     return it;
 }
 
+// Query tile i of a CTA's k-th item goes to warpgroup i ^ wg_swap(k).  The
+// second tile of an item has one key tile more than the first; alternating
+// which warpgroup takes it balances the two warpgroups over a CTA's items
+// (they run ahead of each other by up to the key/value ring's depth).
+#ifndef ATTN_FWD_ALTERNATE
+#define ATTN_FWD_ALTERNATE 1
+#endif
+__device__ __forceinline__ int wg_swap(int k) { return ATTN_FWD_ALTERNATE ? (k & 1) : 0; }
+
 // the k-th item of this CTA, or -1
 __device__ __forceinline__ int item_of(const Params &p, int k) {
     if (p.use_list) {
@@ -229,6 +238,13 @@ fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
         }
         *abort_flag = 0;
         fence_mbar_init();
+        // The kernel is launched as a programmatic dependent of the work before
+        // it on the stream, so its CTAs may start while that work finishes:
+        // nothing that work may write (Q, K, V, O, lse) is touched before this
+        // wait (the other threads pass the barrier after set-up first), and the
+        // next kernel may be scheduled as soon as this grid has started.
+        asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+        asm volatile("griddepcontrol.wait;" ::: "memory");
         // Every CTA's first item is item blockIdx.x (both schedules deal the
         // first items one per CTA, longest first), so its query tiles and first
         // key tile start loading before the rest of the set-up and before the
@@ -319,7 +335,7 @@ fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
         bool ok = true;
         if (warp == 1) {
             constexpr uint32_t idS = idesc_bf16(BM, BN, 0, 0);   // Q, K both K-major
-            int t[2] = {0, 0};     // S tiles issued per query tile (S-empty phases)
+            int t0 = 0, t1 = 0;    // S tiles issued per warpgroup (S-empty phases)
             for (int k = 0; ok; k++) {
                 Item it;
                 if (!next_item(p, items_s, n_local, k, it)) break;
@@ -331,20 +347,22 @@ fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
                     // Descriptors of consecutive K-steps differ only in the
                     // start-address field, so each step adds a constant.
                     const uint64_t kd = sw128_desc(sKV + st * C::STAGE_BYTES, 16, 1024);
-                    for (int i = 0; i < 2; i++) {
+                    for (int i = 0; i < 2; i++) {                 // query tile i of the item
                         if (j >= (i ? it.n1 : it.n0)) continue;
-                        if (t[i] > 0 && !(ok = wait(B_SE + i, t[i] - 1, 0x211 + i))) break;
+                        const int w = i ^ wg_swap(k);                 // ... goes to warpgroup w
+                        const int tw = w ? t1 : t0;
+                        if (tw > 0 && !(ok = wait(B_SE + w, tw - 1, 0x211 + w))) break;
                         tc_fence_after();
                         const uint64_t qd = sw128_desc(sQ + (qb * 2 + i) * C::Q_BYTES, 16, 1024);
-                        const uint32_t d_t = tmem + (i ? C::TM_S1 : C::TM_S0);
+                        const uint32_t d_t = tmem + (w ? C::TM_S1 : C::TM_S0);
                         if (leader) {
 #pragma unroll
                             for (int kk = 0; kk < D / 16; kk++)   // +32 bytes along K per step
                                 mma_bf16_ss(d_t, qd + 2 * kk, kd + 2 * kk, idS, kk > 0);
-                            mma_commit(BAR(B_SF + i));
+                            mma_commit(BAR(B_SF + w));
                         }
                         __syncwarp();
-                        t[i]++;
+                        if (w) t1++; else t0++;
                     }
                     if (!ok) break;
                     release(B_KVE + st, true);
@@ -353,7 +371,7 @@ fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
                 g += it.n_kv;
             }
         } else {
-            const int i = warp - 2;                               // query tile of this issuer
+            const int i = warp - 2;                               // warpgroup of this issuer
             constexpr uint32_t idO = idesc_bf16(BM, D, 0, 1);    // P K-major (TMEM), V MN-major
             const uint32_t pt = tmem + (i ? C::TM_P1 : C::TM_P0);
             const uint32_t d_t = tmem + (i ? C::TM_O1 : C::TM_O0);
@@ -361,7 +379,7 @@ fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
             for (int k = 0; ok; k++) {
                 Item it;
                 if (!next_item(p, items_s, n_local, k, it)) break;
-                const int n = i ? it.n1 : it.n0;
+                const int n = (i ^ wg_swap(k)) ? it.n1 : it.n0;  // key tiles of this warpgroup's query tile
                 for (int j = 0; ok && j < it.n_kv; j++) {
                     const int st = (g + j) % kStages;
                     // the stage's load completing orders this release after the
@@ -404,9 +422,10 @@ fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
         for (int k = 0; ok; k++) {
             Item it;
             if (!next_item(p, items_s, n_local, k, it)) break;
-            const int n = wg ? it.n1 : it.n0;
+            const int qt = wg ^ wg_swap(k);          // this warpgroup's query tile of the item
+            const int n = qt ? it.n1 : it.n0;
             if (n == 0) continue;                    // no second query tile in this item
-            const int qs = it.q0 + wg * BM;
+            const int qs = it.q0 + qt * BM;
             float m_run = -INFINITY, l_run = 0.f;
             for (int j = 0; j < n; j++, t++) {
                 ok = mbar_wait(BAR(B_SF + wg), t & 1, abort_flag, p.err, 0x221);
@@ -691,8 +710,19 @@ int launch_fwd_bf16_sm100(int D, const void *q, const void *k, const void *v, vo
     const size_t smem = Cfg<64>::SMEM;
     if (!ensure_smem_attr((const void *)fwd_kernel<64>, smem))
         return set_error(ATTN_ERR_CUDA, "tcgen05 forward: cannot set shared-memory size");
-    fwd_kernel<64><<<ctas, kThreads, smem, s>>>(tq, tk, tv, to, p);
-    return check_launch("tcgen05 forward kernel");
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(ctas);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, fwd_kernel<64>, tq, tk, tv, to, p);
+    if (e != cudaSuccess) return set_error(ATTN_ERR_CUDA, "tcgen05 forward kernel: %s", cudaGetErrorString(e));
+    return ATTN_OK;
 }
 
 }  // namespace attn_host

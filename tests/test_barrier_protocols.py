@@ -86,9 +86,13 @@ def _run(make_roles, seed):
 
 # ---------------------------------------------------------------------------
 # fwd_bf16_sm100.cu: items of two query tiles (n0 and n1 key tiles, n1 = n0 + 1
-# or 0), Q double buffer, 4-stage K/V ring with K and V on separate barriers
+# or 0), Q double buffer, 4-stage K/V ring with K and V on separate barriers;
+# query tile i of item k goes to warpgroup i ^ swap(k)
 # ---------------------------------------------------------------------------
-def _fwd_roles(items, stages=4):
+def _fwd_roles(items, stages=4, alternate=True):
+    def swap(k):
+        return (k & 1) if alternate else 0
+
     def make(bar, W, A):
         for q in range(2):
             bar(("QF", q))
@@ -127,10 +131,11 @@ def _fwd_roles(items, stages=4):
                     for i in range(2):
                         if j >= (n1 if i else n0):
                             continue
-                        if t[i] > 0:
-                            yield W(("SE", i), t[i])
-                        yield A(("SF", i))
-                        t[i] += 1
+                        w = i ^ swap(k)
+                        if t[w] > 0:
+                            yield W(("SE", w), t[w])
+                        yield A(("SF", w))
+                        t[w] += 1
                     yield A(("KVE", st))
                     if j == nkv - 1:
                         yield A(("QE", qb))
@@ -139,7 +144,7 @@ def _fwd_roles(items, stages=4):
         def pv(i):
             g, t, kw = 0, 0, 0
             for k, (n0, n1, nkv) in enumerate(items):
-                n = n1 if i else n0
+                n = n1 if i ^ swap(k) else n0
                 for j in range(nkv):
                     st = (g + j) % stages
                     yield W(("VF", st), (g + j) // stages + 1)
@@ -158,8 +163,8 @@ def _fwd_roles(items, stages=4):
 
         def softmax(w):
             t = 0
-            for n0, n1, nkv in items:
-                n = n1 if w else n0
+            for k, (n0, n1, nkv) in enumerate(items):
+                n = n1 if w ^ swap(k) else n0
                 if n == 0:
                     continue
                 for j in range(n):
@@ -189,12 +194,13 @@ def _fwd_items(T, pairs):
 
 
 @pytest.mark.parametrize("T", [128, 200, 300, 1024, 1100, 4096])
-def test_fwd_bf16_protocol(T):
+@pytest.mark.parametrize("alternate", [True, False])
+def test_fwd_bf16_protocol(T, alternate):
     n_pairs = (T + 255) // 256
     for trial in range(40):
         rnd = random.Random(trial * 31 + T)
         pairs = sorted((rnd.randrange(n_pairs) for _ in range(rnd.randint(1, 6))), reverse=True)
-        dead, hazards = _run(_fwd_roles(_fwd_items(T, pairs)), trial)
+        dead, hazards = _run(_fwd_roles(_fwd_items(T, pairs), alternate=alternate), trial)
         assert dead is None, (pairs, dead)
         assert not hazards, (pairs, hazards[:3])
 
