@@ -58,6 +58,7 @@ __global__ void bwd_rowdot_kernel(const BwdParams p)
 template <typename T, int D>
 __global__ void __launch_bounds__(256) bwd_rowdot_tile_kernel(const BwdParams p)
 {
+    pdl_begin();   // launched by launch_pdl
     static_assert(D % 32 == 0, "8 threads x a multiple of 4 elements per row");
     constexpr int EP = D / 8;                        // elements per thread
     const int row = threadIdx.x >> 3, part = threadIdx.x & 7;
@@ -115,6 +116,7 @@ template <typename T, int D>
 __global__ void __launch_bounds__(kFThreads)
 bwd_dkdv_kernel(const BwdParams p)
 {
+    pdl_begin();   // launched by launch_pdl
     constexpr int TF = FTile<D>::FLOATS;
     constexpr int NB = BwdCfg<D>::NBUF;
     extern __shared__ __align__(16) float sm[];
@@ -235,6 +237,7 @@ template <typename T, int D>
 __global__ void __launch_bounds__(kFThreads)
 bwd_dq_kernel(const BwdParams p)
 {
+    pdl_begin();   // launched by launch_pdl
     constexpr int TF = FTile<D>::FLOATS;
     constexpr int NB = BwdCfg<D>::NBUF;
     extern __shared__ __align__(16) float sm[];
@@ -344,7 +347,9 @@ static int launch_rowdot_t(const attn::BwdParams &p, cudaStream_t s) {
                          (p.in_stride * (long long)sizeof(T)) % 8 == 0 && (p.out_stride * (long long)sizeof(T)) % 8 == 0;
     if (aligned && p.H <= 65535 && p.B <= 65535) {
         const dim3 grid((unsigned)((p.T + 31) / 32), (unsigned)p.H, (unsigned)p.B);
-        attn::bwd_rowdot_tile_kernel<T, D><<<grid, 256, 0, s>>>(p);
+        const int st = check_pdl(launch_pdl(attn::bwd_rowdot_tile_kernel<T, D>, grid, dim3(256), 0, s, p),
+                                 "bwd_rowdot_tile_kernel");
+        if (st) return st;
     } else {
         const long long rows = (long long)p.B * p.T * p.H;
         attn::bwd_rowdot_kernel<T, D><<<(unsigned)((rows + 7) / 8), 256, 0, s>>>(p);
@@ -389,10 +394,9 @@ static int launch_bwd_f32_t(const attn::BwdParams &p, cudaStream_t s) {
     int st = launch_rowdot_t<T, D>(p, s);
     if (st) return st;
     dim3 grid((p.T + kFBM - 1) / kFBM, p.H, p.B);
-    bwd_dkdv_kernel<T, D><<<grid, kFThreads, smem_kv, s>>>(p);
-    if ((st = check_launch("bwd_dkdv_kernel"))) return st;
-    bwd_dq_kernel<T, D><<<grid, kFThreads, smem_q, s>>>(p);
-    return check_launch("bwd_dq_kernel");
+    if ((st = check_pdl(launch_pdl(bwd_dkdv_kernel<T, D>, grid, dim3(kFThreads), smem_kv, s, p), "bwd_dkdv_kernel")))
+        return st;
+    return check_pdl(launch_pdl(bwd_dq_kernel<T, D>, grid, dim3(kFThreads), smem_q, s, p), "bwd_dq_kernel");
 }
 
 int launch_bwd_f32(int dtype, int D, const void *dout, const void *q, const void *k,

@@ -38,6 +38,7 @@ using namespace sm100;
 constexpr int BT = 128;           // fixed rows per tile (TMEM lanes)
 constexpr int BS = 32;            // streamed rows per tile
 constexpr int kThreads = 384;
+constexpr int kGroupBH = 16;      // (batch, head) pairs per group of the unit order
 // The tensor core's accumulation into TMEM is not round-to-nearest; over the
 // thousands of products a dK/dV/dQ row gathers at T = 4096 that drifts by
 // ~5e-5.  So the accumulators restart every kGroup streamed tiles (96
@@ -77,7 +78,7 @@ struct Params {
     float *out1, *out2;          // dkdv: dK, dV;  dq: dQ
     const float *lse2, *dvec;    // [B][H][T]
     long long out_stride;
-    int T, H, accumulate;
+    int T, H, B, accumulate;
     float scale_log2;            // log2(e) / sqrt(d)
     float ds_scale;              // 1 / sqrt(d)
     int *err;
@@ -93,6 +94,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 bwd_tf32_kernel(const __grid_constant__ CUtensorMap m_a, const __grid_constant__ CUtensorMap m_b,
                 const __grid_constant__ CUtensorMap m_c, const __grid_constant__ CUtensorMap m_d, const Params p)
 {
+    pdl_begin();   // launched by launch_pdl
     using C = Cfg<D>;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
@@ -106,10 +108,19 @@ bwd_tf32_kernel(const __grid_constant__ CUtensorMap m_a, const __grid_constant__
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n_ft = (p.T + BT - 1) / BT;
-    const int h = blockIdx.x, b = blockIdx.y;
+    // Block u of the 1-D grid: the units come in groups of kGroupBH (batch,
+    // head) pairs -- CTAs launched together share a few pairs, whose streamed
+    // tiles are read from DRAM about once and then from L2 -- and within a
+    // group by descending cost (tile rank z), which keeps each wave's CTAs of
+    // similar length.
+    const int u = (int)blockIdx.x, hb_all = p.H * p.B;
+    const int blk = u / (kGroupBH * n_ft), u_in = u - blk * kGroupBH * n_ft;
+    const int hb = min(kGroupBH, hb_all - blk * kGroupBH);
+    const int z = u_in / hb, r = blk * kGroupBH + (u_in - z * hb);
+    const int h = r % p.H, b = r / p.H;
     // dkdv: key tile kt = z (small kt streams the most query tiles: issued first);
     // dq: query tile qt = n_ft-1-z (large qt streams the most key tiles)
-    const int fixed = KIND == 0 ? (int)blockIdx.z : n_ft - 1 - (int)blockIdx.z;
+    const int fixed = KIND == 0 ? z : n_ft - 1 - z;
     const int first = KIND == 0 ? fixed * (BT / BS) : 0;                 // streamed tile range
     const int last = KIND == 0 ? (p.T + BS - 1) / BS : (min(p.T, (fixed + 1) * BT) + BS - 1) / BS;
     const int count = last - first;
@@ -513,6 +524,7 @@ static int launch_bwd_tf32_t(const void *dout, const void *q, const void *k, con
     p.out_stride = out_stride;
     p.T = T;
     p.H = H;
+    p.B = B;
     p.accumulate = accumulate;
     p.scale_log2 = attn::kLog2e / sqrtf((float)D);
     p.ds_scale = 1.0f / sqrtf((float)D);
@@ -522,15 +534,20 @@ static int launch_bwd_tf32_t(const void *dout, const void *q, const void *k, con
         !ensure_smem_attr((const void *)bwd_tf32_kernel<D, 1>, smem))
         return set_error(ATTN_ERR_CUDA, "3xTF32 backward: cannot set shared-memory size");
     const int n_ft = (T + BT - 1) / BT;
-    dim3 grid(H, B, n_ft);
+    const long long n_units = (long long)B * H * n_ft;
+    if (n_units > (1LL << 30)) return set_error(ATTN_ERR_INVALID, "3xTF32 backward: too many tiles");
+    const dim3 grid((unsigned)n_units);
     p.out1 = static_cast<float *>(dk);
     p.out2 = static_cast<float *>(dv);
-    bwd_tf32_kernel<D, 0><<<grid, kThreads, smem, s>>>(mk, mv, mq32, mdo32, p);   // fixed K, V; streamed Q, dO
-    if ((st = check_launch("3xTF32 backward dkdv kernel"))) return st;
+    // fixed K, V; streamed Q, dO
+    if ((st = check_pdl(launch_pdl(bwd_tf32_kernel<D, 0>, grid, dim3(kThreads), smem, s, mk, mv, mq32, mdo32, p),
+                        "3xTF32 backward dkdv kernel")))
+        return st;
     p.out1 = static_cast<float *>(dq);
     p.out2 = nullptr;
-    bwd_tf32_kernel<D, 1><<<grid, kThreads, smem, s>>>(mq, mdo, mk32, mv32, p);   // fixed Q, dO; streamed K, V
-    return check_launch("3xTF32 backward dq kernel");
+    // fixed Q, dO; streamed K, V
+    return check_pdl(launch_pdl(bwd_tf32_kernel<D, 1>, grid, dim3(kThreads), smem, s, mq, mdo, mk32, mv32, p),
+                     "3xTF32 backward dq kernel");
 }
 
 int launch_bwd_tf32_sm100(int D, const void *dout, const void *q, const void *k, const void *v, const void *o,

@@ -53,6 +53,14 @@ __device__ __forceinline__ float4 load4_cg(const float *p) {
     return __ldcg(reinterpret_cast<const float4 *>(p));
 }
 
+// First statement of a kernel launched by launch_pdl: lets the next kernel on
+// the stream be scheduled, then waits until the work before this grid has
+// finished and its memory is visible (the CTAs may start early).
+__device__ __forceinline__ void pdl_begin() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
@@ -69,6 +77,30 @@ __device__ __forceinline__ float warp_sum(float v) {
 // Host-side launch status helper shared by the .cu files of the library.
 namespace attn_host {
 int set_error(int status, const char *fmt, ...);
+
+// Launches `kernel` as a programmatic dependent of the work before it on the
+// stream (the kernel begins with pdl_begin): its CTAs may become resident
+// while that work finishes, which hides most of the launch gap between
+// back-to-back kernels.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                              Args... args) {
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+inline int check_pdl(cudaError_t e, const char *what) {
+    if (e != cudaSuccess) return set_error(ATTN_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+    return ATTN_OK;
+}
 inline int check_launch(const char *what) {
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return set_error(ATTN_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));

@@ -107,6 +107,7 @@ template <int D, bool I8>
 __global__ void __launch_bounds__(kDecThreads)
 decode_split_kernel(const DecodeParams p)
 {
+    pdl_begin();   // launched by launch_pdl
     using Slice = RowSlice<D, I8>;
     constexpr int E = Slice::E;
     constexpr int ROWS = Slice::ROWS;
@@ -617,8 +618,8 @@ static int launch_decode_t(const DecodeLaunch &L) {
     p.qscale = kLog2e / sqrtf((float)D);
     dim3 grid(p.max_splits, L.heads, L.n_seq);
     size_t smem = (size_t)(p.chunk + RowSlice<D, I8>::ROWS * D) * sizeof(float);
-    decode_split_kernel<D, I8><<<grid, kDecThreads, smem, L.stream>>>(p);
-    return check_launch("decode_split_kernel");
+    return check_pdl(launch_pdl(decode_split_kernel<D, I8>, grid, dim3(kDecThreads), smem, L.stream, p),
+                     "decode_split_kernel");
 }
 
 bool ensure_smem_attr(const void *func, size_t bytes);

@@ -68,7 +68,7 @@ decode_head_kernel(const __grid_constant__ Params p)
 
     // the work before this call on the stream may be writing the cache: the
     // CTAs of a programmatic launch become resident early and wait here
-    asm volatile("griddepcontrol.wait;" ::: "memory");
+    pdl_begin();
     const int h = blockIdx.x, e = blockIdx.y;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int grp = lane / LPR, sub = lane % LPR;

@@ -142,6 +142,7 @@ decode_i8mma_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constan
                     const __grid_constant__ CUtensorMap tks, const __grid_constant__ CUtensorMap tvs,
                     const __grid_constant__ Params p)
 {
+    pdl_begin();   // launched by launch_pdl
     using G = Geo<D>;
     constexpr int H = G::H, HB = G::HB, HW = G::HW, BW = G::BW;
     extern __shared__ uint8_t smem_raw[];
@@ -836,8 +837,9 @@ static int launch_i8mma_t(const DecodeLaunch &L) {
     const size_t smem = Gm::SMEM;
     if (!ensure_smem_attr((const void *)decode_i8mma_kernel<D>, smem))
         return set_error(ATTN_ERR_CUDA, "decode: cannot set shared-memory size");
-    decode_i8mma_kernel<D><<<p.grid, kThreads, smem, L.stream>>>(mk, mv, mk32, mv32, mks, mvs, p);
-    int st = check_launch("decode_i8mma_kernel");
+    int st = check_pdl(launch_pdl(decode_i8mma_kernel<D>, dim3(p.grid), dim3(kThreads), smem, L.stream, mk, mv, mk32,
+                                  mv32, mks, mvs, p),
+                       "decode_i8mma_kernel");
     if (st) return st;
     cudaLaunchConfig_t lc = {};
     lc.gridDim = dim3(L.n_seq, HD / 256);

@@ -131,6 +131,7 @@ template <int D, int R>
 __global__ void __launch_bounds__((kMaxHeads + 1) * 32, 1)
 decode_ring_kernel(const __grid_constant__ Params p)
 {
+    pdl_begin();   // launched by launch_pdl
     constexpr int DL = D / 32;                       // elements of a head per lane
     const int H = p.H;
     const Layout Lo(H, D, R);
@@ -536,8 +537,8 @@ static int launch_ring_t(const DecodeLaunch &L) {
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const int grid = std::max(1, std::min(std::min(sms, kMaxGrid), L.n_seq * L.max_len));
-    decode_ring_kernel<D, R><<<grid, (H + 1) * 32, smem, L.stream>>>(p);
-    return check_launch("decode_ring_kernel");
+    return check_pdl(launch_pdl(decode_ring_kernel<D, R>, dim3(grid), dim3((H + 1) * 32), smem, L.stream, p),
+                     "decode_ring_kernel");
 }
 
 int launch_decode_ring(const DecodeLaunch &L) {

@@ -108,6 +108,7 @@ template <int D, int CPL>
 __global__ void __launch_bounds__(kThreads, 1)
 decode_stream_kernel(const __grid_constant__ Params p)
 {
+    pdl_begin();   // launched by launch_pdl
     using G = Geo<D, CPL>;
     constexpr int H = G::H, HD = G::HD, R = G::R, S = G::STAGES, RPW = G::RPW;
     extern __shared__ uint8_t smem_raw[];
@@ -465,6 +466,7 @@ template <int D, int CPL>
 __global__ void __launch_bounds__(256)
 decode_stream_merge(const __grid_constant__ Params p)
 {
+    pdl_begin();   // launched by launch_pdl
     using G = Geo<D, CPL>;
     constexpr int H = G::H, HD = G::HD;
     const int e = blockIdx.x;
@@ -572,11 +574,11 @@ static int launch_stream_t(const DecodeLaunch &L) {
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const int grid = std::max(1, std::min(sms, p.n_items));
-    decode_stream_kernel<D, CPL><<<grid, kThreads, smem, L.stream>>>(p);
-    int st = check_launch("decode_stream_kernel");
+    int st = check_pdl(launch_pdl(decode_stream_kernel<D, CPL>, dim3(grid), dim3(kThreads), smem, L.stream, p),
+                       "decode_stream_kernel");
     if (st) return st;
-    decode_stream_merge<D, CPL><<<L.n_seq, 256, 0, L.stream>>>(p);
-    return check_launch("decode_stream_merge");
+    return check_pdl(launch_pdl(decode_stream_merge<D, CPL>, dim3(L.n_seq), dim3(256), 0, L.stream, p),
+                     "decode_stream_merge");
 }
 
 int launch_decode_stream(const DecodeLaunch &L) {

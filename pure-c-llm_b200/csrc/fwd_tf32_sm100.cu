@@ -196,6 +196,7 @@ __global__ void __launch_bounds__(kThreads, Cfg<D>::CTAS)
 fwd_tf32_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                 const __grid_constant__ CUtensorMap tv, const __grid_constant__ Params p)
 {
+    pdl_begin();   // launched by launch_pdl
     using C = Cfg<D>;
     constexpr int BN = C::BN;
     extern __shared__ uint8_t smem_raw[];
@@ -755,8 +756,8 @@ static int launch_tf32_t(const void *q, const void *k, const void *v, void *o, f
         return set_error(ATTN_ERR_CUDA, "3xTF32 forward: cannot set shared-memory size");
     if (!ensure_carveout((const void *)fwd_tf32_kernel<D>, 100))
         return set_error(ATTN_ERR_CUDA, "3xTF32 forward: cannot set the shared-memory carveout");
-    fwd_tf32_kernel<D><<<ctas, kThreads, smem, s>>>(mq, mk, mv, p);
-    return check_launch("3xTF32 forward kernel");
+    return check_pdl(launch_pdl(fwd_tf32_kernel<D>, dim3(ctas), dim3(kThreads), smem, s, mq, mk, mv, p),
+                     "3xTF32 forward kernel");
 }
 
 int launch_fwd_tf32_sm100(int D, const void *q, const void *k, const void *v, void *o, float *lse,
