@@ -784,7 +784,6 @@ def run_ours(args, keys):
     if world > 1:
         from datetime import timedelta
         os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
-        os.environ.setdefault("NCCL_DEBUG", "WARN")          # rank 0's stdout carries the JSON line only
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
     import attn_b200 as A
     if world > 1:
