@@ -788,7 +788,17 @@ def run_ours(args, keys):
     import attn_b200 as A
     if world > 1:
         import shard
-        shard.init_group(rank, world, local)
+        # NCCL may print its version line at communicator set-up; rank 0's
+        # stdout must carry the JSON line only, so set-up writes go to stderr
+        sys.stdout.flush()
+        saved = os.dup(1)
+        os.dup2(2, 1)
+        try:
+            shard.init_group(rank, world, local)
+        finally:
+            ctypes.CDLL(None).fflush(None)
+            os.dup2(saved, 1)
+            os.close(saved)
     ctx = dict(torch=torch, dist=dist, A=A, world=world, rank=rank, local=local, dev=dev)
     results = {}
     for key in keys:
