@@ -74,24 +74,50 @@ ATTN_API int attn_version(void);
 /* ------------------------------------------------------------------------
  * Training attention, drop-in (gpu_kernels.h:66-72)
  * ---------------------------------------------------------------------- */
+/* A C++ translation unit that also includes the reference's gpu_kernels.h
+ * (which declares attn_fwd / attn_bwd with C++ linkage) defines
+ * ATTN_OMIT_MACRO_DROPINS before including this header, so the two
+ * declarations do not conflict; the library exports both linkages. */
+#ifndef ATTN_OMIT_MACRO_DROPINS
 /* Replaces gpu_kernels.h:67 attn_fwd.  Q,K,V,att: (B*T, H*d) fp32 device.
- * `probs` is the caller's B*H*T*T-float buffer (train_kaggle.cu:123,128); this
- * library stores the per-row log-sum-exp and a head-major copy of the output
- * there, which attn_bwd reads back (needs T >= d+1, true at the reference's
- * T=1024, d=128).  Sets att.  Exits(1) with a message on failure. */
+ * `probs` is the caller's buffer (B*H*T*T floats in train_kaggle.cu:123,128).
+ * In the default mode (ATTN_PROBS_LSE_OUT) this library stores the per-row
+ * log-sum-exp and a copy of the output there, which attn_bwd reads back:
+ * probs needs B*H*T*(1+d) floats, and T >= d+1.  In ATTN_PROBS_LSE mode it
+ * stores only the log-sum-exp (B*H*T floats, any T) and attn_bwd reads the
+ * output from `att` itself (see attn_set_probs_mode).  Sets att.  Exits(1)
+ * with a message on failure. */
 ATTN_API void attn_fwd(const float *Q, const float *K, const float *V, float *att, float *probs);
 
 /* Replaces gpu_kernels.h:70 attn_bwd.  SETS dQ, dK, dV (like the reference's
- * cuBLAS path, beta = 0).  `scratch` is the caller's B*H*T*T-float workspace
- * (train_kaggle.cu:138).  Exits(1) with a message on failure. */
+ * cuBLAS path, beta = 0).  `scratch` is the caller's workspace (B*H*T*T
+ * floats in train_kaggle.cu:138); this library uses 2*B*H*T floats of it.
+ * Exits(1) with a message on failure. */
 ATTN_API void attn_bwd(float *dQ, float *dK, float *dV, float *scratch,
               const float *dAtt, const float *Q, const float *K, const float *V,
               const float *probs);
+#endif
 
 /* Shape used by attn_fwd/attn_bwd.  Defaults are gpu_kernels.h:17-31:
  * B_SIZE 4, N_HEADS 12, T_SIZE 1024, D_HEAD 128 (DIM 1536); a build may
- * override them with -DATTN_B_SIZE= etc.  Returns ATTN_OK or an error. */
+ * override them with -DATTN_B_SIZE= etc.  Returns ATTN_OK or an error
+ * (ATTN_ERR_UNSUPPORTED for T < d+1 in ATTN_PROBS_LSE_OUT mode). */
 ATTN_API int attn_set_macro_shape(int batch, int heads, int seq_len, int head_dim);
+
+/* What attn_fwd keeps in `probs` for attn_bwd.
+ *   ATTN_PROBS_LSE_OUT (default): log-sum-exp and a copy of the output,
+ *     B*H*T*(1+d) floats; attn_bwd needs nothing else.
+ *   ATTN_PROBS_LSE: log-sum-exp only, B*H*T floats -- the trainer's a_probs
+ *     shrinks from B*H*T*T floats per layer (2.4 GB at the 343M shape) to
+ *     B*H*T, and T is no longer bounded by that allocation.  attn_fwd records
+ *     which `att` buffer it wrote for each `probs` buffer; attn_bwd reads the
+ *     output from that `att`, which the caller must leave unchanged between
+ *     the two calls (train_kaggle.cu keeps a_att[l] for the Wo gradient).
+ *     attn_bwd with a `probs` that no attn_fwd of this process has filled is
+ *     an error (exit(1), like any drop-in failure).
+ * Returns ATTN_OK, or ATTN_ERR_INVALID for another value. */
+enum { ATTN_PROBS_LSE_OUT = 0, ATTN_PROBS_LSE = 1 };
+ATTN_API int attn_set_probs_mode(int mode);
 
 /* ------------------------------------------------------------------------
  * Training attention, explicit shapes

@@ -14,6 +14,7 @@ _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libattn_b200.so")
 
 OK, ERR_INVALID, ERR_UNSUPPORTED, ERR_CUDA, ERR_NOMEM, ERR_WORKSPACE, ERR_DEVICE, ERR_COMM = range(8)
+PROBS_LSE_OUT, PROBS_LSE = 0, 1      # attn_set_probs_mode
 F32, BF16, I8 = 0, 1, 2
 MAX_LAYERS = 64
 STATIC_SCRATCH_BYTES = 4 << 20      # ATTN_DECODE_STATIC_SCRATCH_BYTES
@@ -67,6 +68,7 @@ SIGNATURES = {
     "attn_fwd": (None, [P, P, P, P, P]),
     "attn_bwd": (None, [P, P, P, P, P, P, P, P, P]),
     "attn_set_macro_shape": (I, [I, I, I, I]),
+    "attn_set_probs_mode": (I, [I]),
     "attn_fwd_ex": (I, [ctypes.POINTER(Shape), I, P, P, P, P, P, P]),
     "attn_bwd_workspace_bytes": (SZ, [ctypes.POINTER(Shape), I]),
     "attn_bwd_ex": (I, [ctypes.POINTER(Shape), I, P, P, P, P, P, P, P, P, P, I, P, SZ, P]),

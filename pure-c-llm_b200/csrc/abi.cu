@@ -10,6 +10,7 @@
 #include <functional>
 #include <map>
 #include <tuple>
+#include <unordered_map>
 #include <mutex>
 #include <queue>
 #include <utility>
@@ -314,14 +315,22 @@ void dropin_bwd(float *dQ, float *dK, float *dV, float *scratch, const float *dA
 extern "C" {
 
 static attn_shape g_macro = {ATTN_B_SIZE, ATTN_N_HEADS, ATTN_T_SIZE, ATTN_D_HEAD, 0, 0};
+static int g_probs_mode = ATTN_PROBS_LSE_OUT;
 
 int attn_set_macro_shape(int batch, int heads, int seq_len, int head_dim) {
     if (batch < 1 || heads < 1 || seq_len < 1 || !head_dim_ok(head_dim))
         return set_error(ATTN_ERR_INVALID, "bad macro shape B=%d H=%d T=%d d=%d", batch, heads, seq_len, head_dim);
-    if (seq_len < head_dim + 1)
+    if (g_probs_mode == ATTN_PROBS_LSE_OUT && seq_len < head_dim + 1)
         return set_error(ATTN_ERR_UNSUPPORTED,
                          "attn_fwd keeps lse + output in `probs`; needs T >= d+1 (T=%d d=%d)", seq_len, head_dim);
     g_macro = {batch, heads, seq_len, head_dim, 0, 0};
+    return ATTN_OK;
+}
+
+int attn_set_probs_mode(int mode) {
+    if (mode != ATTN_PROBS_LSE_OUT && mode != ATTN_PROBS_LSE)
+        return set_error(ATTN_ERR_INVALID, "probs mode %d: expected ATTN_PROBS_LSE_OUT or ATTN_PROBS_LSE", mode);
+    g_probs_mode = mode;
     return ATTN_OK;
 }
 
@@ -349,13 +358,28 @@ namespace attn_host {
 // Bodies of the drop-ins, shared by the C symbols above and the C++-linkage
 // symbols of abi_cxx.cu (train_kaggle.cu and gpu_kernels.h are compiled as
 // CUDA C++, so an unchanged trainer references the mangled names).
+// ATTN_PROBS_LSE mode: the output buffer each `probs` buffer's forward wrote
+// (the backward reads the output from there).  A trainer has one entry per
+// layer; the table is bounded so that a caller cycling through fresh buffers
+// cannot grow it without end.
+static std::mutex g_probs_mu;
+static std::unordered_map<const float *, const float *> g_probs_att;
+constexpr size_t kProbsEntries = 4096;
+
 void dropin_fwd(const float *Q, const float *K, const float *V, float *att, float *probs) {
     const attn_shape &s = g_macro;
-    if (s.seq_len < s.head_dim + 1) die_on(set_error(ATTN_ERR_UNSUPPORTED, "T < d+1"), "attn_fwd");
-    // probs layout: [lse: B*H*T][copy of att: B*T*H*d]
+    const bool lse_only = g_probs_mode == ATTN_PROBS_LSE;
+    if (!lse_only && s.seq_len < s.head_dim + 1) die_on(set_error(ATTN_ERR_UNSUPPORTED, "T < d+1"), "attn_fwd");
+    // probs layout: [lse: B*H*T] then, unless lse_only, [copy of att: B*T*H*d]
     float *lse = probs;
-    float *ocopy = probs + (size_t)s.batch * s.heads * s.seq_len;
     die_on(attn_fwd_ex(&s, ATTN_F32, Q, K, V, att, lse, nullptr), "attn_fwd");
+    if (lse_only) {
+        std::lock_guard<std::mutex> g(g_probs_mu);
+        if (g_probs_att.size() >= kProbsEntries && !g_probs_att.count(probs)) g_probs_att.clear();
+        g_probs_att[probs] = att;
+        return;
+    }
+    float *ocopy = probs + (size_t)s.batch * s.heads * s.seq_len;
     const size_t bytes = (size_t)s.batch * s.seq_len * s.heads * s.head_dim * sizeof(float);
     cudaError_t e = cudaMemcpyAsync(ocopy, att, bytes, cudaMemcpyDeviceToDevice, nullptr);
     if (e != cudaSuccess) die_on(set_error(ATTN_ERR_CUDA, "%s", cudaGetErrorString(e)), "attn_fwd");
@@ -365,9 +389,19 @@ void dropin_bwd(float *dQ, float *dK, float *dV, float *scratch, const float *dA
                 const float *K, const float *V, const float *probs) {
     const attn_shape &s = g_macro;
     const float *lse = probs;
-    const float *ocopy = probs + (size_t)s.batch * s.heads * s.seq_len;
-    const size_t ws_bytes = (size_t)s.batch * s.heads * s.seq_len * s.seq_len * sizeof(float);
-    die_on(attn_bwd_ex(&s, ATTN_F32, dAtt, Q, K, V, ocopy, lse, dQ, dK, dV, 0, scratch, ws_bytes, nullptr),
+    const float *out = probs + (size_t)s.batch * s.heads * s.seq_len;
+    if (g_probs_mode == ATTN_PROBS_LSE) {
+        std::lock_guard<std::mutex> g(g_probs_mu);
+        auto it = g_probs_att.find(probs);
+        if (it == g_probs_att.end())
+            die_on(set_error(ATTN_ERR_INVALID, "attn_bwd: no attn_fwd has filled this `probs` buffer "
+                                               "(ATTN_PROBS_LSE mode)"), "attn_bwd");
+        out = it->second;
+    }
+    // the caller's scratch holds at least what the backward needs (the
+    // reference allocates B*H*T*T floats; a shrunk trainer 2*B*H*T)
+    const size_t ws_bytes = attn_bwd_workspace_bytes(&s, ATTN_F32);
+    die_on(attn_bwd_ex(&s, ATTN_F32, dAtt, Q, K, V, out, lse, dQ, dK, dV, 0, scratch, ws_bytes, nullptr),
            "attn_bwd");
 }
 

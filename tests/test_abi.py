@@ -94,3 +94,27 @@ def test_drop_in_probs_buffer_is_large_enough_at_reference_shape():
     B, H, T, d = 4, 12, 1024, 128
     assert B * H * T * T >= B * H * T + B * T * H * d
     assert A.lib.attn_set_macro_shape(B, H, T, d) == A.OK
+
+
+def test_probs_mode_validation_needs_no_gpu():
+    assert A.lib.attn_set_probs_mode(5) == A.ERR_INVALID
+    assert A.lib.attn_set_probs_mode(A.PROBS_LSE) == A.OK
+    try:
+        # probs holds only the log-sum-exp, so T < d+1 is allowed
+        assert A.lib.attn_set_macro_shape(4, 12, 64, 128) == A.OK
+    finally:
+        assert A.lib.attn_set_probs_mode(A.PROBS_LSE_OUT) == A.OK
+        assert A.lib.attn_set_macro_shape(4, 12, 1024, 128) == A.OK
+
+
+def test_lse_mode_backward_of_an_unfilled_probs_buffer_exits():
+    """attn_bwd in ATTN_PROBS_LSE mode with a `probs` that no attn_fwd filled
+    stops with the drop-ins' CUDA_CHECK-style exit(1) before any device call."""
+    import subprocess
+    import sys
+    code = ("import sys; sys.path.insert(0, %r); import attn_b200 as A; "
+            "A.lib.attn_set_probs_mode(A.PROBS_LSE); "
+            "A.lib.attn_bwd(16, 16, 16, 16, 16, 16, 16, 16, 4096)") % os.path.dirname(A.__file__)
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=120)
+    assert r.returncode == 1
+    assert "no attn_fwd has filled this `probs` buffer" in r.stderr

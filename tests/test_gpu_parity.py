@@ -254,6 +254,44 @@ def test_drop_in_fwd_bwd(A):
         A.lib.attn_set_macro_shape(4, 12, 1024, 128)
 
 
+@pytest.mark.parametrize("B,H,T,d", [(1, 2, 1536, 128), (2, 3, 100, 128), (1, 2, 40, 64)])
+def test_drop_in_lse_only_probs(A, B, H, T, d):
+    """ATTN_PROBS_LSE: `probs` shrinks to B*H*T floats and `scratch` to the
+    backward's workspace (the trainer-side edit that drops train_kaggle.cu's
+    B*H*T*T a_probs and s_Dbuf), T < d+1 included; nothing past those sizes is
+    written, and the backward reads the output from `att`."""
+    import torch
+    A.check(A.lib.attn_set_probs_mode(A.PROBS_LSE))
+    try:
+        A.check(A.lib.attn_set_macro_shape(B, H, T, d))
+        q, k, v = qkv(23, B, T, H, d)
+        do = synth.normal(24, q.shape)
+        ref, probs, _ = O.attn_forward(q, k, v, B, T, H, d, want_probs=True)
+        rq, rk, rv = O.attn_backward(do, q, k, v, probs, B, T, H, d)
+        qd, kd, vd, gd = dev(q), dev(k), dev(v), dev(do)
+        att = torch.empty_like(qd)
+        n_lse = B * H * T
+        n_ws = A.bwd_workspace_bytes(A.Shape(B, H, T, d, 0, 0), A.F32) // 4
+        canary = 1234.5
+        probs_buf = torch.full((n_lse + 4096,), canary, device="cuda")
+        scratch = torch.full((n_ws + 4096,), canary, device="cuda")
+        dq, dk, dv = (torch.full_like(qd, 7.0) for _ in range(3))
+        torch.cuda.synchronize()
+        A.lib.attn_fwd(qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), att.data_ptr(), probs_buf.data_ptr())
+        A.lib.attn_bwd(dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), scratch.data_ptr(), gd.data_ptr(),
+                       qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), probs_buf.data_ptr())
+        torch.cuda.synchronize()
+        assert rel_err(host(att), ref) < F32_TOL
+        assert rel_err(host(dq), rq) < F32_TOL
+        assert rel_err(host(dk), rk) < F32_TOL
+        assert rel_err(host(dv), rv) < F32_TOL
+        assert bool((probs_buf[n_lse:] == canary).all())
+        assert bool((scratch[n_ws:] == canary).all())
+    finally:
+        A.lib.attn_set_probs_mode(A.PROBS_LSE_OUT)
+        A.lib.attn_set_macro_shape(4, 12, 1024, 128)
+
+
 # ---------------------------------------------------------------------------
 # decode
 # ---------------------------------------------------------------------------

@@ -69,3 +69,36 @@ def test_unguarded_trainer_still_builds_on_its_own(tmp_path):
     defined = subprocess.run(["nm", "-C", "--defined-only", str(tmp_path / "g.o")], capture_output=True,
                              text=True).stdout
     assert "attn_fwd(float const*" in defined
+
+
+# The trainer-side edit that drops the B*H*T*T activation buffers: a_probs
+# keeps only the log-sum-exp (ATTN_PROBS_LSE) and s_Dbuf only the backward's
+# workspace.  Each replacement must match exactly once in the reference file.
+SHRINK_EDITS = [
+    ('#include "gpu_kernels.h"\n',
+     '#include "gpu_kernels.h"\n#define ATTN_OMIT_MACRO_DROPINS\n#include "attn_b200.h"\n'),
+    ("static void alloc_acts(void) {\n",
+     "static void alloc_acts(void) {\n    if (attn_set_probs_mode(ATTN_PROBS_LSE) != ATTN_OK) exit(1);\n"),
+    ("long PB = (long)B_SIZE * N_HEADS * T_SIZE * T_SIZE;",
+     "long PB = (long)B_SIZE * N_HEADS * T_SIZE;"),
+    ("s_Dbuf = dmalloc((long)B_SIZE * N_HEADS * T_SIZE * T_SIZE);",
+     "s_Dbuf = dmalloc(2L * B_SIZE * N_HEADS * T_SIZE);"),
+]
+
+
+def test_trainer_with_shrunk_attention_buffers_links(tmp_path):
+    _ref_or_skip()
+    _guarded_copy(tmp_path)
+    src = open(tmp_path / "train_kaggle.cu").read()
+    for old, new in SHRINK_EDITS:
+        assert src.count(old) == 1, old
+        src = src.replace(old, new)
+    open(tmp_path / "train_kaggle.cu", "w").write(src)
+    exe = tmp_path / "train_gpu_lse"
+    cmd = ["nvcc", "-O1", "-arch=sm_100a", "-DATTN_EXTERNAL", f"-I{os.path.join(ROOT, 'include')}", "-o", str(exe),
+           "train_kaggle.cu", "gpu_kernels.cu", f"-L{PKG}", "-lattn_b200", "-lcublas", "-Xlinker", f"-rpath={PKG}"]
+    r = subprocess.run(cmd, cwd=tmp_path, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stdout + r.stderr
+    undef = subprocess.run(["nm", "-C", "--undefined-only", str(exe)], capture_output=True, text=True).stdout
+    assert "attn_set_probs_mode" in undef
+    assert "attn_fwd(float const*, float const*, float const*, float*, float*)" in undef
