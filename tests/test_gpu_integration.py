@@ -1,4 +1,5 @@
-"""The reference's decoder block with its attention on the GPU.
+"""The reference's decoder block, GPU trainer and C generator with their
+attention on this library.
 
 tests/integration/ builds transformer.c's forward_block (transformer.c:251-285)
 twice from the reference sources: unmodified (block_ref, the CPU reference)
@@ -6,8 +7,20 @@ and with its attention call routed to attn_cached_attention_host (block_gpu,
 the maintainer's one-line edit).  Both run 16 layers x 128 tokens at the C1
 decode shape (d_model 512 = 16 x 32, 512 cached rows before the first token)
 from the same seed; every token's residual vector and last attention output
-must agree within the fp32 tolerance.  The programs are prebuilt, so this
-test needs the GPU and not the reference tree."""
+must agree within the fp32 tolerance.
+
+It also builds the reference's GPU trainer (train_kaggle.cu + gpu_kernels.cu,
+the 343M model of gpu_kernels.h) with its own cuBLAS attention, with the
+library's attn_fwd / attn_bwd linked in, and with the drop-ins plus the
+trainer's T*T buffers shrunk (lse-only probs mode); and the reference's C
+generator (generate.c) with its attention loop as it is and routed to
+attn_cached_attention_host_ex.  The trainers run the same steps on the same
+token stream and must report the same losses; the drop-in trainer's weights,
+written as the CKP1 checkpoint the generator loads, then decode to the same
+logits and the same greedy tokens through both generators.
+
+The programs are prebuilt, so these tests need the GPU and not the reference
+tree."""
 import os
 import subprocess
 
@@ -36,3 +49,54 @@ def test_forward_block_routed_to_gpu_matches_reference(cuda, tmp_path):
         a, b = outs["gpu"][:, which].astype(np.float64), outs["ref"][:, which].astype(np.float64)
         err = np.abs(a - b).max(axis=1) / np.maximum(np.abs(b).max(axis=1), 1e-6)
         assert err.max() < F32_TOL, (which, err.max(), int(err.argmax()))
+
+
+TRAIN_STEPS = 40
+LOSS_TOL = 1e-4          # relative, any step (measured on a B200: <= 4.5e-6)
+LOGITS_TOL = 1e-4        # max|gpu - ref| / max|ref| over every step (measured 1.9e-6)
+
+
+def _tokens(path):
+    """A seeded low-entropy stream the model can learn within a few dozen
+    steps: 64 random 16-token phrases over the 2048-token vocabulary, drawn
+    in random order (40,000 tokens, uint16 like the reference's train.bin)."""
+    rng = np.random.default_rng(7)
+    phrases = rng.integers(0, 2048, size=(64, 16), dtype=np.uint16)
+    order = rng.integers(0, 64, size=40000 // 16 + 1)
+    np.concatenate([phrases[i] for i in order])[:40000].astype(np.uint16).tofile(path)
+
+
+def test_reference_trainer_and_generator_on_the_library(cuda, tmp_path):
+    exes = {n: os.path.join(BUILD, n) for n in
+            ("trainer_ref", "trainer_gpu", "trainer_lse", "generate_ref", "generate_gpu")}
+    if not all(os.path.exists(e) for e in exes.values()):
+        pytest.skip("integration programs not built (the reference tree was absent at build time)")
+    env = dict(os.environ, OMP_NUM_THREADS=str(os.cpu_count() or 1))
+    tokens = tmp_path / "tokens.bin"
+    _tokens(tokens)
+    ckp1 = tmp_path / "model.ckp1"
+    losses = {}
+    for v in ("ref", "gpu", "lse"):
+        out = tmp_path / f"losses_{v}.txt"
+        cmd = [exes["trainer_" + v], str(TRAIN_STEPS), str(tokens), str(out)] + ([str(ckp1)] if v == "gpu" else [])
+        r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=900)
+        assert r.returncode == 0, (v, r.stdout[-2000:], r.stderr[-2000:])
+        losses[v] = np.loadtxt(out)
+        assert losses[v].shape == (TRAIN_STEPS,)
+    assert losses["ref"][-1] < losses["ref"][0] - 2.0          # the model learned the phrases
+    for v in ("gpu", "lse"):
+        err = np.abs(losses[v] - losses["ref"]) / np.abs(losses["ref"])
+        assert err.max() < LOSS_TOL, (v, err.max(), int(err.argmax()))
+
+    # the drop-in trainer's checkpoint through the reference generator, both ways
+    prompt = ["5", "17", "300", "42", "1000", "7"]
+    logits = {}
+    for v in ("ref", "gpu"):
+        out = tmp_path / f"logits_{v}.bin"
+        r = subprocess.run([exes["generate_" + v], str(ckp1), "24", str(out)] + prompt, env=env,
+                           capture_output=True, text=True, timeout=900)
+        assert r.returncode == 0, (v, r.stderr[-2000:])
+        logits[v] = np.fromfile(out, dtype=np.float32).reshape(24, 2048).astype(np.float64)
+    a, b = logits["gpu"], logits["ref"]
+    assert np.abs(a - b).max() / np.abs(b).max() < LOGITS_TOL
+    assert (a.argmax(axis=1) == b.argmax(axis=1)).all()

@@ -99,6 +99,44 @@ def test_forward_strided_heads_subset(A):
     assert rel_err(host(out), ref[:, h0 * d:(h0 + hn) * d]) < F32_TOL
 
 
+@pytest.mark.parametrize("dt,d", [("f32", 64), ("bf16", 64), ("f32", 128)])
+def test_fused_qkv_layout(A, dt, d):
+    """Q, K and V as the three column blocks of one (B*T, 3*H*d) projection
+    output (a fused Wq|Wk|Wv GEMM), and dQ, dK, dV written into the column
+    blocks of one gradient tensor of that width: the kernels take the row
+    stride through their tensor maps, so no head-major copy is needed."""
+    import torch
+    B, T, H = 2, 200, 3
+    q, k, v = qkv(31, B, T, H, d)
+    do = synth.normal(32, (B * T, H * d))
+    tdt, code = (torch.float32, A.F32) if dt == "f32" else (torch.bfloat16, A.BF16)
+    ftol, btol = (F32_TOL, F32_TOL) if dt == "f32" else (BF16_FWD_TOL, BF16_BWD_TOL)
+    if dt == "bf16":
+        q, k, v, do = (bf16_round(x) for x in (q, k, v, do))
+    ref, probs, _ = O.attn_forward(q, k, v, B, T, H, d, want_probs=True)
+    rq, rk, rv = O.attn_backward(do, q, k, v, probs, B, T, H, d)
+    W = 3 * H * d
+    qkv_d = torch.cat([torch.as_tensor(x, device="cuda") for x in (q, k, v)], dim=1).to(tdt).contiguous()
+    o_d = torch.zeros((B * T, W), dtype=tdt, device="cuda")
+    g_d = torch.zeros((B * T, W), dtype=tdt, device="cuda")
+    g_d[:, :H * d] = torch.as_tensor(do, device="cuda").to(tdt)
+    lse = torch.zeros(B * H * T, device="cuda")
+    shape = A.Shape(B, H, T, d, W, W)
+    col = lambda t, i: t[:, i * H * d:].data_ptr()          # noqa: E731
+    A.fwd_ex(shape, code, col(qkv_d, 0), col(qkv_d, 1), col(qkv_d, 2), col(o_d, 0), lse.data_ptr())
+    dqkv = torch.full((B * T, W), 7.0, dtype=tdt, device="cuda")
+    ws = torch.zeros(A.bwd_workspace_bytes(shape, code), dtype=torch.uint8, device="cuda")
+    A.check(A.lib.attn_bwd_ex(ctypes.byref(shape), code, col(g_d, 0), col(qkv_d, 0), col(qkv_d, 1),
+                              col(qkv_d, 2), col(o_d, 0), lse.data_ptr(), col(dqkv, 0), col(dqkv, 1),
+                              col(dqkv, 2), 0, ws.data_ptr(), ws.numel(), None))
+    torch.cuda.synchronize()
+    h = lambda t, i: host(t[:, i * H * d:(i + 1) * H * d].float())   # noqa: E731
+    assert rel_err(h(o_d, 0), ref) < ftol
+    assert bool((o_d[:, H * d:] == 0).all())                 # only O's own columns are written
+    for i, r in enumerate((rq, rk, rv)):
+        assert rel_err(h(dqkv, i), r) < btol
+
+
 def test_forward_deterministic(A):
     q, k, v = qkv(3, 2, 300, 2, 64)
     a, _ = A.forward_t(dev(q), dev(k), dev(v), 2, 2)

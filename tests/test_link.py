@@ -8,6 +8,7 @@ the reference tree is absent."""
 import os
 import shutil
 import subprocess
+import sys
 
 import pytest
 
@@ -16,7 +17,8 @@ from conftest import PKG, ROOT
 import __graft_entry__ as G
 
 REF = G.REFERENCE_DIR
-GUARD_FIRST, GUARD_LAST = 253, 489        # gpu_kernels.cu: the attention section
+sys.path.insert(0, os.path.join(ROOT, "tests", "integration"))
+import ref_edits  # noqa: E402
 
 
 def _ref_or_skip():
@@ -27,12 +29,8 @@ def _ref_or_skip():
 
 
 def _guarded_copy(dst):
-    lines = open(os.path.join(REF, "gpu_kernels.cu")).read().split("\n")
-    assert lines[GUARD_FIRST - 1].startswith("/* ========================== attention")
-    assert lines[GUARD_LAST - 1] == "}" and "embeddings" in lines[GUARD_LAST + 1]
-    lines.insert(GUARD_LAST, "#endif /* ATTN_EXTERNAL */")
-    lines.insert(GUARD_FIRST - 1, "#ifndef ATTN_EXTERNAL")
-    open(os.path.join(dst, "gpu_kernels.cu"), "w").write("\n".join(lines))
+    text = open(os.path.join(REF, "gpu_kernels.cu")).read()
+    open(os.path.join(dst, "gpu_kernels.cu"), "w").write(ref_edits.guard_gpu_kernels(text))
     for f in ("gpu_kernels.h", "train_kaggle.cu"):
         shutil.copy(os.path.join(REF, f), dst)
 
@@ -71,28 +69,11 @@ def test_unguarded_trainer_still_builds_on_its_own(tmp_path):
     assert "attn_fwd(float const*" in defined
 
 
-# The trainer-side edit that drops the B*H*T*T activation buffers: a_probs
-# keeps only the log-sum-exp (ATTN_PROBS_LSE) and s_Dbuf only the backward's
-# workspace.  Each replacement must match exactly once in the reference file.
-SHRINK_EDITS = [
-    ('#include "gpu_kernels.h"\n',
-     '#include "gpu_kernels.h"\n#define ATTN_OMIT_MACRO_DROPINS\n#include "attn_b200.h"\n'),
-    ("static void alloc_acts(void) {\n",
-     "static void alloc_acts(void) {\n    if (attn_set_probs_mode(ATTN_PROBS_LSE) != ATTN_OK) exit(1);\n"),
-    ("long PB = (long)B_SIZE * N_HEADS * T_SIZE * T_SIZE;",
-     "long PB = (long)B_SIZE * N_HEADS * T_SIZE;"),
-    ("s_Dbuf = dmalloc((long)B_SIZE * N_HEADS * T_SIZE * T_SIZE);",
-     "s_Dbuf = dmalloc(2L * B_SIZE * N_HEADS * T_SIZE);"),
-]
-
-
 def test_trainer_with_shrunk_attention_buffers_links(tmp_path):
     _ref_or_skip()
     _guarded_copy(tmp_path)
-    src = open(tmp_path / "train_kaggle.cu").read()
-    for old, new in SHRINK_EDITS:
-        assert src.count(old) == 1, old
-        src = src.replace(old, new)
+    # the trainer-side edit that drops the B*H*T*T activation buffers
+    src = ref_edits.shrink_trainer(open(tmp_path / "train_kaggle.cu").read())
     open(tmp_path / "train_kaggle.cu", "w").write(src)
     exe = tmp_path / "train_gpu_lse"
     cmd = ["nvcc", "-O1", "-arch=sm_100a", "-DATTN_EXTERNAL", f"-I{os.path.join(ROOT, 'include')}", "-o", str(exe),
