@@ -788,17 +788,7 @@ def run_ours(args, keys):
     import attn_b200 as A
     if world > 1:
         import shard
-        # NCCL may print its version line at communicator set-up; rank 0's
-        # stdout must carry the JSON line only, so set-up writes go to stderr
-        sys.stdout.flush()
-        saved = os.dup(1)
-        os.dup2(2, 1)
-        try:
-            shard.init_group(rank, world, local)
-        finally:
-            ctypes.CDLL(None).fflush(None)
-            os.dup2(saved, 1)
-            os.close(saved)
+        shard.init_group(rank, world, local)
     ctx = dict(torch=torch, dist=dist, A=A, world=world, rank=rank, local=local, dev=dev)
     results = {}
     for key in keys:
@@ -828,7 +818,24 @@ def reference_config(key, args):
             "e2e": {"value": round(value, 6), "unit": s.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
+def json_stream():
+    """Rank 0's stdout carries the JSON line and nothing else.  Native code
+    prints on file descriptor 1 too (NCCL its version line when a communicator
+    is set up, with NCCL_DEBUG set), so descriptor 1 is pointed at stderr for
+    the whole run and the line goes to a duplicate of the original stdout."""
+    sys.stdout.flush()
+    out = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
+    return out
+
+
+def emit(out, line):
+    out.write(json.dumps(line) + "\n")
+    out.flush()
+
+
 def main():
+    out = json_stream()
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
@@ -851,11 +858,11 @@ def main():
         try:
             from oracle import oracle as O
             if not O.ref_available():
-                print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref not built (reference sources "
-                                  "absent at build time)"}), flush=True)
+                emit(out, {"impl": "reference", "unavailable": "oracle/_ref not built (reference sources "
+                                "absent at build time)"})
                 return
         except Exception as e:  # pragma: no cover
-            print(json.dumps({"impl": "reference", "unavailable": f"oracle import failed: {e}"}), flush=True)
+            emit(out, {"impl": "reference", "unavailable": f"oracle import failed: {e}"})
             return
         per = {k: reference_config(k, args) for k in keys}
         top = dict(per[head])
@@ -869,7 +876,7 @@ def main():
             line["headline"] = f"{head}: {top['metric']}"
             line["configs"] = {k: {kk: vv for kk, vv in v.items() if kk != "config"} | {"config": config_block(k, world)}
                                for k, v in per.items()}
-        print(json.dumps(line), flush=True)
+        emit(out, line)
         return
 
     res = run_ours(args, keys)
@@ -888,7 +895,7 @@ def main():
         line["configs"] = {k: {kk: vv for kk, vv in r.items()
                                if kk not in ("steps", "warmup", "n_gpus", "higher_is_better", "vs_baseline")}
                            for k, r in res.items()}
-    print(json.dumps(line), flush=True)
+    emit(out, line)
 
 
 def config_block(key, world):
