@@ -26,13 +26,15 @@
 //               its S row, keeps the running max (rescaling O only when it
 //               grows by more than 2^8) and sum, and writes P's high part over
 //               the S row it read and P's low part to a separate TMEM block
-// TMEM (256 columns): S/Ph buffers [0,64) and [64,128), Pl [128,192), O
-// [192, 192+D).  An S buffer is reused once the PV that read its P finished.
-// Head dims 96 and 128: the split query tile would not fit in shared memory
-// next to a two-stage ring, so it lives in TMEM (Qh in columns [0,D), Ql in
-// [D,2D); the S products read their A operand from TMEM) and key tiles are
-// 32 rows; the splitters move each landed query tile from its shared-memory
-// staging buffer into TMEM (512 columns: Q parts, two S buffers, Pl, O).
+// TMEM (d 32: 256 columns): S/Ph buffers [0,64) and [64,128), Pl [128,192),
+// O [192, 192+D).  An S buffer is reused once the PV that read its P finished.
+// Head dims 64 and up: the split query tile lives in TMEM (Qh in columns
+// [0,D), Ql in [D,2D); the S products read their A operand from TMEM, so the
+// tensor core does not re-read it from shared memory for every key tile), and
+// the splitters move each landed query tile from its shared-memory staging
+// buffer into TMEM (512 columns: Q parts, two S buffers, Pl, O, running O).
+// At d 96 and 128 the split tile would not fit in shared memory next to a
+// two-stage ring anyway; there key tiles are 32 rows.
 // Every mbarrier wait is bounded; a timeout records a code in the device
 // error word, raises a CTA-wide abort flag, and all roles fall through to the
 // teardown, which frees TMEM.
@@ -57,10 +59,13 @@ constexpr int kMaxItems = 32768;
 constexpr int kLocalItems = 256;
 constexpr int kFold = 4;           // key tiles per fresh PV sum (see Cfg)
 
+#ifndef ATTN_TF32_QT_MIN_D
+#define ATTN_TF32_QT_MIN_D 64
+#endif
 template <int D>
 struct Cfg {
-    static constexpr bool QT = D > 64;              // query parts in TMEM
-    static constexpr int BN = QT ? 32 : 64;         // keys per tile
+    static constexpr bool QT = D >= ATTN_TF32_QT_MIN_D;   // query parts in TMEM
+    static constexpr int BN = D > 64 ? 32 : 64;     // keys per tile
     static constexpr int CH = D / 32;               // 128-byte column chunks of a row
     static constexpr int QB = BM * D * 4;           // one fp32 Q tile (high or low part)
     static constexpr int KB = BN * D * 4;           // one fp32 K or V tile
@@ -189,6 +194,10 @@ __device__ __forceinline__ void split_hi_lo(float *hi, float *lo, int n, int tid
         *reinterpret_cast<float4 *>(hi + i) = h;
         *reinterpret_cast<float4 *>(lo + i) = l;
     }
+}
+
+__device__ __forceinline__ float f4_at(const float4 &v, int c) {
+    return c == 0 ? v.x : c == 1 ? v.y : c == 2 ? v.z : v.w;
 }
 
 template <int D>
@@ -426,29 +435,73 @@ fwd_tf32_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
                     uint8_t *s0 = sb + C::OFF_ST + st * C::STAGE;
                     split_hi_lo(reinterpret_cast<float *>(s0), reinterpret_cast<float *>(s0 + C::KB), BN * D, tid,
                                 128);                                                     // K
-                    // V: raw tile (TMA, 128-byte swizzle, [64 keys][32-dim chunks]) ->
+                    // V: raw tile (TMA, 128-byte swizzle, [BN keys][32-dim chunks]) ->
                     // V^T high and low parts ([D rows][32-key chunks], same swizzle).
                     // All raw values are read before the low part overwrites them.
-                    constexpr int PER = BN * D / 128;
-                    float vr[PER];
                     uint8_t *vraw = s0 + 2 * C::KB;
+                    if constexpr ((BN * D / 16) % 128 == 0) {
+                        // By 4x4 micro-blocks with 16-byte loads and stores: a 32-key x
+                        // 32-dim block holds an 8x8 grid of them (key group a, dim group
+                        // b), and the 8 lanes of each quarter-warp take one diagonal,
+                        // b = a + p (mod 8), so under either swizzle their loads hit 8
+                        // different 16-byte bank groups, and so do their stores (one
+                        // element per lane, as before, put 4 lanes on each bank).
+                        constexpr int MB = BN * D / 16 / 128;    // micro-blocks per thread
+                        float4 vr[MB][4];
 #pragma unroll
-                    for (int i = 0; i < PER; i++) {
-                        const int idx = tid + 128 * i, key = idx / D, dim = idx % D;
-                        vr[i] = *reinterpret_cast<const float *>(
-                            vraw + (dim >> 5) * (BN * 128) + key * 128 + ((((dim & 31) >> 2) ^ (key & 7)) << 4) +
-                            (dim & 3) * 4);
-                    }
-                    mbar_arrive(BAR(B_SPL));
-                    if (!(ok = wait_w(B_SPL, t, 0x433))) break;
+                        for (int u = 0; u < MB; u++) {
+                            const int m = tid + 128 * u, blk = m >> 6, a = m & 7, b = (a + ((m & 63) >> 3)) & 7;
+                            const int c32 = blk % (D / 32), k32 = blk / (D / 32);
 #pragma unroll
-                    for (int i = 0; i < PER; i++) {
-                        const int idx = tid + 128 * i, key = idx / D, dim = idx % D;
-                        const int off = (key >> 5) * (D * 128) + dim * 128 + ((((key & 31) >> 2) ^ (dim & 7)) << 4) +
-                                        (key & 3) * 4;
-                        const float h = __uint_as_float(__float_as_uint(vr[i]) & 0xFFFFE000u);
-                        *reinterpret_cast<float *>(s0 + 3 * C::KB + off) = h;           // V^T high
-                        *reinterpret_cast<float *>(vraw + off) = vr[i] - h;             // V^T low
+                            for (int r = 0; r < 4; r++) {
+                                const int key = 32 * k32 + 4 * a + r;
+                                vr[u][r] = *reinterpret_cast<const float4 *>(vraw + c32 * (BN * 128) + key * 128 +
+                                                                             ((b ^ (key & 7)) << 4));
+                            }
+                        }
+                        mbar_arrive(BAR(B_SPL));
+                        if (!(ok = wait_w(B_SPL, t, 0x433))) break;
+#pragma unroll
+                        for (int u = 0; u < MB; u++) {
+                            const int m = tid + 128 * u, blk = m >> 6, a = m & 7, b = (a + ((m & 63) >> 3)) & 7;
+                            const int c32 = blk % (D / 32), k32 = blk / (D / 32);
+#pragma unroll
+                            for (int c = 0; c < 4; c++) {
+                                const int dim = 32 * c32 + 4 * b + c;
+                                const int off = k32 * (D * 128) + dim * 128 + ((a ^ (dim & 7)) << 4);
+                                const float x[4] = {f4_at(vr[u][0], c), f4_at(vr[u][1], c), f4_at(vr[u][2], c),
+                                                    f4_at(vr[u][3], c)};
+                                float h[4], l[4];
+#pragma unroll
+                                for (int r = 0; r < 4; r++) {
+                                    h[r] = __uint_as_float(__float_as_uint(x[r]) & 0xFFFFE000u);
+                                    l[r] = x[r] - h[r];
+                                }
+                                *reinterpret_cast<float4 *>(s0 + 3 * C::KB + off) = make_float4(h[0], h[1], h[2], h[3]);
+                                *reinterpret_cast<float4 *>(vraw + off) = make_float4(l[0], l[1], l[2], l[3]);
+                            }
+                        }
+                    } else {
+                        constexpr int PER = BN * D / 128;
+                        float vr[PER];
+#pragma unroll
+                        for (int i = 0; i < PER; i++) {
+                            const int idx = tid + 128 * i, key = idx / D, dim = idx % D;
+                            vr[i] = *reinterpret_cast<const float *>(
+                                vraw + (dim >> 5) * (BN * 128) + key * 128 + ((((dim & 31) >> 2) ^ (key & 7)) << 4) +
+                                (dim & 3) * 4);
+                        }
+                        mbar_arrive(BAR(B_SPL));
+                        if (!(ok = wait_w(B_SPL, t, 0x433))) break;
+#pragma unroll
+                        for (int i = 0; i < PER; i++) {
+                            const int idx = tid + 128 * i, key = idx / D, dim = idx % D;
+                            const int off = (key >> 5) * (D * 128) + dim * 128 + ((((key & 31) >> 2) ^ (dim & 7)) << 4) +
+                                            (key & 3) * 4;
+                            const float h = __uint_as_float(__float_as_uint(vr[i]) & 0xFFFFE000u);
+                            *reinterpret_cast<float *>(s0 + 3 * C::KB + off) = h;           // V^T high
+                            *reinterpret_cast<float *>(vraw + off) = vr[i] - h;             // V^T low
+                        }
                     }
                     fence_async_smem();
                     mbar_arrive(BAR(B_KVS + st));
