@@ -15,13 +15,17 @@
 //         X = K Q_i^T, Y = V dO_i^T;  dV += P^T dO_i,  dK += dS^T Q_i
 //   dq:   fixed Q, dO; streamed K_j, V_j (j up to the diagonal).
 //         X = Q K_j^T, Y = dO V_j^T;  dQ += dS K_j
-// The fixed pair lives in TMEM as high and low parts (the X/Y products read
-// their A operand from TMEM); each streamed tile lands raw in shared memory,
+// The fixed pair's high parts live in TMEM and its low parts in shared memory
+// (split in place in the tiles it was loaded into); the X/Y products read
+// their A operand from there.  Each streamed tile lands raw in shared memory,
 // where splitter warps clear the low bits in place, write the low parts and
 // the transposed high and low parts the accumulation products need (all B
 // operands K-major).  The elementwise warpgroup writes P and dS high parts
 // over X and Y in TMEM and their low parts beside them; the accumulation
-// products read them as their A operand.
+// products read them as their A operand.  X/Y and those parts have two TMEM
+// buffers (by streamed-tile parity), so the next tile's X/Y products run
+// while the elementwise warpgroup works on this one and the tensor core
+// accumulates the one before.
 // Warps: 0 TMA producer; 1 X/Y issuer; 2 accumulation issuer; 3 idle; 4-7
 // splitters; 8-11 elementwise (one thread per TMEM lane = fixed-tile row).
 // Every mbarrier wait is bounded (device error word + abort flag).
@@ -29,6 +33,7 @@
 #include "sm100.cuh"
 
 #include <cudaTypedefs.h>
+#include <type_traits>
 
 namespace attn {
 namespace fbt {
@@ -43,8 +48,7 @@ constexpr int kGroupBH = 16;      // (batch, head) pairs per group of the unit o
 // thousands of products a dK/dV/dQ row gathers at T = 4096 that drifts by
 // ~5e-5.  So the accumulators restart every kGroup streamed tiles (96
 // accumulation steps, ~4e-6 at worst) and the elementwise warpgroup adds each
-// group's sums into fp32 running sums in shared memory (in the fixed tiles'
-// staging area, free once they are in TMEM).
+// group's sums into fp32 running sums in registers (a thread owns one row).
 constexpr int kGroup = 8;
 
 template <int D>
@@ -52,27 +56,34 @@ struct Cfg {
     static constexpr int CH = D / 32;               // 128-byte column chunks of a row
     static constexpr int FB = BT * D * 4;           // one raw fixed tile
     static constexpr int SB = BS * D * 4;           // one part of a streamed tile
-    // shared memory: two raw fixed tiles, 2 stages x (C hi, C lo, C^T hi, C^T lo,
-    // D hi, D lo, D^T hi, D^T lo), 2 stages x row statistics (dkdv), barriers
+    // shared memory: the two fixed tiles (raw, then their low parts), 2 stages x
+    // (C hi, C lo, C^T hi, C^T lo, D hi, D lo, D^T hi, D^T lo), 2 stages x row
+    // statistics (dkdv), barriers
     static constexpr int OFF_FA = 0, OFF_FB = FB;
-    static constexpr int RS_PITCH = D + 1;          // floats per running-sum row (conflict-free columns)
-    static constexpr int RS_BYTES = 2 * BT * RS_PITCH * 4;    // dV and dK (dQ: the first half)
-    static constexpr int OFF_ST = ((2 * FB > RS_BYTES ? 2 * FB : RS_BYTES) + 1023) / 1024 * 1024;
+    static constexpr int OFF_ST = (2 * FB + 1023) / 1024 * 1024;
     static constexpr int STAGE = 8 * SB;
     static constexpr int OFF_STATS = OFF_ST + 2 * STAGE;
     static constexpr int OFF_BAR = OFF_STATS + 2 * 2 * BS * 4;
     static constexpr int SMEM = OFF_BAR + 256 + 1024;
-    // TMEM columns: fixed A and B (high, low), X, Y (P / dS high parts written
-    // over them), P and dS low parts, accumulators
-    static constexpr int TM_AH = 0, TM_AL = D, TM_BH = 2 * D, TM_BL = 3 * D;
-    static constexpr int TM_X = 4 * D, TM_Y = TM_X + BS, TM_W1L = TM_Y + BS, TM_W2L = TM_W1L + BS;
-    static constexpr int TM_A1 = TM_W2L + BS, TM_A2 = TM_A1 + D, TM_COLS = 512;
+    // TMEM columns: the fixed A and B high parts; two buffers of X, Y (P / dS
+    // high parts written over them) and the P and dS low parts; accumulators
+    static constexpr int TM_AH = 0, TM_BH = D, TM_XY = 2 * D, XYB = 4 * BS;
+    static constexpr int TM_A1 = TM_XY + 2 * XYB, TM_A2 = TM_A1 + D, TM_COLS = 512;
     static_assert(TM_A2 + D <= TM_COLS, "TMEM budget");
     static_assert(SMEM <= 232448, "shared memory");
 };
+// column of X (0), Y (1), P low (2) or dS low (3) in X/Y buffer b
+template <int D>
+__device__ __forceinline__ uint32_t xy_col(int b, int which) {
+    return (uint32_t)(Cfg<D>::TM_XY + b * Cfg<D>::XYB + which * BS);
+}
 
 // barrier slots
-enum { B_FXF = 0, B_FX, B_SF, B_SS = B_SF + 2, B_SE = B_SS + 2, B_XY = B_SE + 2, B_W, B_ACC, B_ST, B_AF, B_COUNT };
+enum {
+    B_FXF = 0, B_FX, B_SF, B_SS = B_SF + 2, B_SE = B_SS + 2,   // fixed tiles; stages (2 each)
+    B_XY = B_SE + 2, B_W = B_XY + 2, B_ACC = B_W + 2,           // per X/Y buffer (2 each)
+    B_ST = B_ACC + 2, B_AF, B_COUNT
+};
 
 struct Params {
     float *out1, *out2;          // dkdv: dK, dV;  dq: dQ
@@ -85,6 +96,9 @@ struct Params {
 };
 
 __device__ __forceinline__ uint32_t hi_bits(float x) { return __float_as_uint(x) & 0xFFFFE000u; }
+__device__ __forceinline__ float f4_at(const float4 &v, int c) {
+    return c == 0 ? v.x : c == 1 ? v.y : c == 2 ? v.z : v.w;
+}
 
 // KIND 0: dkdv, KIND 1: dq.  m_a/m_b: the fixed pair (128-row boxes), m_c/m_d:
 // the streamed pair (32-row boxes); 3-D {H*D, T, B} views, 32-float x rows
@@ -133,9 +147,11 @@ bwd_tf32_kernel(const __grid_constant__ CUtensorMap m_a, const __grid_constant__
             mbar_init(BAR(B_SS + s), 128);
             mbar_init(BAR(B_SE + s), 1);
         }
-        mbar_init(BAR(B_XY), 1);
-        mbar_init(BAR(B_W), 128);
-        mbar_init(BAR(B_ACC), 1);
+        for (int x = 0; x < 2; x++) {
+            mbar_init(BAR(B_XY + x), 1);
+            mbar_init(BAR(B_W + x), 128);
+            mbar_init(BAR(B_ACC + x), 1);
+        }
         mbar_init(BAR(B_ST), 128);
         mbar_init(BAR(B_AF), 128);
         *abort_flag = 0;
@@ -154,8 +170,9 @@ bwd_tf32_kernel(const __grid_constant__ CUtensorMap m_a, const __grid_constant__
     };
 
     // registers: 384 x 168 at launch; warpgroup 0 gives back down to 64, the
-    // splitters keep 168 and the elementwise warpgroup rises to 232
-    // (128 x (64 + 168 + 232) = 59392 <= 384 x 168 = 64512)
+    // splitters down to 144, and the elementwise warpgroup (which keeps its
+    // rows' running sums in registers) rises to 256
+    // (128 x (64 + 144 + 256) = 59392 <= 384 x 168 = 64512)
     if (warp < 4) regs_dec<64>();
     if (warp == 0) {
         // ------------------------------------------------------------ producer
@@ -185,37 +202,42 @@ bwd_tf32_kernel(const __grid_constant__ CUtensorMap m_a, const __grid_constant__
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------ X/Y issuer
-        // X = A C^T, Y = B D^T (M = 128 fixed rows, N = 32, K = d); A and B from
-        // TMEM, C and D K-major in shared memory.  The previous tile's
-        // accumulations read P/dS high parts from the X/Y columns, so they must
-        // have finished.
+        // X = A C^T, Y = B D^T (M = 128 fixed rows, N = 32, K = d) into X/Y buffer
+        // it & 1: the high parts of A and B from TMEM, their low parts and C and D
+        // (K-major) from shared memory.  The buffer's previous tile (it - 2) must
+        // have been accumulated: its P/dS parts live in these columns.
         const bool leader = elect_one();
         constexpr uint32_t idXY = idesc_tf32(BT, BS, 0, 0);
         bool ok = wait_w(B_FX, 0, 0x511);
         for (int it = 0; ok && it < count; it++) {
-            const int st = it & 1;
+            const int st = it & 1, xb = it & 1;
             if (!(ok = wait_w(B_SS + st, it >> 1, 0x512))) break;
-            if (it > 0 && !(ok = wait_w(B_ACC, it - 1, 0x513))) break;
+            if (it >= 2 && !(ok = wait_w(B_ACC + xb, (it >> 1) - 1, 0x513))) break;
             tc_fence_after();
             const uint32_t sbase = base + C::OFF_ST + st * C::STAGE;
             if (leader) {
 #pragma unroll
                 for (int xy = 0; xy < 2; xy++) {
                     const uint32_t hi = sbase + (xy ? 4 : 0) * C::SB, lo = hi + C::SB;
-                    const uint32_t fa_h = tmem + (xy ? C::TM_BH : C::TM_AH), fa_l = tmem + (xy ? C::TM_BL : C::TM_AL);
-                    const uint32_t d_t = tmem + (xy ? C::TM_Y : C::TM_X);
+                    const uint32_t fa_h = tmem + (xy ? C::TM_BH : C::TM_AH);
+                    const uint32_t fa_l = base + (xy ? C::OFF_FB : C::OFF_FA);
+                    const uint32_t d_t = tmem + xy_col<D>(xb, xy);
 #pragma unroll
                     for (int part = 0; part < 3; part++) {       // hh, hl, lh
-                        const uint32_t fa = part == 2 ? fa_l : fa_h;
                         const uint32_t sv = part == 1 ? lo : hi;
 #pragma unroll
                         for (int kk = 0; kk < D / 8; kk++) {
                             const uint64_t bd = sw128_desc(sv + (kk >> 2) * (BS * 128) + (kk & 3) * 32, 16, 1024);
-                            mma_tf32_ts(d_t, fa + 8 * kk, bd, idXY, (part > 0 || kk > 0));
+                            if (part < 2) {
+                                mma_tf32_ts(d_t, fa_h + 8 * kk, bd, idXY, (part > 0 || kk > 0));
+                            } else {
+                                const uint64_t ad = sw128_desc(fa_l + (kk >> 2) * (BT * 128) + (kk & 3) * 32, 16, 1024);
+                                mma_tf32_ss(d_t, ad, bd, idXY, true);
+                            }
                         }
                     }
                 }
-                mma_commit(BAR(B_XY));
+                mma_commit(BAR(B_XY + xb));
             }
             __syncwarp();
         }
@@ -227,8 +249,8 @@ bwd_tf32_kernel(const __grid_constant__ CUtensorMap m_a, const __grid_constant__
         const bool leader = elect_one();
         constexpr uint32_t idAcc = idesc_tf32(BT, D, 0, 0);
         for (int it = 0; it < count; it++) {
-            const int st = it & 1;
-            if (!wait_w(B_W, it, 0x515)) break;
+            const int st = it & 1, xb = it & 1;
+            if (!wait_w(B_W + xb, it >> 1, 0x515)) break;
             // a new group overwrites the accumulators: the previous group's sums were read
             if (it >= kGroup && it % kGroup == 0 && !wait_w(B_AF, it / kGroup - 1, 0x516)) break;
             tc_fence_after();
@@ -239,8 +261,8 @@ bwd_tf32_kernel(const __grid_constant__ CUtensorMap m_a, const __grid_constant__
                     // dkdv a=0: dV from P (X cols) and dO^T;  a=1: dK from dS (Y cols) and Q^T
                     // dq: dQ from dS (Y cols) and K^T
                     const bool use_p = KIND == 0 && a == 0;
-                    const uint32_t wh = tmem + (use_p ? C::TM_X : C::TM_Y);
-                    const uint32_t wl = tmem + (use_p ? C::TM_W1L : C::TM_W2L);
+                    const uint32_t wh = tmem + xy_col<D>(xb, use_p ? 0 : 1);
+                    const uint32_t wl = tmem + xy_col<D>(xb, use_p ? 2 : 3);
                     const uint32_t th = sbase + (use_p ? 6 : 2) * C::SB, tl = th + C::SB;   // (D or C)^T hi, lo
                     const uint32_t acc = tmem + (a ? C::TM_A2 : C::TM_A1);
 #pragma unroll
@@ -254,38 +276,43 @@ bwd_tf32_kernel(const __grid_constant__ CUtensorMap m_a, const __grid_constant__
                         }
                     }
                 }
-                mma_commit(BAR(B_ACC));
+                mma_commit(BAR(B_ACC + xb));
                 mma_commit(BAR(B_SE + st));             // the stage's X/Y products finished before W
             }
             __syncwarp();
         }
     } else if (warp >= 4 && warp < 8) {
         // ------------------------------------------------------------ splitters
+        regs_dec<144>();
         const int quad = warp & 3, row = quad * 32 + lane;
         const uint32_t lb = (uint32_t)(quad * 32) << 16;
         bool ok = wait_w(B_FXF, 0, 0x531);
         if (ok) {
-            // fixed tiles -> TMEM high and low parts, 16 columns at a time
+            // fixed tiles: high parts -> TMEM, low parts written over the raw values
+            // in shared memory (each thread its own row), 16 columns at a time
 #pragma unroll 1
             for (int g = 0; g < 2 * 2 * C::CH; g++) {
                 const int f = g / (2 * C::CH), c = (g / 2) % C::CH, hh = g & 1;   // tile, chunk, half chunk
-                uint32_t hi[16], lo[16];
-                const uint8_t *src = sb + (f ? C::OFF_FB : C::OFF_FA) + c * (BT * 128) + row * 128;
+                uint32_t hi[16];
+                uint8_t *src = sb + (f ? C::OFF_FB : C::OFF_FA) + c * (BT * 128) + row * 128;
 #pragma unroll
                 for (int j = 0; j < 4; j++) {
-                    const float4 x = *reinterpret_cast<const float4 *>(src + (((4 * hh + j) ^ (row & 7)) << 4));
+                    float4 *px = reinterpret_cast<float4 *>(src + (((4 * hh + j) ^ (row & 7)) << 4));
+                    const float4 x = *px;
                     const float xv[4] = {x.x, x.y, x.z, x.w};
+                    float lv[4];
 #pragma unroll
                     for (int u = 0; u < 4; u++) {
                         const uint32_t hb = hi_bits(xv[u]);
                         hi[4 * j + u] = hb;
-                        lo[4 * j + u] = __float_as_uint(xv[u] - __uint_as_float(hb));
+                        lv[u] = xv[u] - __uint_as_float(hb);
                     }
+                    *px = make_float4(lv[0], lv[1], lv[2], lv[3]);
                 }
                 tmem_st16(tmem + lb + (f ? C::TM_BH : C::TM_AH) + 32 * c + 16 * hh, hi);
-                tmem_st16(tmem + lb + (f ? C::TM_BL : C::TM_AL) + 32 * c + 16 * hh, lo);
             }
             tmem_wait_st();
+            fence_async_smem();                      // the low parts are MMA operands
             tc_fence_before();
             mbar_arrive(BAR(B_FX));
         }
@@ -294,34 +321,44 @@ bwd_tf32_kernel(const __grid_constant__ CUtensorMap m_a, const __grid_constant__
         // only).  Raw tile layout (TMA): chunk c of 32 columns at c*(BS*128),
         // row r at r*128, 16-byte unit u at (u ^ (r & 7)) << 4.  Transposed:
         // [D rows][32 streamed rows], row = column index, same swizzle.
-        constexpr int PER = BS * D / 128;            // values per thread per part
+        // By 4x4 micro-blocks with 16-byte loads and stores: a part's 32-row x
+        // 32-column block holds an 8x8 grid of them (row group a, column group
+        // b), and the 8 lanes of each quarter-warp take one diagonal, b = a + p
+        // (mod 8), so their loads and in-place stores hit 8 different 16-byte
+        // bank groups of the swizzled rows, and so do their transposed stores.
+        constexpr int NMB = 2 * (D / 32) * 64;       // micro-blocks of both parts
+        const int tid = threadIdx.x - 128;
         for (int it = 0; ok && it < count; it++) {
             const int st = it & 1;
             if (!(ok = wait_w(B_SF + st, it >> 1, 0x532))) break;
             uint8_t *s0 = sb + C::OFF_ST + st * C::STAGE;
 #pragma unroll
-            for (int part = 0; part < 2; part++) {
+            for (int u = 0; u < NMB / 128; u++) {
+                const int m = tid + 128 * u, part = m / (NMB / 2), e = m % (NMB / 2);
+                const int blk = e >> 6, a = e & 7, bcol = (a + ((e & 63) >> 3)) & 7;
                 uint8_t *hi = s0 + (part ? 4 : 0) * C::SB, *lo = hi + C::SB;
                 uint8_t *th = hi + 2 * C::SB, *tl = hi + 3 * C::SB;
-                const bool transpose = KIND == 0 || part == 0;
-                // a warp instruction covers 4 rows x 8 columns: conflict-free both for
-                // the row-major reads and writes and for the transposed writes (the
-                // 16-byte units of 8 transposed rows x 4 words spread over all banks)
+                float4 h4[4], l4[4];
 #pragma unroll
-                for (int i = 0; i < PER; i++) {
-                    const int blk = (warp & 3) + 4 * i;            // block of 4 rows x 8 columns
-                    const int r = 4 * (blk % (BS / 4)) + (lane >> 3), col = 8 * (blk / (BS / 4)) + (lane & 7);
-                    const int off = (col >> 5) * (BS * 128) + r * 128 + ((((col & 31) >> 2) ^ (r & 7)) << 4) +
-                                    (col & 3) * 4;
-                    const float x = *reinterpret_cast<const float *>(hi + off);
-                    const float xh = __uint_as_float(hi_bits(x));
-                    const float xl = x - xh;
-                    *reinterpret_cast<float *>(hi + off) = xh;
-                    *reinterpret_cast<float *>(lo + off) = xl;
-                    if (transpose) {
-                        const int toff = col * 128 + (((r >> 2) ^ (col & 7)) << 4) + (r & 3) * 4;
-                        *reinterpret_cast<float *>(th + toff) = xh;
-                        *reinterpret_cast<float *>(tl + toff) = xl;
+                for (int i = 0; i < 4; i++) {
+                    const int r = 4 * a + i;
+                    const int off = blk * (BS * 128) + r * 128 + ((bcol ^ (r & 7)) << 4);
+                    const float4 x = *reinterpret_cast<const float4 *>(hi + off);
+                    h4[i] = make_float4(__uint_as_float(hi_bits(x.x)), __uint_as_float(hi_bits(x.y)),
+                                        __uint_as_float(hi_bits(x.z)), __uint_as_float(hi_bits(x.w)));
+                    l4[i] = make_float4(x.x - h4[i].x, x.y - h4[i].y, x.z - h4[i].z, x.w - h4[i].w);
+                    *reinterpret_cast<float4 *>(hi + off) = h4[i];
+                    *reinterpret_cast<float4 *>(lo + off) = l4[i];
+                }
+                if (KIND == 0 || part == 0) {
+#pragma unroll
+                    for (int c = 0; c < 4; c++) {
+                        const int col = 32 * blk + 4 * bcol + c;
+                        const int toff = col * 128 + ((a ^ (col & 7)) << 4);
+                        *reinterpret_cast<float4 *>(th + toff) =
+                            make_float4(f4_at(h4[0], c), f4_at(h4[1], c), f4_at(h4[2], c), f4_at(h4[3], c));
+                        *reinterpret_cast<float4 *>(tl + toff) =
+                            make_float4(f4_at(l4[0], c), f4_at(l4[1], c), f4_at(l4[2], c), f4_at(l4[3], c));
                     }
                 }
             }
@@ -330,7 +367,7 @@ bwd_tf32_kernel(const __grid_constant__ CUtensorMap m_a, const __grid_constant__
         }
     } else if (warp >= 8) {
         // ------------------------------------------------------------ elementwise
-        regs_inc<232>();
+        regs_inc<256>();
         const int quad = warp & 3;
         const int row = quad * 32 + lane;            // TMEM lane = row of the fixed tile
         const uint32_t lb = (uint32_t)(quad * 32) << 16;
@@ -341,9 +378,17 @@ bwd_tf32_kernel(const __grid_constant__ CUtensorMap m_a, const __grid_constant__
             my_nl2 = -__ldg(p.lse2 + bh + grow_);
             my_ndd = -__ldg(p.dvec + bh + grow_) * p.ds_scale;
         }
+        const uint64_t scale2 = f2(p.scale_log2, p.scale_log2), ds2 = f2(p.ds_scale, p.ds_scale);
+        constexpr int NA = KIND == 0 ? 2 : 1;        // accumulators: dkdv dV, dK; dq dQ
+        float rs[NA][D];                             // this row's running sums
+#pragma unroll
+        for (int a = 0; a < NA; a++)
+#pragma unroll
+            for (int c = 0; c < D; c++) rs[a][c] = 0.f;
         bool ok = true;
         for (int it = 0; it < count; it++) {
             const int tcol = first + it;             // streamed tile index
+            const int xb = it & 1;                   // X/Y buffer
             float *st_l = stats + (it & 1) * 2 * BS;   // dkdv: -lse2 and -D/sqrt(d) of the 32 query columns
             if (KIND == 0) {
                 if (row < BS) {
@@ -354,62 +399,100 @@ bwd_tf32_kernel(const __grid_constant__ CUtensorMap m_a, const __grid_constant__
                 mbar_arrive(BAR(B_ST));
                 if (!(ok = wait_w(B_ST, it, 0x543))) break;
             }
-            if (!(ok = wait_w(B_XY, it, 0x541))) break;
+            if (!(ok = wait_w(B_XY + xb, it >> 1, 0x541))) break;
             tc_fence_after();
-            // P = 2^(X scale - lse2), dS = P (Y - D) / sqrt(d); masked outside the
-            // causal triangle and past T.  16 columns at a time (all X/Y reads of a
-            // half complete before its P/dS high parts overwrite them).
+            const uint32_t tX = tmem + lb + xy_col<D>(xb, 0), tY = tmem + lb + xy_col<D>(xb, 1);
+            const uint32_t tW1L = tmem + lb + xy_col<D>(xb, 2), tW2L = tmem + lb + xy_col<D>(xb, 3);
+            // P = 2^(X scale - lse2), dS = P (Y - D) / sqrt(d), on f32x2 pairs; the
+            // causal and past-T masks only in tiles that reach them.  16 columns
+            // at a time (all X/Y reads of a half complete before its P/dS high
+            // parts overwrite them).
+            const bool need_mask = KIND == 0 ? (tcol * BS < fixed * BT + BT - 1 || (tcol + 1) * BS > p.T)
+                                             : ((tcol + 1) * BS - 1 > fixed * BT);
+            auto tile = [&](auto masked_tag) {
+                constexpr bool MASKED = decltype(masked_tag)::value;
 #pragma unroll
-            for (int h2 = 0; h2 < 2; h2++) {
-                uint32_t xs[16], ys[16];
-                tmem_ld16(tmem + lb + C::TM_X + 16 * h2, xs);
-                tmem_ld16(tmem + lb + C::TM_Y + 16 * h2, ys);
-                tmem_wait_ld();
-                uint32_t ph[16], pl[16], dh[16], dl[16];
+                for (int h2 = 0; h2 < 2; h2++) {
+                    uint32_t xs[16], ys[16];
+                    tmem_ld16(tX + 16 * h2, xs);
+                    tmem_ld16(tY + 16 * h2, ys);
+                    tmem_wait_ld();
+                    // P first (its parts stored while Y is still in registers), then dS
+                    float pv[16];
 #pragma unroll
-                for (int c = 0; c < 16; c++) {
-                    const int cc = 16 * h2 + c;
-                    const int sidx = tcol * BS + cc;     // streamed row (dkdv: query, dq: key)
-                    const float nl2 = KIND == 0 ? st_l[cc] : my_nl2;
-                    const float ndd = KIND == 0 ? st_l[BS + cc] : my_ndd;
-                    const bool masked = KIND == 0 ? (sidx < grow_ || sidx >= p.T) : (sidx > grow_);
-                    const float pv = masked ? 0.f : ex2(fmaf(__uint_as_float(xs[c]), p.scale_log2, nl2));
-                    // query 0 attends to key 0 alone: P = 1 and dS = dP - D = 0 exactly
-                    // (train.c:393-400 forms the row dot from P and dP, so it gets the exact zero;
-                    // D = dO . O from the pre-pass would leave the products' 1e-7)
-                    const bool q0 = KIND == 0 ? sidx == 0 : grow_ == 0;
-                    const float dv = q0 ? 0.f : pv * fmaf(__uint_as_float(ys[c]), p.ds_scale, ndd);
-                    const uint32_t phb = hi_bits(pv), dhb = hi_bits(dv);
-                    ph[c] = phb;
-                    pl[c] = __float_as_uint(pv - __uint_as_float(phb));
-                    dh[c] = dhb;
-                    dl[c] = __float_as_uint(dv - __uint_as_float(dhb));
+                    for (int c = 0; c < 16; c += 2) {
+                        const int cc = 16 * h2 + c;
+                        const uint64_t nl2 = KIND == 0 ? *reinterpret_cast<const uint64_t *>(st_l + cc)   // query columns
+                                                       : f2(my_nl2, my_nl2);                              // this query row
+                        f2_split(fma2(f2(__uint_as_float(xs[c]), __uint_as_float(xs[c + 1])), scale2, nl2), pv[c],
+                                 pv[c + 1]);
+                        pv[c] = ex2(pv[c]);
+                        pv[c + 1] = ex2(pv[c + 1]);
+                        if (MASKED) {
+#pragma unroll
+                            for (int u = 0; u < 2; u++) {
+                                const int sidx = tcol * BS + cc + u;   // streamed row (dkdv: query, dq: key)
+                                if (KIND == 0 ? (sidx < grow_ || sidx >= p.T) : (sidx > grow_)) pv[c + u] = 0.f;
+                            }
+                        }
+                    }
+                    if (KIND == 0) {
+                        uint32_t ph[16], pl[16];
+#pragma unroll
+                        for (int c = 0; c < 16; c++) {
+                            ph[c] = hi_bits(pv[c]);
+                            pl[c] = __float_as_uint(pv[c] - __uint_as_float(ph[c]));
+                        }
+                        tmem_st16(tX + 16 * h2, ph);
+                        tmem_st16(tW1L + 16 * h2, pl);
+                    }
+                    uint32_t dh[16], dl[16];
+#pragma unroll
+                    for (int c = 0; c < 16; c += 2) {
+                        const int cc = 16 * h2 + c;
+                        const uint64_t ndd = KIND == 0 ? *reinterpret_cast<const uint64_t *>(st_l + BS + cc)
+                                                       : f2(my_ndd, my_ndd);
+                        const uint64_t t2 = fma2(f2(__uint_as_float(ys[c]), __uint_as_float(ys[c + 1])), ds2, ndd);
+                        float dv[2];
+                        f2_split(fma2(f2(pv[c], pv[c + 1]), t2, 0ull), dv[0], dv[1]);
+                        if (MASKED) {
+                            // query 0 attends to key 0 alone: P = 1 and dS = dP - D = 0
+                            // exactly (train.c:393-400 forms the row dot from P and dP,
+                            // so it gets the exact zero; D = dO . O from the pre-pass
+                            // would leave the products' 1e-7)
+#pragma unroll
+                            for (int u = 0; u < 2; u++)
+                                if (KIND == 0 ? tcol * BS + cc + u == 0 : grow_ == 0) dv[u] = 0.f;
+                        }
+#pragma unroll
+                        for (int u = 0; u < 2; u++) {
+                            dh[c + u] = hi_bits(dv[u]);
+                            dl[c + u] = __float_as_uint(dv[u] - __uint_as_float(dh[c + u]));
+                        }
+                    }
+                    tmem_st16(tY + 16 * h2, dh);
+                    tmem_st16(tW2L + 16 * h2, dl);
                 }
-                if (KIND == 0) {
-                    tmem_st16(tmem + lb + C::TM_X + 16 * h2, ph);
-                    tmem_st16(tmem + lb + C::TM_W1L + 16 * h2, pl);
-                }
-                tmem_st16(tmem + lb + C::TM_Y + 16 * h2, dh);
-                tmem_st16(tmem + lb + C::TM_W2L + 16 * h2, dl);
-            }
+            };
+            if (need_mask) tile(std::true_type{});
+            else tile(std::false_type{});
             tmem_wait_st();
             tc_fence_before();
-            mbar_arrive(BAR(B_W));
+            mbar_arrive(BAR(B_W + xb));
             if (it % kGroup == kGroup - 1 || it == count - 1) {
-                // the group's sums -> fp32 running sums (this thread's row), then
-                // the accumulators are free for the next group
-                if (!(ok = wait_w(B_ACC, it, 0x545))) break;
+                // the group's sums (complete with this tile's accumulation) -> the
+                // running sums, then the accumulators are free for the next group
+                if (!(ok = wait_w(B_ACC + xb, it >> 1, 0x545))) break;
                 tc_fence_after();
-                for (int a = 0; a < (KIND == 0 ? 2 : 1); a++) {
-                    float *rs = reinterpret_cast<float *>(sb + C::OFF_FA) + (a * BT + row) * C::RS_PITCH;
-#pragma unroll 1
+#pragma unroll
+                for (int a = 0; a < NA; a++) {
+#pragma unroll
                     for (int c0 = 0; c0 < D; c0 += 16) {
                         uint32_t acc[16];
                         tmem_ld16(tmem + lb + (a ? C::TM_A2 : C::TM_A1) + c0, acc);
                         tmem_wait_ld();
 #pragma unroll
-                        for (int c = 0; c < 16; c++)
-                            rs[c0 + c] = (it < kGroup ? 0.f : rs[c0 + c]) + __uint_as_float(acc[c]);
+                        for (int c = 0; c < 16; c++) rs[a][c0 + c] += __uint_as_float(acc[c]);
                     }
                 }
                 tc_fence_before();
@@ -418,14 +501,14 @@ bwd_tf32_kernel(const __grid_constant__ CUtensorMap m_a, const __grid_constant__
         }
         // epilogue: running sums -> global (fp32, optionally added to the output)
         if (__all_sync(0xffffffffu, ok && count > 0) && grow_ < p.T) {
-            for (int a = 0; a < (KIND == 0 ? 2 : 1); a++) {
+#pragma unroll
+            for (int a = 0; a < NA; a++) {
                 // dkdv: a=0 -> dV (out2), a=1 -> dK (out1);  dq: dQ (out1)
                 float *outp = KIND == 0 ? (a == 0 ? p.out2 : p.out1) : p.out1;
                 float *dst = outp + ((long long)b * p.T + grow_) * p.out_stride + (long long)h * D;
-                const float *rs = reinterpret_cast<const float *>(sb + C::OFF_FA) + (a * BT + row) * C::RS_PITCH;
 #pragma unroll
                 for (int c = 0; c < D; c += 4) {
-                    float4 v = make_float4(rs[c], rs[c + 1], rs[c + 2], rs[c + 3]);
+                    float4 v = make_float4(rs[a][c], rs[a][c + 1], rs[a][c + 2], rs[a][c + 3]);
                     float4 *d4 = reinterpret_cast<float4 *>(dst + c);
                     if (p.accumulate) {
                         const float4 o = *d4;

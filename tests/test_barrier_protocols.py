@@ -294,6 +294,89 @@ def test_bwd_bf16_persistent_protocol(kind):
         assert not hazards, (counts, hazards[:3])
 
 
+# ---------------------------------------------------------------------------
+# bwd_tf32_sm100.cu: one unit of `count` streamed tiles through a 2-stage ring;
+# X/Y (and the P/dS parts written over them) double-buffered in TMEM by tile
+# parity, so tile it+1's X/Y products run while tile it is in the elementwise
+# warpgroup; accumulators restart every `group` tiles once the elementwise
+# warpgroup has folded them into its running sums
+# ---------------------------------------------------------------------------
+def _bwd_tf32_roles(count, kind, group):
+    def make(bar, W, A):
+        bar("FXF")
+        bar("FX", 2)
+        for s in range(2):
+            bar(("SF", s))
+            bar(("SS", s), 2)
+            bar(("SE", s))
+            bar(("XY", s))
+            bar(("W", s), 2)
+            bar(("ACC", s))
+        bar("ST", 2)
+        bar("AF", 2)
+
+        def producer():
+            yield A("FXF")
+            for it in range(count):
+                st = it & 1
+                if it >= 2:
+                    yield W(("SE", st), it >> 1)
+                yield A(("SF", st))
+
+        def splitter():
+            yield W("FXF", 1)
+            yield A("FX")
+            for it in range(count):
+                st = it & 1
+                yield W(("SF", st), (it >> 1) + 1)
+                yield A(("SS", st))
+
+        def xy():
+            yield W("FX", 1)
+            for it in range(count):
+                b = it & 1
+                yield W(("SS", b), (it >> 1) + 1)
+                if it >= 2:
+                    yield W(("ACC", b), it >> 1)        # the buffer's previous tile was accumulated
+                yield A(("XY", b))
+
+        def acc():
+            for it in range(count):
+                b = it & 1
+                yield W(("W", b), (it >> 1) + 1)
+                if it >= group and it % group == 0:
+                    yield W("AF", it // group)
+                yield A(("ACC", b))
+                yield A(("SE", b))
+
+        def elementwise():
+            for it in range(count):
+                b = it & 1
+                if kind == 0:
+                    yield A("ST")
+                    yield W("ST", it + 1)
+                yield W(("XY", b), (it >> 1) + 1)
+                yield A(("W", b))
+                if it % group == group - 1 or it == count - 1:
+                    yield W(("ACC", b), (it >> 1) + 1)
+                    yield A("AF")
+
+        return [("producer", producer()), ("splitter0", splitter()), ("splitter1", splitter()),
+                ("xy", xy()), ("acc", acc()), ("elementwise0", elementwise()), ("elementwise1", elementwise())]
+    return make
+
+
+@pytest.mark.parametrize("kind", [0, 1])
+@pytest.mark.parametrize("group", [1, 2, 3, 8])
+def test_bwd_tf32_double_buffered_protocol(kind, group):
+    for trial in range(150):
+        rnd = random.Random(trial * 7 + group)
+        count = rnd.randint(1, 40)
+        dead, hazards = _run(_bwd_tf32_roles(count, kind, group), trial)
+        assert dead is None, (count, dead)
+        assert not hazards, (count, hazards[:3])
+
+
 def test_models_catch_a_missing_wait():
     """The checker itself: without the producer's wait for a free fixed-tile
     buffer, the backward model must report a parity hazard."""
@@ -318,3 +401,4 @@ def test_models_catch_a_missing_wait():
             found = True
             break
     assert found
+
