@@ -11,6 +11,7 @@
 // groups.
 #pragma once
 #include "common.cuh"
+#include "sm100.cuh"
 
 namespace attn {
 
@@ -96,7 +97,9 @@ __device__ __forceinline__ void store_weights_T(float *Wt, const float (&w)[4][8
 }
 
 // out[i][c] += sum_n W[ty+16i][n] * M[n][4tx + 32(c/4) + c%4]; W given as Wt
-// from store_weights_T, M a padded row-major 64 x D tile.
+// from store_weights_T, M a padded row-major 64 x D tile.  The products run on
+// f32x2 pairs (two adjacent output columns per fma.rn.f32x2, each lane rounded
+// as fmaf would), so a warp issues half the FMA instructions.
 template <int D>
 __device__ __forceinline__ void tile_wM(float (&out)[4][D / 8], const float *Wt, const float *M,
                                         int ty, int tx)
@@ -105,25 +108,20 @@ __device__ __forceinline__ void tile_wM(float (&out)[4][D / 8], const float *Wt,
 #pragma unroll 4
     for (int n = 0; n < kFBN; n++) {
         const float4 w = *reinterpret_cast<const float4 *>(Wt + n * (kFBM + 4) + 4 * ty);
+        const uint64_t wb[4] = {sm100::f2(w.x, w.x), sm100::f2(w.y, w.y), sm100::f2(w.z, w.z), sm100::f2(w.w, w.w)};
 #pragma unroll
         for (int c = 0; c < D / 32; c++) {
             const float4 m = *reinterpret_cast<const float4 *>(M + n * LD + 4 * tx + 32 * c);
-            out[0][4 * c + 0] = fmaf(w.x, m.x, out[0][4 * c + 0]);
-            out[0][4 * c + 1] = fmaf(w.x, m.y, out[0][4 * c + 1]);
-            out[0][4 * c + 2] = fmaf(w.x, m.z, out[0][4 * c + 2]);
-            out[0][4 * c + 3] = fmaf(w.x, m.w, out[0][4 * c + 3]);
-            out[1][4 * c + 0] = fmaf(w.y, m.x, out[1][4 * c + 0]);
-            out[1][4 * c + 1] = fmaf(w.y, m.y, out[1][4 * c + 1]);
-            out[1][4 * c + 2] = fmaf(w.y, m.z, out[1][4 * c + 2]);
-            out[1][4 * c + 3] = fmaf(w.y, m.w, out[1][4 * c + 3]);
-            out[2][4 * c + 0] = fmaf(w.z, m.x, out[2][4 * c + 0]);
-            out[2][4 * c + 1] = fmaf(w.z, m.y, out[2][4 * c + 1]);
-            out[2][4 * c + 2] = fmaf(w.z, m.z, out[2][4 * c + 2]);
-            out[2][4 * c + 3] = fmaf(w.z, m.w, out[2][4 * c + 3]);
-            out[3][4 * c + 0] = fmaf(w.w, m.x, out[3][4 * c + 0]);
-            out[3][4 * c + 1] = fmaf(w.w, m.y, out[3][4 * c + 1]);
-            out[3][4 * c + 2] = fmaf(w.w, m.z, out[3][4 * c + 2]);
-            out[3][4 * c + 3] = fmaf(w.w, m.w, out[3][4 * c + 3]);
+            const uint64_t mlo = sm100::f2(m.x, m.y), mhi = sm100::f2(m.z, m.w);
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                uint64_t lo = sm100::f2(out[i][4 * c + 0], out[i][4 * c + 1]);
+                uint64_t hi = sm100::f2(out[i][4 * c + 2], out[i][4 * c + 3]);
+                lo = sm100::fma2(wb[i], mlo, lo);
+                hi = sm100::fma2(wb[i], mhi, hi);
+                sm100::f2_split(lo, out[i][4 * c + 0], out[i][4 * c + 1]);
+                sm100::f2_split(hi, out[i][4 * c + 2], out[i][4 * c + 3]);
+            }
         }
     }
 }
