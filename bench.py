@@ -11,6 +11,8 @@ measurements for every config:
   c3-f32   causal prefill fp32, d=64  / c3-bf16 in bf16    (TFLOP/s)
   c4-f32   ragged decode, fp32 cache / c4-int8 INT8 cache  (HBM GB/s)
   c5-f32   causal backward fp32 / c5-bf16 in bf16          (TFLOP/s)
+  trainer  the reference GPU trainer's attn_fwd + attn_bwd   (TFLOP/s)
+  qkv      its fused Q, K, V projection (one launch)        (TFLOP/s)
 --config <key> runs one of them alone.
 
 A step is one call of the path over one batch of synthetic input that is
@@ -78,8 +80,15 @@ CONFIGS = {
     "trainer": dict(kind="train", B=4, H=12, T=1024, d=128, dtype="f32",
                     workload="the reference GPU trainer's attention: attn_fwd + attn_bwd drop-ins at "
                              "gpu_kernels.h's shape B4 H12 T1024 d128, fp32"),
+    # not a BASELINE config: the fused QKV projection that feeds attn_fwd in the
+    # reference GPU trainer (train_kaggle.cu:152-154, three gemm_nn calls) at its
+    # shape, M = B*T = 4096 rows, DIM 1536
+    "qkv": dict(kind="qkv", M=4096, K=1536, N=1536, dtype="f32",
+                workload="the reference GPU trainer's Q, K, V projections (train_kaggle.cu:152-154) in one "
+                         "launch: X (4096 x 1536) times Wq, Wk, Wv (1536 x 1536) plus biases, fp32"),
 }
-ORDER = ["c3-bf16", "c1", "c2", "c3-f32", "c4-f32", "c4-int8", "c5-f32", "c5-bf16", "trainer"]
+ORDER = ["c3-bf16", "c1", "c2", "c3-f32", "c4-f32", "c4-int8", "c5-f32", "c5-bf16", "trainer", "qkv"]
+DENSE = ("fwd", "bwd", "train", "qkv")     # kinds measured in TFLOP/s
 HEADLINE = "c3-bf16"
 METRIC = "causal-attn prefill TFLOP/s & KV-decode HBM GB/s per B200 at 1/2/4/8 GPUs"
 L2_BYTES = 126 * 2 ** 20
@@ -91,17 +100,23 @@ def causal_flops(B, H, T, d):
     return 4.0 * B * H * d * T * (T + 1) / 2
 
 
+def qkv_flops(M, K, N):
+    """Three (M x K) @ (K x N) products."""
+    return 3 * 2.0 * M * K * N
+
+
 def metric_of(cfg):
     return {"fwd": "causal-attn prefill TFLOP/s", "bwd": "causal-attn backward TFLOP/s",
-            "train": "causal-attn forward+backward TFLOP/s"}.get(cfg["kind"], "KV-decode HBM GB/s")
+            "train": "causal-attn forward+backward TFLOP/s",
+            "qkv": "fused QKV projection TFLOP/s"}.get(cfg["kind"], "KV-decode HBM GB/s")
 
 
 def unit_of(cfg):
-    return "TFLOP/s" if cfg["kind"] in ("fwd", "bwd", "train") else "GB/s"
+    return "TFLOP/s" if cfg["kind"] in DENSE else "GB/s"
 
 
 def dtype_of(cfg):
-    if cfg["kind"] in ("fwd", "bwd", "train"):
+    if cfg["kind"] in DENSE:
         return cfg["dtype"]
     return "f32 (int8 cache)" if cfg.get("kv") == "int8" else "f32"
 
@@ -207,6 +222,16 @@ class CpuSample:
         self.O, self.cfg = O, cfg
         self.cores = _host_threads()
         kind = cfg["kind"]
+        if kind == "qkv":
+            M, K, N = 256, cfg["K"], cfg["N"]
+            self.x = synth.normal(1, (M, K))
+            self.ws = [synth.normal(2 + i, (K, N), 0, 0.02) for i in range(3)]
+            self.bs = [synth.normal(5 + i, (N,), 0, 0.1) for i in range(3)]
+            self.work = qkv_flops(M, K, N) / 1e12
+            self.unit = "TFLOP/s"
+            self.sample = (f"reference train.c matmul_forward x3 (the Q, K, V projections of train.c:517-519), "
+                           f"{M} of {cfg['M']} rows")
+            return
         if kind in ("fwd", "bwd", "train"):
             B, H, T, d = 1, cfg["H"], cfg["T"], cfg["d"]
             if kind == "bwd":
@@ -245,7 +270,10 @@ class CpuSample:
     def call(self):
         O, c = self.O, self.cfg
         t0 = time.perf_counter()
-        if c["kind"] == "fwd":
+        if c["kind"] == "qkv":
+            for w, b in zip(self.ws, self.bs):
+                O.ref_matmul_forward(self.x, w, b)
+        elif c["kind"] == "fwd":
             B, T, H, d = self.args
             O.ref_attention_forward(self.q, self.k, self.v, B, T, H, d)
         elif c["kind"] == "bwd":
@@ -286,7 +314,21 @@ class Workload:
         g = torch.Generator(device=dev).manual_seed(1234 + rank)
         self.gather_ok = world > 1 and kind in ("fwd", "decode", "ragged")
         self.gather_launches = 0
-        if kind in ("fwd", "bwd", "train"):
+        if kind == "qkv":
+            M, K, N = cfg["M"], cfg["K"], cfg["N"]
+            r0, r1 = A.shard_range(M, world, rank)           # token rows: no exchange needed
+            Ml = r1 - r0
+            self.x = torch.randn((Ml, K), generator=g, device=dev)
+            self.wq, self.wk, self.wv = (torch.randn((K, N), generator=g, device=dev) * 0.02 for _ in range(3))
+            self.bq, self.bk, self.bv = (torch.randn((N,), generator=g, device=dev) * 0.1 for _ in range(3))
+            self.q, self.k, self.v = (torch.empty((Ml, N), device=dev) for _ in range(3))
+            self.shape = A.QKVShape(Ml, K, N, 0, 0)
+            self.work = qkv_flops(Ml, K, N)
+            self.total_work = qkv_flops(M, K, N)
+            self.launches = 1
+            self.in_names, self.out_names = ["x"], ["q", "k", "v"]
+            self.local_desc = f"rows [{r0}, {r1}) of {M}"
+        elif kind in ("fwd", "bwd", "train"):
             B, H, T, d = cfg["B"], cfg["H"], cfg["T"], cfg["d"]
             self.sp = sp = A.split_plan(B, H, world, rank)
             Bl, Hl = sp.batch, sp.heads
@@ -404,14 +446,17 @@ class Workload:
             self.gather_launches = 1 if kind == "ragged" else 0
         self.working_set = self.work if kind in ("decode", "ragged") else \
             sum(getattr(self, a).numel() * getattr(self, a).element_size() for a in self.in_names + self.out_names)
+        if kind == "qkv":
+            self.working_set += 3 * self.wq.numel() * 4
         self.legacy_stream = kind == "train"     # the drop-ins run on the legacy default stream
 
     def unit_is_tflops(self):
-        return self.cfg["kind"] in ("fwd", "bwd", "train")
+        return self.cfg["kind"] in DENSE
 
     # device tensors a step reads or writes, per kind (the rotated input sets)
     _ROT = {"fwd": ("q", "k", "v", "o", "lse"), "bwd": ("q", "k", "v", "o", "lse", "do", "dq", "dk", "dv"),
-            "train": ("q", "k", "v", "o", "do", "dq", "dk", "dv"), "decode": ("kc", "vc", "kp", "vp"), "ragged": ()}
+            "train": ("q", "k", "v", "o", "do", "dq", "dk", "dv"), "decode": ("kc", "vc", "kp", "vp"), "ragged": (),
+            "qkv": ("x", "q", "k", "v")}
 
     def rotate_inputs(self, n):
         """Keeps n copies of the step's device tensors and cycles through them,
@@ -438,6 +483,11 @@ class Workload:
         if kind == "fwd":
             A.fwd_ex(self.shape, self.dtype_code, self.q.data_ptr(), self.k.data_ptr(), self.v.data_ptr(),
                      self.o.data_ptr(), self.lse.data_ptr(), stream)
+        elif kind == "qkv":
+            A.check(A.lib.attn_qkv_proj_ex(ctypes.byref(self.shape), self.x.data_ptr(), self.wq.data_ptr(),
+                                           self.wk.data_ptr(), self.wv.data_ptr(), self.bq.data_ptr(),
+                                           self.bk.data_ptr(), self.bv.data_ptr(), self.q.data_ptr(),
+                                           self.k.data_ptr(), self.v.data_ptr(), stream))
         elif kind == "bwd":
             A.bwd_ex(self.shape, self.dtype_code, self.do.data_ptr(), self.q.data_ptr(), self.k.data_ptr(),
                      self.v.data_ptr(), self.o.data_ptr(), self.lse.data_ptr(), self.dq.data_ptr(),
@@ -476,7 +526,7 @@ class Workload:
     def setup_e2e(self):
         torch = self.torch
         kind = self.cfg["kind"]
-        self.e2e_pipe = kind in ("fwd", "bwd", "train", "ragged")
+        self.e2e_pipe = kind in ("fwd", "bwd", "train", "ragged", "qkv")
         gather = self.gather_ok
         if self.e2e_pipe:
             # Every step copies its inputs in from pinned host memory and its
@@ -566,6 +616,8 @@ def gpu_baseline(key, args, ctx, wl):
     same shape: fp32 prefill and backward configs only, one GPU."""
     torch, A = ctx["torch"], ctx["A"]
     cfg = CONFIGS[key]
+    if cfg["kind"] == "qkv":
+        return gpu_baseline_qkv(args, ctx, wl)
     B, H, T, d = cfg["B"], cfg["H"], cfg["T"], cfg["d"]
     path = os.path.join(ROOT, "baseline", "_ref", f"libref_gpu_{B}x{H}x{T}x{d}.so")
     if not os.path.exists(path):
@@ -622,6 +674,51 @@ def gpu_baseline(key, args, ctx, wl):
             "kind": "reference GPU path: gpu_kernels.cu %s (cuBLAS SGEMM over the full T x T scores + its "
                     "softmax kernels), built from its sources for sm_100a"
                     % {"fwd": "attn_fwd", "bwd": "attn_bwd", "train": "attn_fwd + attn_bwd"}[cfg["kind"]],
+            "max_rel_diff_vs_ours": diff}
+
+
+def gpu_baseline_qkv(args, ctx, wl):
+    """The reference GPU trainer's three gemm_nn calls (gpu_kernels.cu:112-120:
+    cuBLAS SGEMM + its bias kernel each, built from its sources into
+    baseline/_ref/) on the same inputs, same device."""
+    torch, A = ctx["torch"], ctx["A"]
+    path = os.path.join(ROOT, "baseline", "_ref", "libref_gpu_4x12x1024x128.so")
+    if not os.path.exists(path):
+        return {"unavailable": "baseline/_ref not built (reference sources absent at build time)"}
+    L = ctypes.CDLL(path)
+    L.refgpu_gemm_nn.restype = None
+    L.refgpu_init()
+    P, I = ctypes.c_void_p, ctypes.c_int
+    dev = ctx["dev"]
+    s0 = torch.cuda.default_stream(dev)           # the reference runs on the legacy default stream
+    M, K, N = wl.shape.rows, wl.shape.in_features, wl.shape.out_features
+    outs = [torch.empty_like(wl.q) for _ in range(3)]
+    pairs = [(wl.wq, wl.bq), (wl.wk, wl.bk), (wl.wv, wl.bv)]
+
+    def call():
+        for (w, b), o in zip(pairs, outs):
+            L.refgpu_gemm_nn(P(wl.x.data_ptr()), P(w.data_ptr()), P(b.data_ptr()), P(o.data_ptr()), I(M), I(K), I(N))
+
+    with torch.cuda.stream(s0):
+        saved, wl.sets = getattr(wl, "sets", None), None
+        wl.step(0)
+        wl.sets = saved
+        for _ in range(args.warmup):
+            call()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s0)
+        for _ in range(args.steps):
+            call()
+        e1.record(s0)
+        torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / args.steps
+    diff = max(float(((a - b).abs().max() / b.abs().max().clamp_min(1e-6)).item())
+               for a, b in zip((wl.q, wl.k, wl.v), outs))
+    return {"value": round(qkv_flops(M, K, N) / (ms / 1e3) / 1e12, 3), "unit": "TFLOP/s",
+            "ms_per_step": round(ms, 4),
+            "kind": "reference GPU path: gpu_kernels.cu gemm_nn x3 (cuBLAS SGEMM + its bias kernel), built from "
+                    "its sources for sm_100a",
             "max_rel_diff_vs_ours": diff}
 
 
@@ -705,7 +802,7 @@ def measure(key, args, ctx):
 
     h2d_all = wl.h2d_bytes
     gpu_base = None
-    if world == 1 and cfg["kind"] in ("fwd", "bwd", "train") and cfg["dtype"] == "f32" and not args.no_gpu_baseline:
+    if world == 1 and cfg["kind"] in DENSE and cfg["dtype"] == "f32" and not args.no_gpu_baseline:
         gpu_base = gpu_baseline(key, args, ctx, wl)
     if world > 1:
         t = torch.tensor([total_ms, e2e_ms, gather_ms], dtype=torch.float64, device=dev)
@@ -904,7 +1001,7 @@ def config_block(key, world):
     return {"workload": cfg["workload"], "config_key": key,
             "split": "none (one GPU)" if world == 1 else
             {"fwd": "(batch x head) units, attn_split_plan", "bwd": "(batch x head) units, attn_split_plan",
-             "train": "(batch x head) units, attn_split_plan", "decode": "layers",
+             "train": "(batch x head) units, attn_split_plan", "decode": "layers", "qkv": "token rows",
              "ragged": "sequences, LPT by length"}[cfg["kind"]]}
 
 

@@ -153,6 +153,40 @@ ATTN_API int attn_bwd_ex(const attn_shape *s, int dtype,
                 void *workspace, size_t workspace_bytes, attn_stream_t stream);
 
 /* ------------------------------------------------------------------------
+ * Fused QKV projection (train_kaggle.cu:152-154)
+ * ---------------------------------------------------------------------- */
+typedef struct {
+    int rows;                   /* M: token rows of X (B*T)                    */
+    int in_features;            /* columns of X = rows of each W (DIM)         */
+    int out_features;           /* N: columns of each W and of each output;
+                                   a multiple of 4                              */
+    long long x_row_stride;     /* elements between rows of X (0: in_features) */
+    long long out_row_stride;   /* elements between rows of Q, K, V
+                                   (0: out_features; 3*N for the three column
+                                   blocks of one (M, 3N) tensor)                */
+} attn_qkv_shape;
+
+/* Q = X Wq + bq, K = X Wk + bk, V = X Wv + bv in one launch: the three
+ * gemm_nn calls of train_kaggle.cu:152-154 (gemm_nn: gpu_kernels.cu:112-120,
+ * row-major fp32, bias broadcast over rows).  X (rows, in_features), each W
+ * (in_features, out_features) row-major, fp32; biases may be NULL.  fp32
+ * arithmetic on the tensor cores (three tf32 products per product, fp32 sums;
+ * results within ~1e-6 of an fp32 GEMM).  Outputs are SET.  Tensors 16-byte
+ * aligned.  Returns ATTN_OK or a status. */
+ATTN_API int attn_qkv_proj_ex(const attn_qkv_shape *s, const float *x,
+                const float *wq, const float *wk, const float *wv,
+                const float *bq, const float *bk, const float *bv,
+                float *q, float *k, float *v, attn_stream_t stream);
+
+/* The same with gemm_nn's argument style (A, B, bias, C, M, K, N): dense
+ * (M, K) input, (K, N) weights, (M, N) outputs, the legacy default stream,
+ * void return and exit(1) with a message on failure, like the drop-ins.
+ * Replaces train_kaggle.cu:152-154's three calls with one. */
+ATTN_API void attn_qkv_proj(const float *X, const float *Wq, const float *Wk, const float *Wv,
+                const float *bq, const float *bk, const float *bv,
+                float *Q, float *K, float *V, int M, int K_, int N);
+
+/* ------------------------------------------------------------------------
  * KV-cached decode (transformer.c:203-248, model.h:42-45)
  * ---------------------------------------------------------------------- */
 typedef struct {

@@ -267,3 +267,47 @@ ORACLE_API void oracle_dequantize_kv_int8(const int8_t *codes, const float *scal
             }
         }
 }
+
+/* ------------------------------------------------------------------------
+ * out(M,N) = in(M,K) @ W(K,N) + bias(N), rows of `in` ldx apart: the
+ * reference's matmul_forward (train.c:181-211) in its portable i-k-j order
+ * (train.c:193-205: out row zeroed, then out[n] += in[k] * W[k][n] for k in
+ * order), the bias added after the product (train.c:206-212).  train.c:517-519
+ * and train_kaggle.cu:152-154 apply it to a layer's Q, K and V projections.
+ * `bias` may be NULL.  The double-precision twin is the tie-breaker.
+ * ---------------------------------------------------------------------- */
+ORACLE_API void oracle_matmul_forward(float *out, const float *in, const float *W, const float *bias,
+                                      int M, int K, int N, long ldx)
+{
+#pragma omp parallel for schedule(static)
+    for (int m = 0; m < M; m++) {
+        float *o = out + (size_t)m * N;
+        const float *x = in + (size_t)m * ldx;
+        for (int n = 0; n < N; n++) o[n] = 0.0f;
+        for (int k = 0; k < K; k++) {
+            const float a = x[k];
+            const float *wr = W + (size_t)k * N;
+            for (int n = 0; n < N; n++) o[n] += a * wr[n];
+        }
+        if (bias)
+            for (int n = 0; n < N; n++) o[n] += bias[n];
+    }
+}
+
+ORACLE_API void oracle_matmul_forward_f64(double *out, const float *in, const float *W, const float *bias,
+                                          int M, int K, int N, long ldx)
+{
+#pragma omp parallel for schedule(static)
+    for (int m = 0; m < M; m++) {
+        double *o = out + (size_t)m * N;
+        const float *x = in + (size_t)m * ldx;
+        for (int n = 0; n < N; n++) o[n] = 0.0;
+        for (int k = 0; k < K; k++) {
+            const double a = x[k];
+            const float *wr = W + (size_t)k * N;
+            for (int n = 0; n < N; n++) o[n] += a * (double)wr[n];
+        }
+        if (bias)
+            for (int n = 0; n < N; n++) o[n] += bias[n];
+    }
+}

@@ -37,6 +37,8 @@ def lib():
         _lib.oracle_cached_attention_f64.argtypes = [V, V, V, V, I, I, I, L]
         _lib.oracle_quantize_kv_int8.argtypes = [V, V, V, L, I, I, L]
         _lib.oracle_dequantize_kv_int8.argtypes = [V, V, V, L, I, I, L]
+        _lib.oracle_matmul_forward.argtypes = [V, V, V, V, I, I, I, L]
+        _lib.oracle_matmul_forward_f64.argtypes = [V, V, V, V, I, I, I, L]
     return _lib
 
 
@@ -109,6 +111,23 @@ def lse_to_probs(q, k, lse, B, T, H, d):
     return p.reshape(B * H, T, T).astype(np.float32)
 
 
+def matmul_forward(x, w, bias=None, f64=False):
+    """x (M, K) @ w (K, N) + bias: train.c:181-211 restated (fp32, or fp64 sums)."""
+    x, w = _f32(x), _f32(w)
+    b = _f32(bias) if bias is not None else None
+    M, K = x.shape
+    N = w.shape[1]
+    out = np.zeros((M, N), np.float64 if f64 else np.float32)
+    fn = lib().oracle_matmul_forward_f64 if f64 else lib().oracle_matmul_forward
+    fn(_p(out), _p(x), _p(w), _p(b), M, K, N, K)
+    return out
+
+
+def qkv_proj(x, ws, bs=(None, None, None), f64=False):
+    """The three projections of train.c:517-519 / train_kaggle.cu:152-154."""
+    return tuple(matmul_forward(x, w, b, f64) for w, b in zip(ws, bs))
+
+
 # ---------------------------------------------------------------------------
 # the reference itself, compiled from its sources
 # ---------------------------------------------------------------------------
@@ -129,6 +148,7 @@ def _ref(name):
         if name.startswith("libref_train"):
             L.ref_attention_forward.argtypes = [V, V, V, V, V, I, I]
             L.ref_attention_backward.argtypes = [V, V, V, V, V, V, V, V, I, I]
+            L.ref_matmul_forward.argtypes = [V, V, V, V, I, I, I]
         elif name.startswith("libref_quant"):
             L.ref_quantize_A.argtypes = [V, V, I, I, I]
             L.ref_quantize_A.restype = ctypes.c_float
@@ -189,4 +209,17 @@ def ref_cached_attention(q, kcache, vcache, pos, H, d, t_max):
     out = np.zeros(H * d, np.float32)
     scores = np.zeros(H * t_max, np.float32)
     L.ref_cached_attention(_p(q), _p(kcache), _p(vcache), _p(out), _p(scores), pos)
+    return out
+
+
+def ref_matmul_forward(x, w, bias=None):
+    """The reference's own matmul_forward (train.c:181-211), any shape (it is
+    shape-independent; the object of the smallest training build is used)."""
+    L = _ref(ref_train_name(1, 64))
+    x, w = _f32(x), _f32(w)
+    b = _f32(bias) if bias is not None else None
+    M, K = x.shape
+    N = w.shape[1]
+    out = np.zeros((M, N), np.float32)
+    L.ref_matmul_forward(_p(out), _p(x), _p(w), _p(b), M, K, N)
     return out

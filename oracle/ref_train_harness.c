@@ -33,3 +33,12 @@ REF_API void ref_attention_backward(float *dq, float *dk, float *dv, const float
 REF_API int ref_d_model(void) { return D_MODEL; }
 REF_API int ref_n_heads(void) { return N_HEADS; }
 REF_API int ref_block_size(void) { return BLOCK_SIZE; }
+
+/* out(M,N) = in(M,K) @ W(K,N) + bias(N): the reference's own matmul_forward
+ * (train.c:181-211), which train.c:517-519 calls for the Q, K and V
+ * projections of a layer. */
+REF_API void ref_matmul_forward(float *out, const float *in, const float *W, const float *bias,
+                                int M, int K, int N)
+{
+    matmul_forward(out, in, W, bias, M, K, N);
+}

@@ -50,6 +50,11 @@ class KVCache(ctypes.Structure):
                 ("kscale", ctypes.c_void_p * MAX_LAYERS), ("vscale", ctypes.c_void_p * MAX_LAYERS)]
 
 
+class QKVShape(ctypes.Structure):
+    _fields_ = [("rows", ctypes.c_int), ("in_features", ctypes.c_int), ("out_features", ctypes.c_int),
+                ("x_row_stride", ctypes.c_longlong), ("out_row_stride", ctypes.c_longlong)]
+
+
 class Split(ctypes.Structure):
     _fields_ = [("batch0", ctypes.c_int), ("batch", ctypes.c_int), ("head0", ctypes.c_int),
                 ("heads", ctypes.c_int), ("nb", ctypes.c_int), ("nh", ctypes.c_int)]
@@ -72,6 +77,8 @@ SIGNATURES = {
     "attn_fwd_ex": (I, [ctypes.POINTER(Shape), I, P, P, P, P, P, P]),
     "attn_bwd_workspace_bytes": (SZ, [ctypes.POINTER(Shape), I]),
     "attn_bwd_ex": (I, [ctypes.POINTER(Shape), I, P, P, P, P, P, P, P, P, P, I, P, SZ, P]),
+    "attn_qkv_proj_ex": (I, [ctypes.POINTER(QKVShape), P, P, P, P, P, P, P, P, P, P, P]),
+    "attn_qkv_proj": (None, [P, P, P, P, P, P, P, P, P, P, I, I, I]),
     "attn_decode_workspace_bytes": (SZ, [ctypes.POINTER(DecodeShape)]),
     "attn_decode_ex": (I, [ctypes.POINTER(DecodeShape), P, P, P, P, P, P, P, P, SZ, P]),
     "attn_decode_ptrs_ex": (I, [ctypes.POINTER(DecodeShape), P, P, P, P, P, P, P, P, SZ, P]),
@@ -211,6 +218,30 @@ def backward_t(do, q, k, v, o, lse, heads: int, batch: int, dq=None, dk=None, dv
            lse.data_ptr(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), accumulate, ws.data_ptr(), nbytes,
            _stream())
     return dq, dk, dv
+
+
+def qkv_proj_t(x, wq, wk, wv, bq=None, bk=None, bv=None, fused=False, out=None):
+    """Q, K, V = x @ W + b for the three weights in one launch (train_kaggle.cu:152-154).
+    x: (M, Kd) fp32 CUDA tensor (any row stride that is a multiple of 4); W: (Kd, N).
+    fused=True writes one (M, 3N) tensor whose column blocks are Q, K and V and
+    returns (qkv, q_view, k_view, v_view); otherwise returns three (M, N) tensors."""
+    import torch
+    M, Kd = x.shape
+    N = wq.shape[1]
+    if fused:
+        qkv = torch.empty((M, 3 * N), dtype=torch.float32, device=x.device) if out is None else out
+        outs = (qkv[:, :N], qkv[:, N:2 * N], qkv[:, 2 * N:])
+    else:
+        outs = tuple(torch.empty((M, N), dtype=torch.float32, device=x.device) for _ in range(3)) \
+            if out is None else out
+    shape = QKVShape(M, Kd, N, x.stride(0), outs[0].stride(0))
+
+    def ptr(t):
+        return t.data_ptr() if t is not None else None
+    check(lib.attn_qkv_proj_ex(ctypes.byref(shape), x.data_ptr(), wq.data_ptr(), wk.data_ptr(), wv.data_ptr(),
+                               ptr(bq), ptr(bk), ptr(bv), outs[0].data_ptr(), outs[1].data_ptr(),
+                               outs[2].data_ptr(), _stream()))
+    return (qkv,) + outs if fused else outs
 
 
 def decode_t(q, kcache, vcache, lens, heads: int, cap: int, max_len: int, kscale=None, vscale=None,

@@ -4,6 +4,7 @@ Every expected output here is produced by pure-c-llm's own attention code,
 compiled from its unmodified sources into oracle/_ref/ by oracle/Makefile:
   - train.c attention_forward / attention_backward (train.c:339-407)
   - transformer.c cached_attention (transformer.c:203-248)
+  - train.c matmul_forward (train.c:181-211), as the Q, K, V projections
 Inputs come from the seeded splitmix64/Box-Muller generator (synth.py) and
 are stored in the fixture next to the outputs, so the fixtures do not depend
 on the generator staying bit-identical.  The INT8 fixture's codes/scales come
@@ -92,6 +93,18 @@ def int8_decode_case(name, seed, H, d, t_max, pos):
          shape=np.array([H, d, t_max]))
 
 
+def qkv_case(name, seed, M, K, N):
+    """Q, K, V projections of train.c:517-519 through the reference's own
+    matmul_forward (train.c:181-211; its AVX-512 micro-kernel when M % 8 == 0
+    and N % 16 == 0, else its i-k-j loop)."""
+    x = synth.normal(seed, (M, K))
+    ws = [synth.normal(seed + 1 + i, (K, N), 0, 0.02) for i in range(3)]
+    bs = [synth.normal(seed + 4 + i, (N,), 0, 0.1) for i in range(3)]
+    outs = [O.ref_matmul_forward(x, w, b) for w, b in zip(ws, bs)]
+    save(name, x=x, wq=ws[0], wk=ws[1], wv=ws[2], bq=bs[0], bk=bs[1], bv=bs[2], q=outs[0], k=outs[1],
+         v=outs[2], shape=np.array([M, K, N]))
+
+
 if __name__ == "__main__":
     fwd_case("fwd_h4_d32", 101, B=2, T=37, H=4, d=32)
     fwd_case("fwd_h2_d64", 111, B=1, T=65, H=2, d=64)
@@ -104,3 +117,5 @@ if __name__ == "__main__":
     decode_case("decode_h2_d64", 311, H=2, d=64, t_max=512, positions=[0, 40, 511 - 470])
     quant_case("quant_h4_d32", 401, rows=20, H=4, d=32)
     int8_decode_case("int8_decode_h2_d64", 501, H=2, d=64, t_max=512, pos=90)
+    qkv_case("qkv_m72_k96_n64", 601, M=72, K=96, N=64)
+    qkv_case("qkv_m37_k52_n36", 611, M=37, K=52, N=36)

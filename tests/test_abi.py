@@ -118,3 +118,22 @@ def test_lse_mode_backward_of_an_unfilled_probs_buffer_exits():
     r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=120)
     assert r.returncode == 1
     assert "no attn_fwd has filled this `probs` buffer" in r.stderr
+
+
+def test_qkv_proj_rejects_bad_arguments():
+    """Argument checks of the fused QKV projection run before any CUDA call."""
+    P16 = 1 << 20                                   # a 16-byte-aligned stand-in address
+    ptrs = [P16] * 4
+    outs = [P16] * 3
+    assert A.lib.attn_qkv_proj_ex(None, *ptrs, None, None, None, *outs, None) == A.ERR_INVALID
+    bad = A.QKVShape(64, 96, 66, 0, 0)               # out_features not a multiple of 4
+    assert A.lib.attn_qkv_proj_ex(ctypes.byref(bad), *ptrs, None, None, None, *outs, None) == A.ERR_INVALID
+    bad = A.QKVShape(64, 96, 64, 90, 0)              # X row stride shorter than its rows
+    assert A.lib.attn_qkv_proj_ex(ctypes.byref(bad), *ptrs, None, None, None, *outs, None) == A.ERR_INVALID
+    ok = A.QKVShape(64, 96, 64, 0, 0)
+    st = A.lib.attn_qkv_proj_ex(ctypes.byref(ok), P16 + 4, P16, P16, P16, None, None, None, *outs, None)
+    assert st == A.ERR_INVALID and "aligned" in A.last_error()
+    st = A.lib.attn_qkv_proj_ex(ctypes.byref(ok), P16, None, P16, P16, None, None, None, *outs, None)
+    assert st == A.ERR_INVALID
+    empty = A.QKVShape(0, 96, 64, 0, 0)              # no rows: nothing to do
+    assert A.lib.attn_qkv_proj_ex(ctypes.byref(empty), *ptrs, None, None, None, *outs, None) == A.OK

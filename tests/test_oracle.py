@@ -89,3 +89,26 @@ def test_restatement_vs_live_reference_random_shapes():
         att, probs, _ = O.attn_forward(q, k, v, B, T, H, d, want_probs=True)
         ra, rp = O.ref_attention_forward(q, k, v, B, T, H, d)
         assert rel_err(att, ra) < F32_TOL and rel_err(probs, rp) < F32_TOL
+
+
+@pytest.mark.parametrize("name", ["qkv_m72_k96_n64", "qkv_m37_k52_n36"])
+def test_qkv_projection_matches_reference(name):
+    """matmul_forward restated (train.c:181-211) against the reference's own
+    object, for the three projections of train.c:517-519; both of the
+    reference's code paths (micro-kernel and i-k-j loop) are covered."""
+    z = golden(name)
+    ws, bs = (z["wq"], z["wk"], z["wv"]), (z["bq"], z["bk"], z["bv"])
+    for out, want in zip(O.qkv_proj(z["x"], ws, bs), (z["q"], z["k"], z["v"])):
+        assert rel_err(out, want) < F32_TOL
+    for out, want in zip(O.qkv_proj(z["x"], ws, bs, f64=True), (z["q"], z["k"], z["v"])):
+        assert rel_err(out, want) < F32_TOL
+
+
+def test_matmul_restatement_vs_live_reference():
+    import synth
+    for seed, (M, K, N) in enumerate([(64, 128, 96), (9, 20, 12), (128, 1536, 16)]):
+        x = synth.normal(950 + seed, (M, K))
+        w = synth.normal(960 + seed, (K, N), 0, 0.02)
+        b = synth.normal(970 + seed, (N,), 0, 0.1)
+        assert rel_err(O.matmul_forward(x, w, b), O.ref_matmul_forward(x, w, b)) < F32_TOL
+        assert rel_err(O.matmul_forward(x, w, None), O.ref_matmul_forward(x, w, None)) < F32_TOL
