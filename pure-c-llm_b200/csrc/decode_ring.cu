@@ -57,6 +57,8 @@ struct Params {
     long long row_bytes_stride;       // bytes between cache rows
     long long cap;                    // rows per sequence (contiguous layout)
     long long wait_limit;             // SM cycles a bounded wait may take
+    long long stall_limit;            // the test hook's wait alone (the others keep wait_limit,
+                                      // so only its code reaches the error word)
     int n_seq, max_len, H, stall;     // stall != 0: test hook, see the kernel
     unsigned gen;                     // this call's ticket generation (never 0)
     float qscale;                     // log2(e) / sqrt(D)
@@ -283,7 +285,7 @@ decode_ring_kernel(const __grid_constant__ Params p)
     if (p.stall && h == 0) {
         // Test hook: wait on a barrier nothing arrives at, so the bounded wait
         // runs out and the abort path (error word, drained copies) runs.
-        if (!mbar_wait(STALL_BAR, 0u, abort_flag, p.err, 0x32f, p.wait_limit)) return;
+        if (!mbar_wait(STALL_BAR, 0u, abort_flag, p.err, 0x32f, p.stall_limit)) return;
     }
     float qv[DL], o[DL];
     float mrun = -INFINITY, lrun = 0.f;
@@ -520,10 +522,11 @@ static int launch_ring_t(const DecodeLaunch &L) {
     p.qscale = attn::kLog2e / sqrtf((float)D);
     p.wait_limit = 4000000000LL;
     p.stall = 0;
+    p.stall_limit = 0;
     if (g_ring_stall.load() > 0) {
         g_ring_stall.fetch_sub(1);
         p.stall = 1;
-        p.wait_limit = g_ring_stall_limit.load();
+        p.stall_limit = g_ring_stall_limit.load();
     }
     unsigned g = g_ring_gen.fetch_add(1) + 1;
     if (g == 0) g = g_ring_gen.fetch_add(1) + 1;
