@@ -10,12 +10,16 @@ temporary directory; nothing edited is kept in the repository.
   shrink_trainer     train_kaggle.cu: a_probs and s_Dbuf shrunk from B*H*T*T
                      floats to B*H*T and 2*B*H*T, with the library in its
                      lse-only probs mode.
+  fuse_qkv           train_kaggle.cu (on top of shrink_trainer): the three
+                     gemm_nn calls of the Q, K and V projections
+                     (train_kaggle.cu:152-154) replaced by one attn_qkv_proj.
   route_generate     generate.c: the per-head attention loop of block()
                      (generate.c:129-152) replaced by one call of
                      attn_cached_attention_host_ex.
 
 Usage: python ref_edits.py <reference dir> <out dir>  (writes
-gpu_kernels.cu, train_kaggle_lse.cu and generate_routed.c into <out dir>)
+gpu_kernels.cu, train_kaggle_lse.cu, train_kaggle_qkv.cu and
+generate_routed.c into <out dir>)
 """
 import os
 import sys
@@ -32,6 +36,14 @@ SHRINK_EDITS = [
     ("s_Dbuf = dmalloc((long)B_SIZE * N_HEADS * T_SIZE * T_SIZE);",
      "s_Dbuf = dmalloc(2L * B_SIZE * N_HEADS * T_SIZE);"),
 ]
+
+# train_kaggle.cu:152-154
+QKV_OLD = (
+    "        gemm_nn(a_ln1[l], W(o_Wq[l]), W(o_bq[l]), a_q[l], M, DIM, DIM);\n"
+    "        gemm_nn(a_ln1[l], W(o_Wk[l]), W(o_bk[l]), a_k[l], M, DIM, DIM);\n"
+    "        gemm_nn(a_ln1[l], W(o_Wv[l]), W(o_bv[l]), a_v[l], M, DIM, DIM);\n")
+QKV_NEW = ("        attn_qkv_proj(a_ln1[l], W(o_Wq[l]), W(o_Wk[l]), W(o_Wv[l]), W(o_bq[l]), W(o_bk[l]), W(o_bv[l]),\n"
+           "                      a_q[l], a_k[l], a_v[l], M, DIM, DIM);\n")
 
 # generate.c:129 (the scale) .. 152 (the end of the per-head loop)
 GEN_LOOP_FIRST = "    const float scale = 1.0f / sqrtf((float)DH);\n"
@@ -56,6 +68,13 @@ def shrink_trainer(text):
             raise ValueError("train_kaggle.cu: expected one %r" % old)
         text = text.replace(old, new)
     return text
+
+
+def fuse_qkv(text):
+    """Applied to the output of shrink_trainer (which includes attn_b200.h)."""
+    if text.count(QKV_OLD) != 1:
+        raise ValueError("train_kaggle.cu: the three Q, K, V gemm_nn calls were not found together")
+    return text.replace(QKV_OLD, QKV_NEW)
 
 
 def route_generate(text):
@@ -87,6 +106,7 @@ def main(argv):
 
     wr("gpu_kernels.cu", guard_gpu_kernels(rd("gpu_kernels.cu")))
     wr("train_kaggle_lse.cu", shrink_trainer(rd("train_kaggle.cu")))
+    wr("train_kaggle_qkv.cu", fuse_qkv(shrink_trainer(rd("train_kaggle.cu"))))
     wr("generate_routed.c", route_generate(rd("generate.c")))
 
 

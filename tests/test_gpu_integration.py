@@ -12,7 +12,9 @@ must agree within the fp32 tolerance.
 It also builds the reference's GPU trainer (train_kaggle.cu + gpu_kernels.cu,
 the 343M model of gpu_kernels.h) with its own cuBLAS attention, with the
 library's attn_fwd / attn_bwd linked in, and with the drop-ins plus the
-trainer's T*T buffers shrunk (lse-only probs mode); and the reference's C
+trainer's T*T buffers shrunk (lse-only probs mode), and with those plus its
+three Q, K, V gemm_nn calls (train_kaggle.cu:152-154) replaced by one
+attn_qkv_proj; and the reference's C
 generator (generate.c) with its attention loop as it is and routed to
 attn_cached_attention_host_ex.  The trainers run the same steps on the same
 token stream and must report the same losses; the drop-in trainer's weights,
@@ -68,7 +70,7 @@ def _tokens(path):
 
 def test_reference_trainer_and_generator_on_the_library(cuda, tmp_path):
     exes = {n: os.path.join(BUILD, n) for n in
-            ("trainer_ref", "trainer_gpu", "trainer_lse", "generate_ref", "generate_gpu")}
+            ("trainer_ref", "trainer_gpu", "trainer_lse", "trainer_qkv", "generate_ref", "generate_gpu")}
     if not all(os.path.exists(e) for e in exes.values()):
         pytest.skip("integration programs not built (the reference tree was absent at build time)")
     env = dict(os.environ, OMP_NUM_THREADS=str(os.cpu_count() or 1))
@@ -76,7 +78,7 @@ def test_reference_trainer_and_generator_on_the_library(cuda, tmp_path):
     _tokens(tokens)
     ckp1 = tmp_path / "model.ckp1"
     losses = {}
-    for v in ("ref", "gpu", "lse"):
+    for v in ("ref", "gpu", "lse", "qkv"):
         out = tmp_path / f"losses_{v}.txt"
         cmd = [exes["trainer_" + v], str(TRAIN_STEPS), str(tokens), str(out)] + ([str(ckp1)] if v == "gpu" else [])
         r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=900)
@@ -84,7 +86,7 @@ def test_reference_trainer_and_generator_on_the_library(cuda, tmp_path):
         losses[v] = np.loadtxt(out)
         assert losses[v].shape == (TRAIN_STEPS,)
     assert losses["ref"][-1] < losses["ref"][0] - 2.0          # the model learned the phrases
-    for v in ("gpu", "lse"):
+    for v in ("gpu", "lse", "qkv"):
         err = np.abs(losses[v] - losses["ref"]) / np.abs(losses["ref"])
         assert err.max() < LOSS_TOL, (v, err.max(), int(err.argmax()))
 

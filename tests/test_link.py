@@ -83,3 +83,20 @@ def test_trainer_with_shrunk_attention_buffers_links(tmp_path):
     undef = subprocess.run(["nm", "-C", "--undefined-only", str(exe)], capture_output=True, text=True).stdout
     assert "attn_set_probs_mode" in undef
     assert "attn_fwd(float const*, float const*, float const*, float*, float*)" in undef
+
+
+def test_trainer_with_fused_qkv_projection_links(tmp_path):
+    """On top of the shrunk buffers, the three Q, K, V gemm_nn calls
+    (train_kaggle.cu:152-154) replaced by one attn_qkv_proj from the library."""
+    _ref_or_skip()
+    _guarded_copy(tmp_path)
+    src = ref_edits.fuse_qkv(ref_edits.shrink_trainer(open(tmp_path / "train_kaggle.cu").read()))
+    assert src.count("attn_qkv_proj(") == 1 and "gemm_nn(a_ln1[l]" not in src
+    open(tmp_path / "train_kaggle.cu", "w").write(src)
+    exe = tmp_path / "train_gpu_qkv"
+    cmd = ["nvcc", "-O1", "-arch=sm_100a", "-DATTN_EXTERNAL", f"-I{os.path.join(ROOT, 'include')}", "-o", str(exe),
+           "train_kaggle.cu", "gpu_kernels.cu", f"-L{PKG}", "-lattn_b200", "-lcublas", "-Xlinker", f"-rpath={PKG}"]
+    r = subprocess.run(cmd, cwd=tmp_path, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stdout + r.stderr
+    undef = subprocess.run(["nm", "--undefined-only", str(exe)], capture_output=True, text=True).stdout
+    assert " attn_qkv_proj\n" in undef + "\n"
