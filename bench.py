@@ -323,9 +323,11 @@ class Workload:
             self.bq, self.bk, self.bv = (torch.randn((N,), generator=g, device=dev) * 0.1 for _ in range(3))
             self.q, self.k, self.v = (torch.empty((Ml, N), device=dev) for _ in range(3))
             self.shape = A.QKVShape(Ml, K, N, 0, 0)
+            self.ws_bytes = A.lib.attn_qkv_workspace_bytes(ctypes.byref(self.shape))
+            self.ws = torch.empty(self.ws_bytes, dtype=torch.uint8, device=dev)
             self.work = qkv_flops(Ml, K, N)
             self.total_work = qkv_flops(M, K, N)
-            self.launches = 1
+            self.launches = 2                        # weight split, then the projection
             self.in_names, self.out_names = ["x"], ["q", "k", "v"]
             self.local_desc = f"rows [{r0}, {r1}) of {M}"
         elif kind in ("fwd", "bwd", "train"):
@@ -487,7 +489,8 @@ class Workload:
             A.check(A.lib.attn_qkv_proj_ex(ctypes.byref(self.shape), self.x.data_ptr(), self.wq.data_ptr(),
                                            self.wk.data_ptr(), self.wv.data_ptr(), self.bq.data_ptr(),
                                            self.bk.data_ptr(), self.bv.data_ptr(), self.q.data_ptr(),
-                                           self.k.data_ptr(), self.v.data_ptr(), stream))
+                                           self.k.data_ptr(), self.v.data_ptr(), self.ws.data_ptr(),
+                                           self.ws_bytes, stream))
         elif kind == "bwd":
             A.bwd_ex(self.shape, self.dtype_code, self.do.data_ptr(), self.q.data_ptr(), self.k.data_ptr(),
                      self.v.data_ptr(), self.o.data_ptr(), self.lse.data_ptr(), self.dq.data_ptr(),

@@ -166,17 +166,26 @@ typedef struct {
                                    blocks of one (M, 3N) tensor)                */
 } attn_qkv_shape;
 
-/* Q = X Wq + bq, K = X Wk + bk, V = X Wv + bv in one launch: the three
- * gemm_nn calls of train_kaggle.cu:152-154 (gemm_nn: gpu_kernels.cu:112-120,
- * row-major fp32, bias broadcast over rows).  X (rows, in_features), each W
- * (in_features, out_features) row-major, fp32; biases may be NULL.  fp32
- * arithmetic on the tensor cores (three tf32 products per product, fp32 sums;
- * results within ~1e-6 of an fp32 GEMM).  Outputs are SET.  Tensors 16-byte
- * aligned.  Returns ATTN_OK or a status. */
+/* Bytes of device workspace attn_qkv_proj_ex uses for this shape: the three
+ * weights transposed and split, 2 * 3 * out_features * in_features floats
+ * (in_features rounded up to 4). */
+ATTN_API size_t attn_qkv_workspace_bytes(const attn_qkv_shape *s);
+
+/* Q = X Wq + bq, K = X Wk + bk, V = X Wv + bv: the three gemm_nn calls of
+ * train_kaggle.cu:152-154 (gemm_nn: gpu_kernels.cu:112-120, row-major fp32,
+ * bias broadcast over rows) in one tensor-core launch, after one small launch
+ * that splits the weights.  X (rows, in_features), each W (in_features,
+ * out_features) row-major, fp32; biases may be NULL.  fp32 arithmetic (three
+ * tf32 products per product, fp32 sums; results within ~1e-6 of an fp32
+ * GEMM).  Outputs are SET.  Tensors 16-byte aligned.  `workspace` (256-byte
+ * aligned, attn_qkv_workspace_bytes) may be NULL: the library then uses its
+ * own per-device buffer, grown on demand, and calls that use it must not
+ * overlap on the GPU.  Returns ATTN_OK or a status. */
 ATTN_API int attn_qkv_proj_ex(const attn_qkv_shape *s, const float *x,
                 const float *wq, const float *wk, const float *wv,
                 const float *bq, const float *bk, const float *bv,
-                float *q, float *k, float *v, attn_stream_t stream);
+                float *q, float *k, float *v,
+                void *workspace, size_t workspace_bytes, attn_stream_t stream);
 
 /* The same with gemm_nn's argument style (A, B, bias, C, M, K, N): dense
  * (M, K) input, (K, N) weights, (M, N) outputs, the legacy default stream,

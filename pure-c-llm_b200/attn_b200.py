@@ -77,7 +77,8 @@ SIGNATURES = {
     "attn_fwd_ex": (I, [ctypes.POINTER(Shape), I, P, P, P, P, P, P]),
     "attn_bwd_workspace_bytes": (SZ, [ctypes.POINTER(Shape), I]),
     "attn_bwd_ex": (I, [ctypes.POINTER(Shape), I, P, P, P, P, P, P, P, P, P, I, P, SZ, P]),
-    "attn_qkv_proj_ex": (I, [ctypes.POINTER(QKVShape), P, P, P, P, P, P, P, P, P, P, P]),
+    "attn_qkv_workspace_bytes": (SZ, [ctypes.POINTER(QKVShape)]),
+    "attn_qkv_proj_ex": (I, [ctypes.POINTER(QKVShape), P, P, P, P, P, P, P, P, P, P, P, SZ, P]),
     "attn_qkv_proj": (None, [P, P, P, P, P, P, P, P, P, P, I, I, I]),
     "attn_decode_workspace_bytes": (SZ, [ctypes.POINTER(DecodeShape)]),
     "attn_decode_ex": (I, [ctypes.POINTER(DecodeShape), P, P, P, P, P, P, P, P, SZ, P]),
@@ -220,7 +221,7 @@ def backward_t(do, q, k, v, o, lse, heads: int, batch: int, dq=None, dk=None, dv
     return dq, dk, dv
 
 
-def qkv_proj_t(x, wq, wk, wv, bq=None, bk=None, bv=None, fused=False, out=None):
+def qkv_proj_t(x, wq, wk, wv, bq=None, bk=None, bv=None, fused=False, out=None, workspace=None):
     """Q, K, V = x @ W + b for the three weights in one launch (train_kaggle.cu:152-154).
     x: (M, Kd) fp32 CUDA tensor (any row stride that is a multiple of 4); W: (Kd, N).
     fused=True writes one (M, 3N) tensor whose column blocks are Q, K and V and
@@ -238,9 +239,12 @@ def qkv_proj_t(x, wq, wk, wv, bq=None, bk=None, bv=None, fused=False, out=None):
 
     def ptr(t):
         return t.data_ptr() if t is not None else None
+    ws_ptr, ws_bytes = (None, 0)
+    if workspace is not None:
+        ws_ptr, ws_bytes = workspace.data_ptr(), workspace.numel() * workspace.element_size()
     check(lib.attn_qkv_proj_ex(ctypes.byref(shape), x.data_ptr(), wq.data_ptr(), wk.data_ptr(), wv.data_ptr(),
                                ptr(bq), ptr(bk), ptr(bv), outs[0].data_ptr(), outs[1].data_ptr(),
-                               outs[2].data_ptr(), _stream()))
+                               outs[2].data_ptr(), ws_ptr, ws_bytes, _stream()))
     return (qkv,) + outs if fused else outs
 
 

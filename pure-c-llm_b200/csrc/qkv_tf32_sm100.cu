@@ -16,17 +16,27 @@
 // TMEM is not round-to-nearest, so a fresh TMEM sum starts every kFold k
 // stages and the epilogue warps add the partial sums into fp32 registers.
 //
-// Persistent kernel, one 128 x 128 output tile per work item (the 3 * ceil(N/128)
-// column tiles of the three outputs times ceil(M/128) row tiles), items dealt
-// round-robin to one CTA per SM.  12 warps:
-//   warp 0      TMA producer: X box (32 k x 128 rows) and W boxes (4 x 32 n x 32 k)
-//               into a 3-stage ring
+// Two launches per call:
+//   qkv_split_w_kernel  the three weights, transposed to (N x K) rows (K-major,
+//               as the tf32 B operand must be) and split into high and low parts,
+//               into a workspace [part][3N][Kp] (Kp = K rounded up to 4); every
+//               weight element is read once and written twice, instead of being
+//               re-split by each of the ceil(M/128) row tiles that use it
+//   qkv_tf32_kernel  persistent, one 128 x 128 output tile per work item (the
+//               3 * ceil(N/128) column tiles of the three outputs times ceil(M/128)
+//               row tiles), items dealt round-robin to one CTA per SM.  12 warps:
+//   warp 0      TMA producer: per 32-k stage the raw X box (32 k x 128 rows) and
+//               the W^T high and low boxes (32 k x 128 n) into a 4-stage ring
 //   warp 1      MMA issuer: D += Xh Wh + Xh Wl + Xl Wh, M=128 N=128 K=8,
-//               tcgen05.mma kind::tf32, into one of two TMEM accumulators
+//               tcgen05.mma kind::tf32 with A (X's parts) from TMEM and B from
+//               shared memory, into one of two TMEM accumulators
 //   warps 2-3   idle
-//   warps 4-7   splitters: X's high part in place and its low part beside it;
-//               W transposed (K-major, as the B operand must be for tf32) as
-//               high and low parts, by 4x4 micro-blocks
+//   warps 4-7   splitters: X's high and low parts into the stage's TMEM slot (a
+//               warp per 32 rows, its TMEM lane quadrant)
+// Shared memory's 128 bytes per clock bound this kernel: with both operands
+// in shared memory and both split there, a 32-k stage moved 224 KB through it
+// against ~770 cycles of tensor work.  Now a stage moves 112 KB: TMA's 48 KB,
+// the splitters' 16 KB read of X, and the MMAs' 48 KB read of W's parts.
 //   warps 8-11  epilogue: a thread owns one output row (one TMEM lane), adds
 //               each partial sum into 128 fp32 registers, adds the bias and
 //               writes the tile through shared memory with TMA stores
@@ -40,6 +50,9 @@
 #include <cudaTypedefs.h>
 #include <cstdio>
 #include <cstdlib>
+#include <map>
+#include <mutex>
+#include <utility>
 
 namespace attn {
 namespace qkv {
@@ -50,33 +63,34 @@ constexpr int BM = 128;            // output rows per tile (TMEM lanes)
 constexpr int BN = 128;            // output columns per tile
 constexpr int BK = 32;             // k per stage (one 128-byte swizzle row of fp32)
 constexpr int kThreads = 384;
-constexpr int kStages = 3;
+constexpr int kStages = 4;
 constexpr int kFold = 8;           // k stages per fresh TMEM sum (256 k)
 constexpr int XB = BM * BK * 4;    // 16 KB: one X part
 constexpr int WB = BN * BK * 4;    // 16 KB: one W part
-constexpr int STAGE = 2 * XB + 2 * WB;
-constexpr int OFF_XH = 0, OFF_XL = XB, OFF_WL = 2 * XB, OFF_WH = 2 * XB + WB;   // within a stage
+constexpr int STAGE = XB + 2 * WB;
+constexpr int OFF_X = 0, OFF_WH = XB, OFF_WL = XB + WB;   // within a stage: raw X, W^T high, W^T low
 constexpr int OFF_OUT = kStages * STAGE;          // 4 epilogue warps x 2 buffers x 4 KB
 constexpr int OFF_BAR = OFF_OUT + 4 * 2 * 4096;
 constexpr int SMEM = OFF_BAR + 256 + 1024;
-constexpr int TM_COLS = 2 * BN;                   // two accumulators
-constexpr int REG_LOW = 72, REG_EPI = 232;        // 128 x (72 + 168 + 232) <= 384 x 168; no spills
+constexpr int TM_X = 2 * BN;                      // TMEM: two accumulators, then per stage Xh, Xl (32 each)
+constexpr int TM_COLS = 512;
+static_assert(TM_X + 64 * kStages <= TM_COLS, "TMEM budget");
+constexpr int REG_LOW = 104, REG_EPI = 232;       // 128 x (104 + 168 + 232) <= 384 x 168; no spills
 static_assert(SMEM <= 227 * 1024, "shared memory");
 static_assert(REG_LOW + 168 + REG_EPI <= 3 * 168, "register split exceeds the launch allocation");
 
 enum {
-    B_FULL = 0,                    // 3: stage landed
-    B_SPLIT = 3,                   // 3: stage split
-    B_EMPTY = 6,                   // 3: stage's MMAs finished
-    B_ACCF = 9,                    // 2: accumulator holds a finished partial sum
-    B_ACCE = 11,                   // 2: accumulator read by the epilogue
-    B_SPL = 13,                    // splitters: raw W read (before W^T low overwrites it)
-    B_COUNT = 14
+    B_FULL = 0,                    // 4: stage landed
+    B_SPLIT = 4,                   // 4: stage split (W^T parts in shared memory, X's parts in TMEM)
+    B_EMPTY = 8,                   // 4: stage's MMAs finished (its shared memory and TMEM slot are free)
+    B_ACCF = 12,                   // 2: accumulator holds a finished partial sum
+    B_ACCE = 14,                   // 2: accumulator read by the epilogue
+    B_COUNT = 16
 };
 
 struct Params {
     const float *bias[3];
-    int M, N, K;
+    int M, N, K;                   // (N: out_features, K: in_features)
     int mt, nt;                    // row tiles, column tiles per output
     int n_items, nk;
     int *err;
@@ -103,16 +117,44 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, uint32_t sr
 }
 __device__ __forceinline__ void bulk_wait_read_1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
 
-__device__ __forceinline__ float f4_at(const float4 &v, int c) {
-    return c == 0 ? v.x : c == 1 ? v.y : c == 2 ? v.z : v.w;
-}
 __device__ __forceinline__ float hi_part(float x) { return __uint_as_float(__float_as_uint(x) & 0xFFFFE000u); }
 
+// W (K x N, row-major, one of three) -> rows [w*N, (w+1)*N) of W^T high and
+// low (3N x Kp).  A block moves a 32 x 32 tile through shared memory: reads
+// are coalesced along n, writes along k.
+__global__ void __launch_bounds__(256)
+qkv_split_w_kernel(const float *__restrict__ w0, const float *__restrict__ w1, const float *__restrict__ w2,
+                   float *__restrict__ wth, float *__restrict__ wtl, int K, int N, long long Kp)
+{
+    pdl_begin();   // launched by launch_pdl
+    __shared__ float tile[32][33];
+    const int w = blockIdx.z;
+    const float *src = w == 0 ? w0 : w == 1 ? w1 : w2;
+    const int n0 = blockIdx.x * 32, k0 = blockIdx.y * 32;
+    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int k = k0 + ty + 8 * i, n = n0 + tx;
+        tile[ty + 8 * i][tx] = (k < K && n < N) ? __ldg(src + (long long)k * N + n) : 0.f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int n = n0 + ty + 8 * i, k = k0 + tx;
+        if (n < N && k < K) {
+            const float x = tile[tx][ty + 8 * i], h = hi_part(x);
+            const long long o = ((long long)w * N + n) * Kp + k;
+            wth[o] = h;
+            wtl[o] = x - h;
+        }
+    }
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
-qkv_tf32_kernel(const __grid_constant__ CUtensorMap tx, const __grid_constant__ CUtensorMap tw0,
-                const __grid_constant__ CUtensorMap tw1, const __grid_constant__ CUtensorMap tw2,
-                const __grid_constant__ CUtensorMap to0, const __grid_constant__ CUtensorMap to1,
-                const __grid_constant__ CUtensorMap to2, const __grid_constant__ Params p)
+qkv_tf32_kernel(const __grid_constant__ CUtensorMap tx, const __grid_constant__ CUtensorMap twh,
+                const __grid_constant__ CUtensorMap twl, const __grid_constant__ CUtensorMap to0,
+                const __grid_constant__ CUtensorMap to1, const __grid_constant__ CUtensorMap to2,
+                const __grid_constant__ Params p)
 {
     pdl_begin();   // launched by launch_pdl
     extern __shared__ uint8_t smem_raw[];
@@ -135,7 +177,6 @@ qkv_tf32_kernel(const __grid_constant__ CUtensorMap tx, const __grid_constant__ 
             mbar_init(BAR(B_ACCF + i), 1);
             mbar_init(BAR(B_ACCE + i), 128);
         }
-        mbar_init(BAR(B_SPL), 128);
         *abort_flag = 0;
         fence_mbar_init();
     }
@@ -158,26 +199,25 @@ qkv_tf32_kernel(const __grid_constant__ CUtensorMap tx, const __grid_constant__ 
             const bool leader = elect_one();
             if (leader) {
                 prefetch_tmap(&tx);
-                prefetch_tmap(&tw0);
-                prefetch_tmap(&tw1);
-                prefetch_tmap(&tw2);
+                prefetch_tmap(&twh);
+                prefetch_tmap(&twl);
             }
             int g = 0;                                       // stages issued
             bool ok = true;
             for (int item = blockIdx.x; ok && item < p.n_items; item += gridDim.x) {
                 int m0, w, n0;
                 item_coords(p, item, m0, w, n0);
-                const CUtensorMap *mw = w == 0 ? &tw0 : w == 1 ? &tw1 : &tw2;
+                const int wrow = w * p.N + n0;               // rows of W^T (rows past N read the next
+                                                             // weight's or zeros; their columns are not stored)
                 for (int ks = 0; ks < p.nk; ks++, g++) {
                     const int st = g % kStages;
                     if (g >= kStages && !(ok = wait_w(B_EMPTY + st, g / kStages - 1, 0x501))) break;
                     if (leader) {
                         const uint32_t s0 = base + st * STAGE;
-                        mbar_arrive_expect_tx(BAR(B_FULL + st), XB + WB);
-                        tma_load_2d(s0 + OFF_XH, &tx, BAR(B_FULL + st), ks * BK, m0);
-#pragma unroll
-                        for (int c = 0; c < BN / 32; c++)
-                            tma_load_2d(s0 + OFF_WL + c * (BK * 128), mw, BAR(B_FULL + st), n0 + 32 * c, ks * BK);
+                        mbar_arrive_expect_tx(BAR(B_FULL + st), XB + 2 * WB);
+                        tma_load_2d(s0 + OFF_X, &tx, BAR(B_FULL + st), ks * BK, m0);
+                        tma_load_2d(s0 + OFF_WH, &twh, BAR(B_FULL + st), ks * BK, wrow);
+                        tma_load_2d(s0 + OFF_WL, &twl, BAR(B_FULL + st), ks * BK, wrow);
                     }
                     __syncwarp();
                 }
@@ -199,12 +239,11 @@ qkv_tf32_kernel(const __grid_constant__ CUtensorMap tx, const __grid_constant__ 
                     if (leader) {
 #pragma unroll
                         for (int part = 0; part < 3; part++) {       // hh, hl, lh
-                            const uint32_t xa = s0 + (part == 2 ? OFF_XL : OFF_XH);
+                            const uint32_t xa = tmem + TM_X + 64 * st + (part == 2 ? 32 : 0);
                             const uint32_t wb = s0 + (part == 1 ? OFF_WL : OFF_WH);
 #pragma unroll
                             for (int kk = 0; kk < BK / 8; kk++)
-                                mma_tf32_ss(tmem + BN * a, sw128_desc(xa + 32 * kk, 16, 1024),
-                                            sw128_desc(wb + 32 * kk, 16, 1024), idD,
+                                mma_tf32_ts(tmem + BN * a, xa + 8 * kk, sw128_desc(wb + 32 * kk, 16, 1024), idD,
                                             (ks % kFold > 0 || part > 0 || kk > 0));
                         }
                         mma_commit(BAR(B_EMPTY + st));
@@ -219,7 +258,6 @@ qkv_tf32_kernel(const __grid_constant__ CUtensorMap tx, const __grid_constant__ 
             }
         } else if (warp >= 4) {
             // -------------------------------------------------------- splitters
-            const int tid = threadIdx.x - 128;
             int g = 0;
             bool ok = true;
             for (int item = blockIdx.x; ok && item < p.n_items; item += gridDim.x) {
@@ -227,61 +265,31 @@ qkv_tf32_kernel(const __grid_constant__ CUtensorMap tx, const __grid_constant__ 
                     const int st = g % kStages;
                     if (!(ok = wait_w(B_FULL + st, g / kStages, 0x521))) break;
                     uint8_t *s0 = sb + st * STAGE;
-                    // X: high part in place, low part beside it (same swizzled offsets)
+                    tc_fence_after();
+                    // X: this warp's 32 rows (its TMEM lane quadrant), one row per thread
+                    // (128 bytes, 128-byte swizzle) -> high and low parts in the stage's
+                    // TMEM slot.  The slot is free: the stage's previous MMAs finished
+                    // before its TMA load was issued.
                     {
-                        float *xh = reinterpret_cast<float *>(s0 + OFF_XH);
-                        float *xl = reinterpret_cast<float *>(s0 + OFF_XL);
+                        const int quad = warp & 3, row = quad * 32 + lane;
+                        uint32_t hi[32], lo[32];
 #pragma unroll
-                        for (int i = 0; i < BM * BK / (128 * 4); i++) {
-                            const int e = 4 * (tid + 128 * i);
-                            const float4 x = *reinterpret_cast<const float4 *>(xh + e);
-                            const float4 h = make_float4(hi_part(x.x), hi_part(x.y), hi_part(x.z), hi_part(x.w));
-                            *reinterpret_cast<float4 *>(xh + e) = h;
-                            *reinterpret_cast<float4 *>(xl + e) = make_float4(x.x - h.x, x.y - h.y, x.z - h.z, x.w - h.w);
-                        }
-                    }
-                    // W: raw boxes ([32 k][32 n] per 32-column chunk, 128-byte swizzle)
-                    // -> W^T high and low ([128 n][32 k], K-major, same swizzle).  4x4
-                    // micro-blocks with 16-byte loads and stores; the 8 lanes of each
-                    // quarter-warp take one diagonal of a 32 x 32 block's 8 x 8 grid of
-                    // micro-blocks (k group a, n group b = a + p mod 8), so their loads
-                    // hit 8 different 16-byte bank groups, and so do their stores.
-                    // Every raw value is read before the low part overwrites the raw tile.
-                    uint8_t *wraw = s0 + OFF_WL;
-                    constexpr int MB = BN * BK / 16 / 128;     // micro-blocks per thread
-                    float4 vr[MB][4];
+                        for (int j = 0; j < 8; j++) {
+                            const float4 x = *reinterpret_cast<const float4 *>(s0 + OFF_X + row * 128 + ((j ^ (row & 7)) << 4));
+                            const float xv[4] = {x.x, x.y, x.z, x.w};
 #pragma unroll
-                    for (int u = 0; u < MB; u++) {
-                        const int m = tid + 128 * u, c32 = m >> 6, a = m & 7, b = (a + ((m & 63) >> 3)) & 7;
-#pragma unroll
-                        for (int r = 0; r < 4; r++) {
-                            const int k = 4 * a + r;
-                            vr[u][r] = *reinterpret_cast<const float4 *>(wraw + c32 * (BK * 128) + k * 128 +
-                                                                         ((b ^ (k & 7)) << 4));
-                        }
-                    }
-                    mbar_arrive(BAR(B_SPL));
-                    if (!(ok = wait_w(B_SPL, g, 0x522))) break;
-#pragma unroll
-                    for (int u = 0; u < MB; u++) {
-                        const int m = tid + 128 * u, c32 = m >> 6, a = m & 7, b = (a + ((m & 63) >> 3)) & 7;
-#pragma unroll
-                        for (int c = 0; c < 4; c++) {
-                            const int n = 32 * c32 + 4 * b + c;
-                            const int off = n * 128 + ((a ^ (n & 7)) << 4);
-                            const float x[4] = {f4_at(vr[u][0], c), f4_at(vr[u][1], c), f4_at(vr[u][2], c),
-                                                f4_at(vr[u][3], c)};
-                            float h[4], l[4];
-#pragma unroll
-                            for (int r = 0; r < 4; r++) {
-                                h[r] = hi_part(x[r]);
-                                l[r] = x[r] - h[r];
+                            for (int u = 0; u < 4; u++) {
+                                const float h = hi_part(xv[u]);
+                                hi[4 * j + u] = __float_as_uint(h);
+                                lo[4 * j + u] = __float_as_uint(xv[u] - h);
                             }
-                            *reinterpret_cast<float4 *>(s0 + OFF_WH + off) = make_float4(h[0], h[1], h[2], h[3]);
-                            *reinterpret_cast<float4 *>(wraw + off) = make_float4(l[0], l[1], l[2], l[3]);
                         }
+                        const uint32_t t = tmem + ((uint32_t)(quad * 32) << 16) + TM_X + 64 * st;
+                        tmem_st32(t, hi);
+                        tmem_st32(t + 32, lo);
                     }
-                    fence_async_smem();
+                    tmem_wait_st();
+                    tc_fence_before();
                     mbar_arrive(BAR(B_SPLIT + st));
                 }
             }
@@ -403,18 +411,51 @@ static bool map_2d(CUtensorMap *m, const void *ptr, long long cols, long long ro
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// Workspace of the split weights: W^T high then W^T low, each 3N x Kp floats.
+static long long qkv_kp(const attn_qkv_shape *s) { return ((long long)s->in_features + 3) / 4 * 4; }
+static size_t qkv_ws_half(const attn_qkv_shape *s) {
+    return ((size_t)3 * s->out_features * (size_t)qkv_kp(s) * 4 + 255) / 256 * 256;
+}
+static size_t qkv_ws_bytes(const attn_qkv_shape *s) { return 2 * qkv_ws_half(s); }
+
+// Library-owned workspace, one per device, grown on demand; calls that use it
+// must not overlap on the GPU.
+static void *qkv_library_workspace(size_t bytes, cudaStream_t s) {
+    static std::mutex mu;
+    static std::map<int, std::pair<void *, size_t>> pool;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+    std::lock_guard<std::mutex> lk(mu);
+    auto &slot = pool[dev];
+    if (slot.second >= bytes) return slot.first;
+    if (slot.first) {
+        cudaStreamSynchronize(s);
+        cudaFree(slot.first);
+        slot = {nullptr, 0};
+    }
+    void *ptr = nullptr;
+    if (cudaMalloc(&ptr, bytes) != cudaSuccess) return nullptr;
+    slot = {ptr, bytes};
+    return ptr;
+}
+
 int launch_qkv_tf32_sm100(const attn_qkv_shape *s, const float *x, const float *const w[3],
-                          const float *const bias[3], float *const out[3], int *err, cudaStream_t stream) {
+                          const float *const bias[3], float *const out[3], void *ws, int *err, cudaStream_t stream) {
     using namespace attn::qkv;
     const long long ldx = s->x_row_stride ? s->x_row_stride : s->in_features;
     const long long ldo = s->out_row_stride ? s->out_row_stride : s->out_features;
-    CUtensorMap mx, mw[3], mo[3];
-    if (!map_2d(&mx, x, s->in_features, s->rows, ldx, BK, BM))
-        return set_error(ATTN_ERR_CUDA, "QKV projection: cuTensorMapEncodeTiled failed (X)");
+    const long long Kp = qkv_kp(s);
+    const size_t half = qkv_ws_half(s);
+    float *wth = static_cast<float *>(ws);
+    float *wtl = reinterpret_cast<float *>(static_cast<char *>(ws) + half);
+    CUtensorMap mx, mwh, mwl, mo[3];
+    if (!map_2d(&mx, x, s->in_features, s->rows, ldx, BK, BM) ||
+        !map_2d(&mwh, wth, s->in_features, 3LL * s->out_features, Kp, BK, BN) ||
+        !map_2d(&mwl, wtl, s->in_features, 3LL * s->out_features, Kp, BK, BN))
+        return set_error(ATTN_ERR_CUDA, "QKV projection: cuTensorMapEncodeTiled failed (X or W)");
     for (int i = 0; i < 3; i++)
-        if (!map_2d(&mw[i], w[i], s->out_features, s->in_features, s->out_features, 32, BK) ||
-            !map_2d(&mo[i], out[i], s->out_features, s->rows, ldo, 32, 32))
-            return set_error(ATTN_ERR_CUDA, "QKV projection: cuTensorMapEncodeTiled failed (W or output)");
+        if (!map_2d(&mo[i], out[i], s->out_features, s->rows, ldo, 32, 32))
+            return set_error(ATTN_ERR_CUDA, "QKV projection: cuTensorMapEncodeTiled failed (output)");
     Params p;
     for (int i = 0; i < 3; i++) p.bias[i] = bias[i];
     p.M = s->rows;
@@ -425,13 +466,18 @@ int launch_qkv_tf32_sm100(const attn_qkv_shape *s, const float *x, const float *
     p.n_items = 3 * p.mt * p.nt;
     p.nk = (p.K + BK - 1) / BK;
     p.err = err;
+    const dim3 sgrid((p.N + 31) / 32, (p.K + 31) / 32, 3);
+    int st = check_pdl(launch_pdl(qkv_split_w_kernel, sgrid, dim3(256), 0, stream, w[0], w[1], w[2], wth, wtl, p.K,
+                                  p.N, Kp),
+                       "QKV projection: weight split kernel");
+    if (st != ATTN_OK) return st;
     const int ctas = std::max(1, std::min(sm_count_here(), p.n_items));
     if (!ensure_smem_attr((const void *)qkv_tf32_kernel, SMEM))
         return set_error(ATTN_ERR_CUDA, "QKV projection: cannot set shared-memory size");
     if (!ensure_carveout((const void *)qkv_tf32_kernel, 100))
         return set_error(ATTN_ERR_CUDA, "QKV projection: cannot set the shared-memory carveout");
-    return check_pdl(launch_pdl(qkv_tf32_kernel, dim3(ctas), dim3(kThreads), (size_t)SMEM, stream, mx, mw[0], mw[1],
-                                mw[2], mo[0], mo[1], mo[2], p),
+    return check_pdl(launch_pdl(qkv_tf32_kernel, dim3(ctas), dim3(kThreads), (size_t)SMEM, stream, mx, mwh, mwl,
+                                mo[0], mo[1], mo[2], p),
                      "QKV projection kernel");
 }
 
@@ -446,9 +492,14 @@ int *device_error_ptr();
 
 extern "C" {
 
+size_t attn_qkv_workspace_bytes(const attn_qkv_shape *s) {
+    if (!s || s->in_features < 1 || s->out_features < 1) return 0;
+    return attn_host::qkv_ws_bytes(s);
+}
+
 int attn_qkv_proj_ex(const attn_qkv_shape *s, const float *x, const float *wq, const float *wk, const float *wv,
                      const float *bq, const float *bk, const float *bv, float *q, float *k, float *v,
-                     attn_stream_t stream) {
+                     void *workspace, size_t workspace_bytes, attn_stream_t stream) {
     using attn_host::set_error;
     if (!s) return set_error(ATTN_ERR_INVALID, "QKV projection: shape is NULL");
     if (s->rows < 0 || s->in_features < 1 || s->out_features < 1)
@@ -467,17 +518,25 @@ int attn_qkv_proj_ex(const attn_qkv_shape *s, const float *x, const float *wq, c
         if (reinterpret_cast<uintptr_t>(ptr) & 15)
             return set_error(ATTN_ERR_INVALID, "QKV projection: tensors must be 16-byte aligned");
     }
+    const size_t need = attn_host::qkv_ws_bytes(s);
+    cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
+    if (workspace) {
+        if (workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255))
+            return set_error(ATTN_ERR_WORKSPACE, "QKV projection: workspace needs %zu bytes (256-byte aligned), "
+                             "got %zu", need, workspace_bytes);
+    } else if (!(workspace = attn_host::qkv_library_workspace(need, cs))) {
+        return set_error(ATTN_ERR_NOMEM, "QKV projection: cannot allocate the %zu-byte workspace", need);
+    }
     const float *w[3] = {wq, wk, wv};
     const float *b[3] = {bq, bk, bv};
     float *o[3] = {q, k, v};
-    return attn_host::launch_qkv_tf32_sm100(s, x, w, b, o, attn_host::device_error_ptr(),
-                                            reinterpret_cast<cudaStream_t>(stream));
+    return attn_host::launch_qkv_tf32_sm100(s, x, w, b, o, workspace, attn_host::device_error_ptr(), cs);
 }
 
 void attn_qkv_proj(const float *X, const float *Wq, const float *Wk, const float *Wv, const float *bq,
                    const float *bk, const float *bv, float *Q, float *K, float *V, int M, int K_, int N) {
     const attn_qkv_shape s = {M, K_, N, 0, 0};
-    const int st = attn_qkv_proj_ex(&s, X, Wq, Wk, Wv, bq, bk, bv, Q, K, V, nullptr);
+    const int st = attn_qkv_proj_ex(&s, X, Wq, Wk, Wv, bq, bk, bv, Q, K, V, nullptr, 0, nullptr);
     if (st != ATTN_OK) {
         fprintf(stderr, "CUDA error '%s' at attn_qkv_proj\n", attn_last_error());
         exit(1);

@@ -125,15 +125,26 @@ def test_qkv_proj_rejects_bad_arguments():
     P16 = 1 << 20                                   # a 16-byte-aligned stand-in address
     ptrs = [P16] * 4
     outs = [P16] * 3
-    assert A.lib.attn_qkv_proj_ex(None, *ptrs, None, None, None, *outs, None) == A.ERR_INVALID
+    assert A.lib.attn_qkv_proj_ex(None, *ptrs, None, None, None, *outs, None, 0, None) == A.ERR_INVALID
     bad = A.QKVShape(64, 96, 66, 0, 0)               # out_features not a multiple of 4
-    assert A.lib.attn_qkv_proj_ex(ctypes.byref(bad), *ptrs, None, None, None, *outs, None) == A.ERR_INVALID
+    assert A.lib.attn_qkv_proj_ex(ctypes.byref(bad), *ptrs, None, None, None, *outs, None, 0, None) == A.ERR_INVALID
     bad = A.QKVShape(64, 96, 64, 90, 0)              # X row stride shorter than its rows
-    assert A.lib.attn_qkv_proj_ex(ctypes.byref(bad), *ptrs, None, None, None, *outs, None) == A.ERR_INVALID
+    assert A.lib.attn_qkv_proj_ex(ctypes.byref(bad), *ptrs, None, None, None, *outs, None, 0, None) == A.ERR_INVALID
     ok = A.QKVShape(64, 96, 64, 0, 0)
-    st = A.lib.attn_qkv_proj_ex(ctypes.byref(ok), P16 + 4, P16, P16, P16, None, None, None, *outs, None)
+    st = A.lib.attn_qkv_proj_ex(ctypes.byref(ok), P16 + 4, P16, P16, P16, None, None, None, *outs, None, 0, None)
     assert st == A.ERR_INVALID and "aligned" in A.last_error()
-    st = A.lib.attn_qkv_proj_ex(ctypes.byref(ok), P16, None, P16, P16, None, None, None, *outs, None)
+    st = A.lib.attn_qkv_proj_ex(ctypes.byref(ok), P16, None, P16, P16, None, None, None, *outs, None, 0, None)
     assert st == A.ERR_INVALID
     empty = A.QKVShape(0, 96, 64, 0, 0)              # no rows: nothing to do
-    assert A.lib.attn_qkv_proj_ex(ctypes.byref(empty), *ptrs, None, None, None, *outs, None) == A.OK
+    assert A.lib.attn_qkv_proj_ex(ctypes.byref(empty), *ptrs, None, None, None, *outs, None, 0, None) == A.OK
+
+
+def test_qkv_workspace_size_and_check():
+    shape = A.QKVShape(4096, 1536, 1536, 0, 0)
+    assert A.lib.attn_qkv_workspace_bytes(ctypes.byref(shape)) == 2 * 3 * 1536 * 1536 * 4
+    odd = A.QKVShape(10, 37, 12, 40, 0)            # in_features rounded up to 4 in the split weights
+    assert A.lib.attn_qkv_workspace_bytes(ctypes.byref(odd)) == 2 * ((3 * 12 * 40 * 4 + 255) // 256 * 256)
+    P16 = 1 << 20
+    st = A.lib.attn_qkv_proj_ex(ctypes.byref(shape), P16, P16, P16, P16, None, None, None, P16, P16, P16,
+                                P16, 1024, None)   # a caller workspace that is too small
+    assert st == A.ERR_WORKSPACE

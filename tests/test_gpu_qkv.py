@@ -131,7 +131,8 @@ def test_qkv_trainer_shape_vs_cublas_sgemm(A):
 
 def test_qkv_dropin_signature_and_repeat(A):
     """attn_qkv_proj (gemm_nn's argument style, default stream) equals the _ex
-    entry point bit for bit, call after call (deterministic)."""
+    entry point bit for bit, call after call (deterministic), with the
+    library's workspace or the caller's."""
     import torch
     M, K, N = 300, 256, 192
     x, ws, bs = case(77, M, K, N)
@@ -145,6 +146,12 @@ def test_qkv_dropin_signature_and_repeat(A):
         torch.cuda.synchronize()
         for o, r in zip(outs, ref):
             assert torch.equal(o, r)
+    # a caller workspace instead of the library's own gives the same bits
+    shape = A.QKVShape(M, K, N, 0, 0)
+    ws = torch.empty(A.lib.attn_qkv_workspace_bytes(ctypes.byref(shape)), dtype=torch.uint8, device="cuda")
+    mine = A.qkv_proj_t(xd, *wd, *bd, workspace=ws)
+    for o, r in zip(mine, ref):
+        assert torch.equal(o, r)
     code = ctypes.c_int(0)
     A.check(A.lib.attn_device_error(0, ctypes.byref(code)))
     assert code.value == 0
