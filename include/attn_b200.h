@@ -429,6 +429,14 @@ ATTN_API int attn_decode_multi(const attn_decode_shape *shapes, const float *con
  * no GPU fault is involved. */
 ATTN_API int attn_debug_decode_timeout(int launches, long long limit_cycles);
 
+/* The same for the next `launches` calls of the QKV projection: the MMA
+ * warp of its tensor-core kernel first waits on a barrier that nothing
+ * arrives at, bounded by `limit_cycles` (>= 1000).  The kernel records 0x5ff
+ * in the device error word, every role stops, and the teardown frees the
+ * kernel's TMEM; the call's outputs are undefined and later calls run
+ * normally. */
+ATTN_API int attn_debug_qkv_timeout(int launches, long long limit_cycles);
+
 #ifdef __cplusplus
 }
 #endif

@@ -93,6 +93,7 @@ SIGNATURES = {
     "attn_shard_lpt": (I, [P, I, I, I, P, P]),
     "attn_gather_permute": (I, [P, P, I, I, I, I, I, I, P]),
     "attn_debug_decode_timeout": (I, [I, LL]),
+    "attn_debug_qkv_timeout": (I, [I, LL]),
     "attn_cached_attention_host": (None, [P, P, P, P, P, I]),
     "attn_set_decode_macro_shape": (I, [I, I, I]),
     "attn_cached_attention_host_ex": (I, [P, P, P, P, I, I, I, LL, I]),

@@ -47,6 +47,7 @@
 #include "sm100.cuh"
 
 #include <algorithm>
+#include <atomic>
 #include <cudaTypedefs.h>
 #include <cstdio>
 #include <cstdlib>
@@ -85,7 +86,8 @@ enum {
     B_EMPTY = 8,                   // 4: stage's MMAs finished (its shared memory and TMEM slot are free)
     B_ACCF = 12,                   // 2: accumulator holds a finished partial sum
     B_ACCE = 14,                   // 2: accumulator read by the epilogue
-    B_COUNT = 16
+    B_STALL = 16,                  // test hook: nothing arrives here (see Params::stall)
+    B_COUNT = 17
 };
 
 struct Params {
@@ -94,6 +96,8 @@ struct Params {
     int mt, nt;                    // row tiles, column tiles per output
     int n_items, nk;
     int *err;
+    int stall;                     // test hook: the MMA warp first waits on B_STALL for
+    long long stall_limit;         // stall_limit SM cycles (the other waits keep their bound)
 };
 
 __device__ __forceinline__ void item_coords(const Params &p, int item, int &m0, int &w, int &n0) {
@@ -177,6 +181,7 @@ qkv_tf32_kernel(const __grid_constant__ CUtensorMap tx, const __grid_constant__ 
             mbar_init(BAR(B_ACCF + i), 1);
             mbar_init(BAR(B_ACCE + i), 128);
         }
+        mbar_init(BAR(B_STALL), 1);
         *abort_flag = 0;
         fence_mbar_init();
     }
@@ -228,6 +233,8 @@ qkv_tf32_kernel(const __grid_constant__ CUtensorMap tx, const __grid_constant__ 
             constexpr uint32_t idD = idesc_tf32(BM, BN, 0, 0);      // X, W^T both K-major
             int g = 0, ch = 0;
             bool ok = true;
+            if (p.stall)         // the bounded wait runs out: code 0x5ff, abort flag, every role stops
+                ok = __all_sync(0xffffffffu, mbar_wait(BAR(B_STALL), 0u, abort_flag, p.err, 0x5ff, p.stall_limit));
             for (int item = blockIdx.x; ok && item < p.n_items; item += gridDim.x) {
                 for (int ks = 0; ks < p.nk; ks++, g++) {
                     const int a = ch & 1;
@@ -439,6 +446,10 @@ static void *qkv_library_workspace(size_t bytes, cudaStream_t s) {
     return ptr;
 }
 
+// Test hook (attn_debug_qkv_timeout): the next `g_qkv_stall` launches stall.
+static std::atomic<int> g_qkv_stall{0};
+static std::atomic<long long> g_qkv_stall_limit{0};
+
 int launch_qkv_tf32_sm100(const attn_qkv_shape *s, const float *x, const float *const w[3],
                           const float *const bias[3], float *const out[3], void *ws, int *err, cudaStream_t stream) {
     using namespace attn::qkv;
@@ -466,6 +477,13 @@ int launch_qkv_tf32_sm100(const attn_qkv_shape *s, const float *x, const float *
     p.n_items = 3 * p.mt * p.nt;
     p.nk = (p.K + BK - 1) / BK;
     p.err = err;
+    p.stall = 0;
+    p.stall_limit = 0;
+    if (g_qkv_stall.load() > 0) {
+        g_qkv_stall.fetch_sub(1);
+        p.stall = 1;
+        p.stall_limit = g_qkv_stall_limit.load();
+    }
     const dim3 sgrid((p.N + 31) / 32, (p.K + 31) / 32, 3);
     int st = check_pdl(launch_pdl(qkv_split_w_kernel, sgrid, dim3(256), 0, stream, w[0], w[1], w[2], wth, wtl, p.K,
                                   p.N, Kp),
@@ -531,6 +549,15 @@ int attn_qkv_proj_ex(const attn_qkv_shape *s, const float *x, const float *wq, c
     const float *b[3] = {bq, bk, bv};
     float *o[3] = {q, k, v};
     return attn_host::launch_qkv_tf32_sm100(s, x, w, b, o, workspace, attn_host::device_error_ptr(), cs);
+}
+
+int attn_debug_qkv_timeout(int launches, long long limit_cycles) {
+    if (launches < 0 || (launches > 0 && limit_cycles < 1000))
+        return attn_host::set_error(ATTN_ERR_INVALID, "attn_debug_qkv_timeout: launches %d, limit %lld "
+                                    "(the limit must be >= 1000 cycles)", launches, limit_cycles);
+    attn_host::g_qkv_stall_limit.store(limit_cycles);
+    attn_host::g_qkv_stall.store(launches);
+    return ATTN_OK;
 }
 
 void attn_qkv_proj(const float *X, const float *Wq, const float *Wk, const float *Wv, const float *bq,

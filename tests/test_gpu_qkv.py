@@ -155,3 +155,32 @@ def test_qkv_dropin_signature_and_repeat(A):
     code = ctypes.c_int(0)
     A.check(A.lib.attn_device_error(0, ctypes.byref(code)))
     assert code.value == 0
+
+
+def test_qkv_bounded_wait_timeout_path(A):
+    """Failure detection in a TMEM-holding tensor-core kernel without a fault:
+    a test hook makes the QKV kernel's MMA warp wait on a barrier nothing
+    arrives at.  The bounded wait runs out, the kernel records 0x5ff in the
+    device error word, every role stops, and the teardown frees TMEM -- the
+    next call allocates TMEM on every SM again, is correct and leaves the
+    error word clear."""
+    import torch
+    M, K, N = 512, 256, 128
+    x, ws, bs = case(91, M, K, N)
+    xd, wd, bd = dev(x), [dev(w) for w in ws], [dev(b) for b in bs]
+    code = ctypes.c_int()
+    A.check(A.lib.attn_device_error(0, ctypes.byref(code)))       # clear
+    A.check(A.lib.attn_debug_qkv_timeout(1, 200000))
+    try:
+        A.qkv_proj_t(xd, *wd, *bd)
+        torch.cuda.synchronize()
+    finally:
+        A.check(A.lib.attn_debug_qkv_timeout(0, 0))                 # disarmed whatever ran
+    A.check(A.lib.attn_device_error(0, ctypes.byref(code)))
+    assert code.value == 0x5ff
+    outs = A.qkv_proj_t(xd, *wd, *bd)
+    torch.cuda.synchronize()
+    A.check(A.lib.attn_device_error(0, ctypes.byref(code)))
+    assert code.value == 0
+    for out, want in zip(outs, O.qkv_proj(x, ws, bs, f64=True)):
+        assert rel_err(out.cpu().numpy(), want) < F32_TOL
