@@ -90,9 +90,15 @@ enum {
     B_COUNT = 17
 };
 
+// mode 0: the Q, K, V projection.  mode 1: dQ = dS K of the causal backward
+// for every (batch, head): A = dS [bh][T rows][T keys] (zero above the
+// diagonal), B = that head's K transposed and split (K^T high / low
+// [bh][d][Tp]), C = dQ in the activation layout; an item is one 128-row tile
+// of one (batch, head) and reads keys 0 .. min(m0 + 128, T) only.
 struct Params {
     const float *bias[3];
-    int M, N, K;                   // (N: out_features, K: in_features)
+    int M, N, K;                   // (N: out_features, K: in_features; mode 1: T, d, T)
+    int mode, H;                   // mode 1: heads (bh = b * H + h)
     int mt, nt;                    // row tiles, column tiles per output
     int n_items, nk;
     int *err;
@@ -100,11 +106,24 @@ struct Params {
     long long stall_limit;         // stall_limit SM cycles (the other waits keep their bound)
 };
 
+// mode 0: output w, rows m0.., columns n0..; mode 1: w = (batch, head) index,
+// n0 = 0, items longest first (the last row tiles read the most keys)
 __device__ __forceinline__ void item_coords(const Params &p, int item, int &m0, int &w, int &n0) {
+    if (p.mode == 1) {
+        const int bhn = p.n_items / p.mt;
+        m0 = (p.mt - 1 - item / bhn) * BM;
+        w = item % bhn;
+        n0 = 0;
+        return;
+    }
     const int ng = item / p.mt;                    // consecutive CTAs share a column tile of W
     m0 = (item % p.mt) * BM;
     w = ng / p.nt;
     n0 = (ng % p.nt) * BN;
+}
+// k stages of an item
+__device__ __forceinline__ int item_nk(const Params &p, int m0) {
+    return p.mode == 1 ? (min(m0 + BM, p.K) + BK - 1) / BK : p.nk;
 }
 
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, uint32_t bar, int x, int y) {
@@ -150,6 +169,37 @@ qkv_split_w_kernel(const float *__restrict__ w0, const float *__restrict__ w1, c
             const long long o = ((long long)w * N + n) * Kp + k;
             wth[o] = h;
             wtl[o] = x - h;
+        }
+    }
+}
+
+// K of every (batch, head) -> rows [bh*D, (bh+1)*D) of K^T high and low
+// (B*H*D x Tp), the B operand of dQ = dS K.  K is in the activation layout:
+// row b*T + j, columns h*D .. h*D + D - 1, rows in_stride floats apart.
+__global__ void __launch_bounds__(256)
+split_kt_kernel(const float *__restrict__ k, float *__restrict__ kth, float *__restrict__ ktl, long long in_stride,
+                int T, int H, int D, long long Tp)
+{
+    pdl_begin();   // launched by launch_pdl
+    __shared__ float tile[32][33];
+    const int bh = blockIdx.z;
+    const float *src = k + (long long)(bh / H) * T * in_stride + (long long)(bh % H) * D;
+    const int n0 = blockIdx.x * 32, j0 = blockIdx.y * 32;
+    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int j = j0 + ty + 8 * i, n = n0 + tx;
+        tile[ty + 8 * i][tx] = (j < T && n < D) ? __ldg(src + (long long)j * in_stride + n) : 0.f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int n = n0 + ty + 8 * i, j = j0 + tx;
+        if (n < D && j < T) {
+            const float x = tile[tx][ty + 8 * i], hh = hi_part(x);
+            const long long o = ((long long)bh * D + n) * Tp + j;
+            kth[o] = hh;
+            ktl[o] = x - hh;
         }
     }
 }
@@ -214,15 +264,22 @@ qkv_tf32_kernel(const __grid_constant__ CUtensorMap tx, const __grid_constant__ 
                 item_coords(p, item, m0, w, n0);
                 const int wrow = w * p.N + n0;               // rows of W^T (rows past N read the next
                                                              // weight's or zeros; their columns are not stored)
-                for (int ks = 0; ks < p.nk; ks++, g++) {
+                const int nk = item_nk(p, m0);
+                for (int ks = 0; ks < nk; ks++, g++) {
                     const int st = g % kStages;
                     if (g >= kStages && !(ok = wait_w(B_EMPTY + st, g / kStages - 1, 0x501))) break;
                     if (leader) {
                         const uint32_t s0 = base + st * STAGE;
                         mbar_arrive_expect_tx(BAR(B_FULL + st), XB + 2 * WB);
-                        tma_load_2d(s0 + OFF_X, &tx, BAR(B_FULL + st), ks * BK, m0);
-                        tma_load_2d(s0 + OFF_WH, &twh, BAR(B_FULL + st), ks * BK, wrow);
-                        tma_load_2d(s0 + OFF_WL, &twl, BAR(B_FULL + st), ks * BK, wrow);
+                        if (p.mode == 1) {                   // 3-D maps over the (batch, head) index
+                            tma_load_3d(s0 + OFF_X, &tx, BAR(B_FULL + st), ks * BK, m0, w);
+                            tma_load_3d(s0 + OFF_WH, &twh, BAR(B_FULL + st), ks * BK, 0, w);
+                            tma_load_3d(s0 + OFF_WL, &twl, BAR(B_FULL + st), ks * BK, 0, w);
+                        } else {
+                            tma_load_2d(s0 + OFF_X, &tx, BAR(B_FULL + st), ks * BK, m0);
+                            tma_load_2d(s0 + OFF_WH, &twh, BAR(B_FULL + st), ks * BK, wrow);
+                            tma_load_2d(s0 + OFF_WL, &twl, BAR(B_FULL + st), ks * BK, wrow);
+                        }
                     }
                     __syncwarp();
                 }
@@ -236,7 +293,10 @@ qkv_tf32_kernel(const __grid_constant__ CUtensorMap tx, const __grid_constant__ 
             if (p.stall)         // the bounded wait runs out: code 0x5ff, abort flag, every role stops
                 ok = __all_sync(0xffffffffu, mbar_wait(BAR(B_STALL), 0u, abort_flag, p.err, 0x5ff, p.stall_limit));
             for (int item = blockIdx.x; ok && item < p.n_items; item += gridDim.x) {
-                for (int ks = 0; ks < p.nk; ks++, g++) {
+                int m0, w, n0;
+                item_coords(p, item, m0, w, n0);
+                const int nk = item_nk(p, m0);
+                for (int ks = 0; ks < nk; ks++, g++) {
                     const int a = ch & 1;
                     if (ks % kFold == 0 && ch >= 2 && !(ok = wait_w(B_ACCE + a, ch / 2 - 1, 0x511))) break;
                     const int st = g % kStages;
@@ -255,7 +315,7 @@ qkv_tf32_kernel(const __grid_constant__ CUtensorMap tx, const __grid_constant__ 
                         }
                         mma_commit(BAR(B_EMPTY + st));
                     }
-                    const bool last = ks % kFold == kFold - 1 || ks == p.nk - 1;
+                    const bool last = ks % kFold == kFold - 1 || ks == nk - 1;
                     if (last) {
                         if (leader) mma_commit(BAR(B_ACCF + a));
                         ch++;
@@ -268,7 +328,10 @@ qkv_tf32_kernel(const __grid_constant__ CUtensorMap tx, const __grid_constant__ 
             int g = 0;
             bool ok = true;
             for (int item = blockIdx.x; ok && item < p.n_items; item += gridDim.x) {
-                for (int ks = 0; ks < p.nk; ks++, g++) {
+                int m0, w, n0;
+                item_coords(p, item, m0, w, n0);
+                const int nk = item_nk(p, m0);
+                for (int ks = 0; ks < nk; ks++, g++) {
                     const int st = g % kStages;
                     if (!(ok = wait_w(B_FULL + st, g / kStages, 0x521))) break;
                     uint8_t *s0 = sb + st * STAGE;
@@ -308,13 +371,13 @@ qkv_tf32_kernel(const __grid_constant__ CUtensorMap tx, const __grid_constant__ 
         const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
         uint8_t *stage_out = sb + OFF_OUT + quad * 8192;
         const bool leader = lane == 0;
-        const int nchunks = (p.nk + kFold - 1) / kFold;
         float acc[BN];
         int ch = 0;
         bool ok = true;
         for (int item = blockIdx.x; ok && item < p.n_items; item += gridDim.x) {
             int m0, w, n0;
             item_coords(p, item, m0, w, n0);
+            const int nchunks = (item_nk(p, m0) + kFold - 1) / kFold;
 #pragma unroll
             for (int c = 0; c < BN; c++) acc[c] = 0.f;
             for (int c = 0; c < nchunks; c++, ch++) {
@@ -334,8 +397,8 @@ qkv_tf32_kernel(const __grid_constant__ CUtensorMap tx, const __grid_constant__ 
             }
             if (!ok) break;
             // bias, then 32 x 32 blocks through shared memory (128-byte swizzle) to TMA stores
-            const float *bias = p.bias[w];
-            const CUtensorMap *mo = w == 0 ? &to0 : w == 1 ? &to1 : &to2;
+            const float *bias = p.mode == 1 ? nullptr : p.bias[w];
+            const CUtensorMap *mo = p.mode == 1 || w == 0 ? &to0 : w == 1 ? &to1 : &to2;
             const bool rows_in = m0 + 32 * quad < p.M;       // TMA clips partial boxes; skip empty ones
 #pragma unroll
             for (int q = 0; q < BN / 32; q++) {
@@ -357,7 +420,10 @@ qkv_tf32_kernel(const __grid_constant__ CUtensorMap tx, const __grid_constant__ 
                 fence_async_smem();
                 __syncwarp();
                 if (leader) {
-                    tma_store_2d(mo, smem_u32(buf), col0, m0 + 32 * quad);
+                    if (p.mode == 1)                  // dQ rows b*T + i, columns h*d + n
+                        tma_store_3d(mo, smem_u32(buf), (w % p.H) * p.N + col0, m0 + 32 * quad, w / p.H);
+                    else
+                        tma_store_2d(mo, smem_u32(buf), col0, m0 + 32 * quad);
                     bulk_commit_group();
                 }
             }
@@ -425,15 +491,16 @@ static size_t qkv_ws_half(const attn_qkv_shape *s) {
 }
 static size_t qkv_ws_bytes(const attn_qkv_shape *s) { return 2 * qkv_ws_half(s); }
 
-// Library-owned workspace, one per device, grown on demand; calls that use it
-// must not overlap on the GPU.
-static void *qkv_library_workspace(size_t bytes, cudaStream_t s) {
+// Library-owned workspaces, one per (device, slot), grown on demand; calls that
+// use one must not overlap on the GPU.  Slot 0: the QKV projection's split
+// weights; slot 1: the drop-in backward's row statistics and split K.
+void *library_workspace(int which, size_t bytes, cudaStream_t s) {
     static std::mutex mu;
-    static std::map<int, std::pair<void *, size_t>> pool;
+    static std::map<std::pair<int, int>, std::pair<void *, size_t>> pool;
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
     std::lock_guard<std::mutex> lk(mu);
-    auto &slot = pool[dev];
+    auto &slot = pool[std::make_pair(dev, which)];
     if (slot.second >= bytes) return slot.first;
     if (slot.first) {
         cudaStreamSynchronize(s);
@@ -472,6 +539,8 @@ int launch_qkv_tf32_sm100(const attn_qkv_shape *s, const float *x, const float *
     p.M = s->rows;
     p.N = s->out_features;
     p.K = s->in_features;
+    p.mode = 0;
+    p.H = 0;
     p.mt = (p.M + BM - 1) / BM;
     p.nt = (p.N + BN - 1) / BN;
     p.n_items = 3 * p.mt * p.nt;
@@ -497,6 +566,73 @@ int launch_qkv_tf32_sm100(const attn_qkv_shape *s, const float *x, const float *
     return check_pdl(launch_pdl(qkv_tf32_kernel, dim3(ctas), dim3(kThreads), (size_t)SMEM, stream, mx, mwh, mwl,
                                 mo[0], mo[1], mo[2], p),
                      "QKV projection kernel");
+}
+
+// 3-D view {cols, rows, batch} of fp32 data, boxes of box_cols x box_rows x 1
+// with the 128-byte swizzle.
+static bool map_3d(CUtensorMap *m, const void *ptr, long long cols, long long rows, long long batch,
+                   long long row_stride, long long batch_stride, int box_cols, int box_rows) {
+    auto fn = encode_fn_qkv();
+    if (!fn) return false;
+    cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)rows, (cuuint64_t)batch};
+    cuuint64_t strides[2] = {(cuuint64_t)row_stride * 4, (cuuint64_t)batch_stride * 4};
+    cuuint32_t box[3] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<void *>(ptr), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Bytes of the split K the dQ GEMM needs (K^T high, then low).
+size_t dq_gemm_ws_bytes(int B, int H, int T, int D) {
+    const long long Tp = ((long long)T + 3) / 4 * 4;
+    return 2 * (((size_t)B * H * D * Tp * 4 + 255) / 256 * 256);
+}
+
+// dQ = dS K per (batch, head) on the tensor cores (3xTF32), SET: dS is
+// [B*H][T][ds_ld] fp32 with zeros above the diagonal for every 128 x 128
+// block the GEMM reads (bwd_dkdv_kernel<.., true> writes it); ws holds
+// dq_gemm_ws_bytes.  Needs ds_ld % 4 == 0 and 16-byte aligned tensors.
+int launch_dq_gemm_sm100(const float *ds, long long ds_ld, const float *k, long long in_stride, float *dq,
+                         long long out_stride, int B, int H, int T, int D, void *ws, int *err, cudaStream_t stream) {
+    using namespace attn::qkv;
+    const long long Tp = ((long long)T + 3) / 4 * 4;
+    const size_t half = dq_gemm_ws_bytes(B, H, T, D) / 2;
+    float *kth = static_cast<float *>(ws);
+    float *ktl = reinterpret_cast<float *>(static_cast<char *>(ws) + half);
+    const long long BH = (long long)B * H;
+    CUtensorMap mx, mwh, mwl, mo;
+    if (!map_3d(&mx, ds, T, T, BH, ds_ld, (long long)T * ds_ld, BK, BM) ||
+        !map_3d(&mwh, kth, T, D, BH, Tp, (long long)D * Tp, BK, BN) ||
+        !map_3d(&mwl, ktl, T, D, BH, Tp, (long long)D * Tp, BK, BN) ||
+        !map_3d(&mo, dq, (long long)H * D, T, B, out_stride, (long long)T * out_stride, 32, 32))
+        return set_error(ATTN_ERR_CUDA, "dQ GEMM: cuTensorMapEncodeTiled failed");
+    Params p;
+    for (int i = 0; i < 3; i++) p.bias[i] = nullptr;
+    p.M = T;
+    p.N = D;
+    p.K = T;
+    p.mode = 1;
+    p.H = H;
+    p.mt = (T + BM - 1) / BM;
+    p.nt = 1;
+    p.n_items = (int)(BH * p.mt);
+    p.nk = (T + BK - 1) / BK;
+    p.err = err;
+    p.stall = 0;
+    p.stall_limit = 0;
+    const dim3 sgrid((D + 31) / 32, (T + 31) / 32, (unsigned)BH);
+    int st = check_pdl(launch_pdl(split_kt_kernel, sgrid, dim3(256), 0, stream, k, kth, ktl, in_stride, T, H, D, Tp),
+                       "dQ GEMM: K split kernel");
+    if (st != ATTN_OK) return st;
+    const int ctas = std::max(1, std::min(sm_count_here(), p.n_items));
+    if (!ensure_smem_attr((const void *)qkv_tf32_kernel, SMEM))
+        return set_error(ATTN_ERR_CUDA, "dQ GEMM: cannot set shared-memory size");
+    if (!ensure_carveout((const void *)qkv_tf32_kernel, 100))
+        return set_error(ATTN_ERR_CUDA, "dQ GEMM: cannot set the shared-memory carveout");
+    return check_pdl(launch_pdl(qkv_tf32_kernel, dim3(ctas), dim3(kThreads), (size_t)SMEM, stream, mx, mwh, mwl, mo,
+                                mo, mo, p),
+                     "dQ GEMM kernel");
 }
 
 }  // namespace attn_host
@@ -542,7 +678,7 @@ int attn_qkv_proj_ex(const attn_qkv_shape *s, const float *x, const float *wq, c
         if (workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255))
             return set_error(ATTN_ERR_WORKSPACE, "QKV projection: workspace needs %zu bytes (256-byte aligned), "
                              "got %zu", need, workspace_bytes);
-    } else if (!(workspace = attn_host::qkv_library_workspace(need, cs))) {
+    } else if (!(workspace = attn_host::library_workspace(0, need, cs))) {
         return set_error(ATTN_ERR_NOMEM, "QKV projection: cannot allocate the %zu-byte workspace", need);
     }
     const float *w[3] = {wq, wk, wv};

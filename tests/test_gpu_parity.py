@@ -292,6 +292,46 @@ def test_drop_in_fwd_bwd(A):
         A.lib.attn_set_macro_shape(4, 12, 1024, 128)
 
 
+@pytest.mark.parametrize("B,H,T,d", [(2, 2, 256, 128), (1, 2, 132, 128), (1, 3, 200, 96), (1, 1, 516, 128)])
+def test_drop_in_bwd_dq_on_tensor_cores(A, B, H, T, d):
+    """The drop-in backward at d 96 / 128 in the default probs mode: dK, dV from
+    the CUDA-core kernel, which also writes dS into the caller's B*H*T*T
+    scratch (the reference's size), and dQ = dS K as a 3xTF32 tensor-core GEMM
+    per (batch, head) that reads keys up to each 128-row tile's diagonal.
+    Ragged row tiles included; compared with the oracle and with the
+    explicit-shape backward (CUDA-core dQ)."""
+    import torch
+    A.check(A.lib.attn_set_macro_shape(B, H, T, d))
+    try:
+        q, k, v = qkv(7 * T + d, B, T, H, d)
+        do = synth.normal(8 * T + d, q.shape)
+        ref, probs, _ = O.attn_forward(q, k, v, B, T, H, d, want_probs=True)
+        rq, rk, rv = O.attn_backward(do, q, k, v, probs, B, T, H, d)
+        qd, kd, vd, gd = dev(q), dev(k), dev(v), dev(do)
+        att = torch.empty_like(qd)
+        probs_buf = torch.empty(B * H * T * T, device="cuda")
+        scratch = torch.full((B * H * T * T,), float("nan"), device="cuda")
+        dq, dk, dv = (torch.full_like(qd, 7.0) for _ in range(3))
+        torch.cuda.synchronize()
+        A.lib.attn_fwd(qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), att.data_ptr(), probs_buf.data_ptr())
+        A.lib.attn_bwd(dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), scratch.data_ptr(), gd.data_ptr(),
+                       qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), probs_buf.data_ptr())
+        torch.cuda.synchronize()
+        assert rel_err(host(dq), rq) < F32_TOL
+        assert rel_err(host(dk), rk) < F32_TOL
+        assert rel_err(host(dv), rv) < F32_TOL
+        o, lse = A.forward_t(qd, kd, vd, H, B)
+        fq, fk, fv = A.backward_t(gd, qd, kd, vd, o, lse, H, B)
+        torch.cuda.synchronize()
+        assert rel_err(host(dq), host(fq)) < F32_TOL
+        assert torch.equal(dk, fk) and torch.equal(dv, fv)      # the same CUDA-core kernel
+        code = ctypes.c_int()
+        A.check(A.lib.attn_device_error(0, ctypes.byref(code)))
+        assert code.value == 0
+    finally:
+        A.lib.attn_set_macro_shape(4, 12, 1024, 128)
+
+
 @pytest.mark.parametrize("B,H,T,d", [(1, 2, 1536, 128), (2, 3, 100, 128), (1, 2, 40, 64)])
 def test_drop_in_lse_only_probs(A, B, H, T, d):
     """ATTN_PROBS_LSE: `probs` shrinks to B*H*T floats and `scratch` to the
