@@ -91,7 +91,12 @@ ATTN_API void attn_fwd(const float *Q, const float *K, const float *V, float *at
 
 /* Replaces gpu_kernels.h:70 attn_bwd.  SETS dQ, dK, dV (like the reference's
  * cuBLAS path, beta = 0).  `scratch` is the caller's workspace (B*H*T*T
- * floats in train_kaggle.cu:138); this library uses 2*B*H*T floats of it.
+ * floats in train_kaggle.cu:138).  In the default ATTN_PROBS_LSE_OUT mode at
+ * head_dim 96 and 128 with T a multiple of 4, this library fills all of it
+ * with dS (as the reference's own softmax backward does) and computes dQ from
+ * it on the tensor cores, keeping its row statistics and a split copy of K in
+ * a library-owned device buffer (2*B*H*T*(1+d) floats; calls that use it must
+ * not overlap on the GPU); otherwise it uses 2*B*H*T floats of `scratch`.
  * Exits(1) with a message on failure. */
 ATTN_API void attn_bwd(float *dQ, float *dK, float *dV, float *scratch,
               const float *dAtt, const float *Q, const float *K, const float *V,
