@@ -51,10 +51,10 @@ int launch_bwd_f32(int dtype, int D, const void *dout, const void *q, const void
                    int accumulate, void *ws, long long in_stride, long long out_stride, int B,
                    int H, int T, cudaStream_t s);
 size_t bwd_f32_workspace_bytes(int B, int H, int T);
-size_t bwd_f32_tc_dq_ws_bytes(int B, int H, int T, int D);
-int launch_bwd_f32_tc_dq(int D, const void *dout, const void *q, const void *k, const void *v, const void *o,
-                         const float *lse, void *dq, void *dk, void *dv, float *ds, void *ws, long long in_stride,
-                         long long out_stride, int B, int H, int T, int *err, cudaStream_t s);
+size_t bwd_tc_ws_bytes(int B, int H, int T, int D);
+int launch_bwd_tc(int D, const float *dout, const float *q, const float *k, const float *v, const float *o,
+                  const float *lse, float *dq, float *dk, float *dv, float *ds, void *ws, long long in_stride,
+                  long long out_stride, int B, int H, int T, int *err, cudaStream_t s);
 void *library_workspace(int which, size_t bytes, cudaStream_t s);
 bool bwd_bf16_sm100_supported(int D, long long in_stride, long long out_stride);
 bool bwd_tf32_sm100_supported(int D, long long in_stride, long long out_stride);
@@ -403,20 +403,25 @@ void dropin_bwd(float *dQ, float *dK, float *dV, float *scratch, const float *dA
                                                "(ATTN_PROBS_LSE mode)"), "attn_bwd");
         out = it->second;
     }
-    // d 96 and 128 (no 3xTF32 backward): in the default probs mode the
-    // caller's scratch is the reference's B*H*T*T floats (train_kaggle.cu:138,
-    // which its own softmax backward fills with dS), so dS goes there and
-    // dQ = dS K runs on the tensor cores; the row statistics and the split K
-    // live in a library-owned buffer.
+    // d 96 and 128 (the fused 3xTF32 backward does not fit TMEM there): in the
+    // default probs mode the caller's scratch is the reference's B*H*T*T
+    // floats (train_kaggle.cu:138, which its own softmax backward fills with
+    // dS), so the backward runs as tensor-core GEMMs over explicit score
+    // tiles: dS goes to scratch, the scores, P^T, dS^T, the row statistics and
+    // the split operands to a library-owned buffer.
     if (g_probs_mode == ATTN_PROBS_LSE_OUT && (s.head_dim == 96 || s.head_dim == 128) && s.seq_len % 4 == 0 &&
-        (long long)s.batch * s.heads <= 65535 && ((reinterpret_cast<uintptr_t>(scratch) |
-        reinterpret_cast<uintptr_t>(dQ) | reinterpret_cast<uintptr_t>(K)) & 15) == 0) {
-        const size_t need = bwd_f32_tc_dq_ws_bytes(s.batch, s.heads, s.seq_len, s.head_dim);
+        (long long)s.batch * s.heads <= 65535 &&
+        ((reinterpret_cast<uintptr_t>(scratch) | reinterpret_cast<uintptr_t>(dQ) | reinterpret_cast<uintptr_t>(dK) |
+          reinterpret_cast<uintptr_t>(dV) | reinterpret_cast<uintptr_t>(Q) | reinterpret_cast<uintptr_t>(K) |
+          reinterpret_cast<uintptr_t>(V) | reinterpret_cast<uintptr_t>(dAtt) | reinterpret_cast<uintptr_t>(out)) &
+         15) == 0) {
+        const long long hd = (long long)s.heads * s.head_dim;
+        const size_t need = bwd_tc_ws_bytes(s.batch, s.heads, s.seq_len, s.head_dim);
         void *ws = library_workspace(1, need, nullptr);
         if (!ws) die_on(set_error(ATTN_ERR_NOMEM, "attn_bwd: cannot allocate a %zu-byte workspace", need), "attn_bwd");
-        const long long hd = (long long)s.heads * s.head_dim;
-        die_on(launch_bwd_f32_tc_dq(s.head_dim, dAtt, Q, K, V, out, lse, dQ, dK, dV, scratch, ws, hd, hd, s.batch,
-                                    s.heads, s.seq_len, device_error_ptr(), nullptr),
+        die_on(launch_bwd_tc(s.head_dim, static_cast<const float *>(dAtt), Q, K, V, static_cast<const float *>(out),
+                             lse, dQ, dK, dV, scratch, ws, hd, hd, s.batch, s.heads, s.seq_len, device_error_ptr(),
+                             nullptr),
                "attn_bwd");
         return;
     }

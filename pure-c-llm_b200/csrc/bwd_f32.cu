@@ -24,8 +24,6 @@ struct BwdParams {
     int B, H, T, accumulate;
     float qk_scale;            // log2(e) / sqrt(d)
     float ds_scale;            // 1 / sqrt(d)
-    float *ds;                 // bwd_dkdv_kernel<.., true>: dS as [B*H][T][ds_ld], rows i, keys j
-    long long ds_ld;
 };
 
 template <typename T, int D>
@@ -114,12 +112,7 @@ __device__ __forceinline__ void store_row4(T *dst, float4 v, bool acc) {
 }
 
 // ---- dK, dV: one CTA per key tile ------------------------------------------
-// WDS: also write dS (the scaled score gradients, 0 above the diagonal) of
-// every visited (query tile, key tile) pair into p.ds, rows i and keys j, so
-// that dQ = dS K can run as a tensor-core GEMM instead of bwd_dq_kernel.  The
-// CTA of an odd key tile kt also zeroes the pair (kt - 1, kt), above the
-// diagonal, which a 128-row GEMM tile reads.
-template <typename T, int D, bool WDS = false>
+template <typename T, int D>
 __global__ void __launch_bounds__(kFThreads)
 bwd_dkdv_kernel(const BwdParams p)
 {
@@ -168,19 +161,6 @@ bwd_dkdv_kernel(const BwdParams p)
     for (int i = 0; i < 4; i++)
 #pragma unroll
         for (int c = 0; c < D / 8; c++) { dk[i][c] = 0.f; dvv[i][c] = 0.f; }
-    float *dsg = nullptr;
-    if constexpr (WDS) {
-        dsg = p.ds + ((long long)b * p.H + h) * p.T * p.ds_ld;
-        if ((kt & 1) && kt > 0) {                 // the pair above the diagonal: zeros
-            const int lane = tid & 31, wp = tid >> 5;
-            for (int r = wp; r < kFBM; r += kFThreads / 32) {
-                const int qi = (kt - 1) * kFBM + r;
-#pragma unroll
-                for (int hh = 0; hh < 2; hh++)
-                    if (k0 + lane + 32 * hh < p.T) dsg[(long long)qi * p.ds_ld + k0 + lane + 32 * hh] = 0.f;
-            }
-        }
-    }
 
     for (int qt = kt; qt < n_t; qt++) {
         const int buf = NB == 2 ? ((qt - kt) & 1) : 0;
@@ -233,21 +213,6 @@ bwd_dkdv_kernel(const BwdParams p)
 
         tile_wM<D>(dvv, W1, Gb, ty, tx);
         tile_wM<D>(dk, W2, Qb, ty, tx);
-        if constexpr (WDS) {
-            // W2[q][c] holds dS for query q and key ty + 16 i at c = 4 ty + i: a warp
-            // writes one query row at a time, 64 keys as two coalesced 128-byte runs
-            const int lane = tid & 31, wp = tid >> 5;
-            for (int r = wp; r < kFBM; r += kFThreads / 32) {
-                const int qi = qt * kFBM + r;
-                if (qi >= p.T) break;
-#pragma unroll
-                for (int hh = 0; hh < 2; hh++) {
-                    const int kk = lane + 32 * hh;                  // key within the tile
-                    if (k0 + kk < p.T)
-                        dsg[(long long)qi * p.ds_ld + k0 + kk] = W2[r * (kFBM + 4) + 4 * (kk & 15) + (kk >> 4)];
-                }
-            }
-        }
         __syncthreads();
         if (NB == 1 && qt + 1 < n_t) { stage_q(qt + 1, 0); cp_async_commit(); }
     }
@@ -434,59 +399,6 @@ static int launch_bwd_f32_t(const attn::BwdParams &p, cudaStream_t s) {
     return check_pdl(launch_pdl(bwd_dq_kernel<T, D>, grid, dim3(kFThreads), smem_q, s, p), "bwd_dq_kernel");
 }
 
-int launch_dq_gemm_sm100(const float *ds, long long ds_ld, const float *k, long long in_stride, float *dq,
-                         long long out_stride, int B, int H, int T, int D, void *ws, int *err, cudaStream_t stream);
-size_t dq_gemm_ws_bytes(int B, int H, int T, int D);
-
-template <int D>
-static int launch_bwd_f32_tc_dq_t(const attn::BwdParams &p, void *kt_ws, int *err, cudaStream_t s) {
-    using namespace attn;
-    constexpr int TF = FTile<D>::FLOATS;
-    constexpr int NB = BwdCfg<D>::NBUF;
-    const size_t smem_kv = (size_t)((2 + 2 * NB) * TF + 2 * kFBN * (kFBM + 4) + NB * 128) * sizeof(float);
-    if (!ensure_smem_attr((const void *)bwd_dkdv_kernel<float, D, true>, smem_kv))
-        return set_error(ATTN_ERR_CUDA, "bwd_f32: cannot set shared-memory size");
-    int st = launch_rowdot_t<float, D>(p, s);
-    if (st) return st;
-    dim3 grid((p.T + kFBM - 1) / kFBM, p.H, p.B);
-    if ((st = check_pdl(launch_pdl(bwd_dkdv_kernel<float, D, true>, grid, dim3(kFThreads), smem_kv, s, p),
-                        "bwd_dkdv_kernel (dS)")))
-        return st;
-    return launch_dq_gemm_sm100(p.ds, p.ds_ld, static_cast<const float *>(p.k), p.in_stride, static_cast<float *>(p.dq),
-                                p.out_stride, p.B, p.H, p.T, D, kt_ws, err, s);
-}
-
-// Bytes of the workspace launch_bwd_f32_tc_dq takes besides the dS buffer.
-size_t bwd_f32_tc_dq_ws_bytes(int B, int H, int T, int D) {
-    return (bwd_f32_workspace_bytes(B, H, T) + 255) / 256 * 256 + dq_gemm_ws_bytes(B, H, T, D);
-}
-
-// fp32 backward at d 96 / 128 with dQ on the tensor cores: the FFMA dK/dV
-// kernel also writes dS (scaled, zero above the diagonal) into `ds`
-// ([B*H][T][T] floats, T % 4 == 0), and dQ = dS K runs as a 3xTF32 GEMM.
-// dQ, dK and dV are SET.  ws: bwd_f32_tc_dq_ws_bytes, 256-byte aligned.
-int launch_bwd_f32_tc_dq(int D, const void *dout, const void *q, const void *k, const void *v, const void *o,
-                         const float *lse, void *dq, void *dk, void *dv, float *ds, void *ws, long long in_stride,
-                         long long out_stride, int B, int H, int T, int *err, cudaStream_t s) {
-    attn::BwdParams p;
-    p.q = q; p.k = k; p.v = v; p.o = o; p.dout = dout; p.lse = lse;
-    p.lse2 = static_cast<float *>(ws);
-    p.dvec = p.lse2 + (long long)B * H * T;
-    p.dq = dq; p.dk = dk; p.dv = dv;
-    p.in_stride = in_stride; p.out_stride = out_stride;
-    p.B = B; p.H = H; p.T = T; p.accumulate = 0;
-    p.qk_scale = attn::kLog2e / sqrtf((float)D);
-    p.ds_scale = 1.0f / sqrtf((float)D);
-    p.ds = ds;
-    p.ds_ld = T;
-    void *kt_ws = static_cast<char *>(ws) + (bwd_f32_workspace_bytes(B, H, T) + 255) / 256 * 256;
-    switch (D) {
-        case 96: return launch_bwd_f32_tc_dq_t<96>(p, kt_ws, err, s);
-        case 128: return launch_bwd_f32_tc_dq_t<128>(p, kt_ws, err, s);
-        default: return set_error(ATTN_ERR_UNSUPPORTED, "bwd (dQ on tensor cores): head_dim %d", D);
-    }
-}
-
 int launch_bwd_f32(int dtype, int D, const void *dout, const void *q, const void *k,
                    const void *v, const void *o, const float *lse, void *dq, void *dk, void *dv,
                    int accumulate, void *ws, long long in_stride, long long out_stride, int B,
@@ -501,8 +413,6 @@ int launch_bwd_f32(int dtype, int D, const void *dout, const void *q, const void
     p.B = B; p.H = H; p.T = T; p.accumulate = accumulate;
     p.qk_scale = attn::kLog2e / sqrtf((float)D);
     p.ds_scale = 1.0f / sqrtf((float)D);
-    p.ds = nullptr;
-    p.ds_ld = 0;
     const bool bf = dtype == ATTN_BF16;
     switch (D) {
         case 32: return bf ? launch_bwd_f32_t<__nv_bfloat16, 32>(p, s) : launch_bwd_f32_t<float, 32>(p, s);

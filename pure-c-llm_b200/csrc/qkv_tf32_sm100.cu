@@ -10,10 +10,10 @@
 // row stride ldo -- three separate tensors, or the three column blocks of one
 // (M x 3N) tensor that the attention kernels read as it is (in_row_stride 3N).
 //
-// Every product x*y is formed as xh*yh + xh*yl + xl*yh (xh: x with its 13 low
-// mantissa bits cleared, exact in tf32; xl = x - xh, exact in fp32); the
-// dropped xl*yl term is ~2^-21 relative.  The tensor core's accumulation into
-// TMEM is not round-to-nearest, so a fresh TMEM sum starts every kFold k
+// Every product x*y is formed as xh*yh + xh*yl + xl*yh (xh: x rounded to the
+// nearest tf32 value, exact in tf32; xl = x - xh, exact in fp32); the
+// dropped xl*yl term is ~2^-22 relative.  The tensor core's accumulation into
+// TMEM is not round-to-nearest, so a fresh TMEM sum starts every Params::fold k
 // stages and the epilogue warps add the partial sums into fp32 registers.
 //
 // Two launches per call:
@@ -65,7 +65,12 @@ constexpr int BN = 128;            // output columns per tile
 constexpr int BK = 32;             // k per stage (one 128-byte swizzle row of fp32)
 constexpr int kThreads = 384;
 constexpr int kStages = 4;
-constexpr int kFold = 8;           // k stages per fresh TMEM sum (256 k)
+// k stages per fresh TMEM sum (Params::fold): 8 (256 k) for the projection;
+// 2 (64 k) for the backward's GEMMs, whose sums cancel more: at the trainer
+// shape their largest errors against the reference fall from 3.4e-6 (dQ),
+// 6.5e-6 (dK) and 5.1e-6 (dV) with 8 to 1.6e-6, 3.3e-6 and 2.7e-6, for 1 % of
+// the backward's time (1 stage: 1.0e-6 / 2.5e-6 / 2.2e-6, 7 % slower).
+constexpr int kFoldQKV = 8, kFoldBwd = 2;
 constexpr int XB = BM * BK * 4;    // 16 KB: one X part
 constexpr int WB = BN * BK * 4;    // 16 KB: one W part
 constexpr int STAGE = XB + 2 * WB;
@@ -90,18 +95,26 @@ enum {
     B_COUNT = 17
 };
 
-// mode 0: the Q, K, V projection.  mode 1: dQ = dS K of the causal backward
-// for every (batch, head): A = dS [bh][T rows][T keys] (zero above the
-// diagonal), B = that head's K transposed and split (K^T high / low
-// [bh][d][Tp]), C = dQ in the activation layout; an item is one 128-row tile
-// of one (batch, head) and reads keys 0 .. min(m0 + 128, T) only.
+// mode 0: the Q, K, V projection.
+// mode 1: dQ = dS K of the causal backward for every (batch, head): A = dS
+//   [bh][T rows][T keys] (zero above the diagonal), B = that head's K
+//   transposed and split (K^T high / low [bh][d][Tp]), C = dQ in the activation
+//   layout; an item is one 128-row tile of one (batch, head) and reads keys
+//   0 .. min(m0 + 128, T) only.
+// mode 2: dV = P^T dO or dK = dS^T Q: as mode 1 with A = P^T or dS^T [bh][T
+//   keys][T queries] (zero left of the diagonal), reading queries m0 .. T only.
+// mode 3: the scores X = Q K^T or Y = dO V^T per (batch, head), 128 x 128 tiles
+//   at or below the diagonal: A = Q or dO read raw in the activation layout, B =
+//   K or V split by rows ([bh][T][d] high / low), C = the tile of a
+//   [bh][T][T] buffer.
 struct Params {
     const float *bias[3];
-    int M, N, K;                   // (N: out_features, K: in_features; mode 1: T, d, T)
-    int mode, H;                   // mode 1: heads (bh = b * H + h)
+    int M, N, K;                   // (N: out_features, K: in_features; modes 1-2: T, d, T; mode 3: T, T, d)
+    int mode, H, D;                // modes 1-3: heads (bh = b * H + h), head dim
     int mt, nt;                    // row tiles, column tiles per output
     int n_items, nk;
     int *err;
+    int fold;                      // k stages per fresh TMEM sum (a power of two)
     int stall;                     // test hook: the MMA warp first waits on B_STALL for
     long long stall_limit;         // stall_limit SM cycles (the other waits keep their bound)
 };
@@ -109,9 +122,20 @@ struct Params {
 // mode 0: output w, rows m0.., columns n0..; mode 1: w = (batch, head) index,
 // n0 = 0, items longest first (the last row tiles read the most keys)
 __device__ __forceinline__ void item_coords(const Params &p, int item, int &m0, int &w, int &n0) {
-    if (p.mode == 1) {
+    if (p.mode == 3) {                             // (bh, query tile qt, key tile kt <= qt)
+        const int pairs = p.mt * (p.mt + 1) / 2;
+        w = item / pairs;
+        const int r = item % pairs;
+        int qt = (int)((sqrtf(8.f * (float)r + 1.f) - 1.f) * 0.5f);
+        while (qt * (qt + 1) / 2 > r) qt--;
+        while ((qt + 1) * (qt + 2) / 2 <= r) qt++;
+        m0 = qt * BM;
+        n0 = (r - qt * (qt + 1) / 2) * BN;
+        return;
+    }
+    if (p.mode == 1 || p.mode == 2) {              // longest first: mode 1's last tiles, mode 2's first
         const int bhn = p.n_items / p.mt;
-        m0 = (p.mt - 1 - item / bhn) * BM;
+        m0 = (p.mode == 1 ? p.mt - 1 - item / bhn : item / bhn) * BM;
         w = item % bhn;
         n0 = 0;
         return;
@@ -121,10 +145,13 @@ __device__ __forceinline__ void item_coords(const Params &p, int item, int &m0, 
     w = ng / p.nt;
     n0 = (ng % p.nt) * BN;
 }
-// k stages of an item
+// k stages of an item, and its first k stage
 __device__ __forceinline__ int item_nk(const Params &p, int m0) {
-    return p.mode == 1 ? (min(m0 + BM, p.K) + BK - 1) / BK : p.nk;
+    if (p.mode == 1) return (min(m0 + BM, p.K) + BK - 1) / BK;
+    if (p.mode == 2) return (p.K + BK - 1) / BK - m0 / BK;
+    return p.nk;
 }
+__device__ __forceinline__ int item_k0(const Params &p, int m0) { return p.mode == 2 ? m0 / BK : 0; }
 
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, uint32_t bar, int x, int y) {
     asm volatile(
@@ -140,7 +167,14 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, uint32_t sr
 }
 __device__ __forceinline__ void bulk_wait_read_1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
 
-__device__ __forceinline__ float hi_part(float x) { return __uint_as_float(__float_as_uint(x) & 0xFFFFE000u); }
+// The high part is x rounded to the nearest tf32 value (its 13 low mantissa
+// bits cleared after adding half of their weight), so the low part x - xh,
+// exact in fp32, is at most half a tf32 step: the MMA's tf32 view of it then
+// loses at most 2^-23 of x, where clearing the bits without rounding loses
+// up to 2^-21 (and the dropped xl * yl term shrinks from 2^-20 to 2^-22).
+__device__ __forceinline__ float hi_part(float x) {
+    return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u);
+}
 
 // W (K x N, row-major, one of three) -> rows [w*N, (w+1)*N) of W^T high and
 // low (3N x Kp).  A block moves a 32 x 32 tile through shared memory: reads
@@ -200,6 +234,104 @@ split_kt_kernel(const float *__restrict__ k, float *__restrict__ kth, float *__r
             const long long o = ((long long)bh * D + n) * Tp + j;
             kth[o] = hh;
             ktl[o] = x - hh;
+        }
+    }
+}
+
+// K or V of every (batch, head), split by rows: [bh][T][D] high and low (the
+// B operand of the score GEMMs, K-major along d as it is in memory).
+__global__ void __launch_bounds__(256)
+split_rows_kernel(const float *__restrict__ src, float *__restrict__ dh, float *__restrict__ dl, long long in_stride,
+                  int T, int H, int D, long long total4)
+{
+    pdl_begin();   // launched by launch_pdl
+    const int d4 = D / 4;
+    for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < total4;
+         e += (long long)gridDim.x * blockDim.x) {
+        const long long row = e / d4;              // bh * T + j
+        const int c = (int)(e % d4) * 4;
+        const int bh = (int)(row / T), j = (int)(row % T);
+        const float4 x = __ldg(reinterpret_cast<const float4 *>(
+            src + ((long long)(bh / H) * T + j) * in_stride + (long long)(bh % H) * D + c));
+        const float4 h = make_float4(hi_part(x.x), hi_part(x.y), hi_part(x.z), hi_part(x.w));
+        *reinterpret_cast<float4 *>(dh + row * D + c) = h;
+        *reinterpret_cast<float4 *>(dl + row * D + c) = make_float4(x.x - h.x, x.y - h.y, x.z - h.z, x.w - h.w);
+    }
+}
+
+// One 128 x 128 tile (query tile qt, key tile kt <= qt) of one (batch, head):
+// from the scores X = Q K^T (buf1) and Y = dO V^T (buf2), both [bh][T][T] with
+// rows i, keys j, forms P = 2^(X log2(e)/sqrt(d) - lse2_i) and
+// dS = P (Y - D_i) / sqrt(d) (0 for j > i, train.c:385-400 restated on the
+// saved row statistics), and writes dS (rows i) into `ds`, and P^T and dS^T
+// (rows j) into the tile (kt, qt) of buf1 and buf2 -- above the diagonal,
+// where no score tile lives; the diagonal tile is read whole before it is
+// overwritten.
+constexpr int kSgLd = 129;                         // padded row of the shared tiles (odd: conflict-free columns)
+constexpr int kSgThreads = 512;
+__global__ void __launch_bounds__(kSgThreads)
+scores_to_grads_kernel(float *__restrict__ buf1, float *__restrict__ buf2, const float *__restrict__ lse2,
+                       const float *__restrict__ dvec, float *__restrict__ ds, int T, int mt, float qk_scale,
+                       float ds_scale)
+{
+    pdl_begin();   // launched by launch_pdl
+    extern __shared__ float sg[];
+    float *sx = sg, *sy = sg + BM * kSgLd;
+    __shared__ float rl[BM], rd[BM];
+    const int bh = blockIdx.y;
+    const int r = blockIdx.x;
+    int qt = (int)((sqrtf(8.f * (float)r + 1.f) - 1.f) * 0.5f);
+    while (qt * (qt + 1) / 2 > r) qt--;
+    while ((qt + 1) * (qt + 2) / 2 <= r) qt++;
+    const int kt = r - qt * (qt + 1) / 2;
+    const int i0 = qt * BM, j0 = kt * BN;
+    const long long base = (long long)bh * T * T;
+    if (threadIdx.x < BM) {
+        const int i = i0 + threadIdx.x;
+        rl[threadIdx.x] = i < T ? lse2[(long long)bh * T + i] : 0.f;
+        rd[threadIdx.x] = i < T ? dvec[(long long)bh * T + i] : 0.f;
+    }
+    // rows of 128 floats as 32 float4 (T % 4 == 0, so a float4 is all in or all out)
+    for (int idx = threadIdx.x; idx < BM * (BN / 4); idx += kSgThreads) {
+        const int a = idx >> 5, c = (idx & 31) * 4, i = i0 + a, j = j0 + c;
+        float4 x = make_float4(0.f, 0.f, 0.f, 0.f), y = x;
+        if (i < T && j < T) {
+            x = *reinterpret_cast<const float4 *>(buf1 + base + (long long)i * T + j);
+            y = *reinterpret_cast<const float4 *>(buf2 + base + (long long)i * T + j);
+        }
+        float *px = sx + a * kSgLd + c, *py = sy + a * kSgLd + c;
+        px[0] = x.x; px[1] = x.y; px[2] = x.z; px[3] = x.w;
+        py[0] = y.x; py[1] = y.y; py[2] = y.z; py[3] = y.w;
+    }
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < BM * BN; idx += kSgThreads) {
+        const int a = idx >> 7, c = idx & 127, i = i0 + a, j = j0 + c;
+        float pv = 0.f, dv = 0.f;
+        if (i < T && j < T && j <= i) {
+            pv = exp2f(sx[a * kSgLd + c] * qk_scale - rl[a]);
+            dv = pv * (sy[a * kSgLd + c] - rd[a]) * ds_scale;
+        }
+        sx[a * kSgLd + c] = pv;
+        sy[a * kSgLd + c] = dv;
+    }
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < BM * (BN / 4); idx += kSgThreads) {
+        const int a = idx >> 5, c = (idx & 31) * 4;          // dS, rows i
+        const int i = i0 + a, j = j0 + c;
+        if (i < T && j < T) {
+            const float *py = sy + a * kSgLd + c;
+            *reinterpret_cast<float4 *>(ds + base + (long long)i * T + j) = make_float4(py[0], py[1], py[2], py[3]);
+        }
+    }
+    for (int idx = threadIdx.x; idx < BN * (BM / 4); idx += kSgThreads) {
+        const int c = idx >> 5, a = (idx & 31) * 4;          // P^T and dS^T, rows j: column c of the tiles
+        const int i = i0 + a, j = j0 + c;
+        if (i < T && j < T) {
+            const float *px = sx + a * kSgLd + c, *py = sy + a * kSgLd + c;
+            *reinterpret_cast<float4 *>(buf1 + base + (long long)j * T + i) =
+                make_float4(px[0], px[kSgLd], px[2 * kSgLd], px[3 * kSgLd]);
+            *reinterpret_cast<float4 *>(buf2 + base + (long long)j * T + i) =
+                make_float4(py[0], py[kSgLd], py[2 * kSgLd], py[3 * kSgLd]);
         }
     }
 }
@@ -264,17 +396,22 @@ qkv_tf32_kernel(const __grid_constant__ CUtensorMap tx, const __grid_constant__ 
                 item_coords(p, item, m0, w, n0);
                 const int wrow = w * p.N + n0;               // rows of W^T (rows past N read the next
                                                              // weight's or zeros; their columns are not stored)
-                const int nk = item_nk(p, m0);
+                const int nk = item_nk(p, m0), k0 = item_k0(p, m0);
                 for (int ks = 0; ks < nk; ks++, g++) {
                     const int st = g % kStages;
                     if (g >= kStages && !(ok = wait_w(B_EMPTY + st, g / kStages - 1, 0x501))) break;
                     if (leader) {
                         const uint32_t s0 = base + st * STAGE;
+                        const int kx = (k0 + ks) * BK;
                         mbar_arrive_expect_tx(BAR(B_FULL + st), XB + 2 * WB);
-                        if (p.mode == 1) {                   // 3-D maps over the (batch, head) index
-                            tma_load_3d(s0 + OFF_X, &tx, BAR(B_FULL + st), ks * BK, m0, w);
-                            tma_load_3d(s0 + OFF_WH, &twh, BAR(B_FULL + st), ks * BK, 0, w);
-                            tma_load_3d(s0 + OFF_WL, &twl, BAR(B_FULL + st), ks * BK, 0, w);
+                        if (p.mode == 1 || p.mode == 2) {    // 3-D maps over the (batch, head) index
+                            tma_load_3d(s0 + OFF_X, &tx, BAR(B_FULL + st), kx, m0, w);
+                            tma_load_3d(s0 + OFF_WH, &twh, BAR(B_FULL + st), kx, 0, w);
+                            tma_load_3d(s0 + OFF_WL, &twl, BAR(B_FULL + st), kx, 0, w);
+                        } else if (p.mode == 3) {            // A raw in the activation layout
+                            tma_load_3d(s0 + OFF_X, &tx, BAR(B_FULL + st), (w % p.H) * p.D + kx, m0, w / p.H);
+                            tma_load_3d(s0 + OFF_WH, &twh, BAR(B_FULL + st), kx, n0, w);
+                            tma_load_3d(s0 + OFF_WL, &twl, BAR(B_FULL + st), kx, n0, w);
                         } else {
                             tma_load_2d(s0 + OFF_X, &tx, BAR(B_FULL + st), ks * BK, m0);
                             tma_load_2d(s0 + OFF_WH, &twh, BAR(B_FULL + st), ks * BK, wrow);
@@ -298,7 +435,8 @@ qkv_tf32_kernel(const __grid_constant__ CUtensorMap tx, const __grid_constant__ 
                 const int nk = item_nk(p, m0);
                 for (int ks = 0; ks < nk; ks++, g++) {
                     const int a = ch & 1;
-                    if (ks % kFold == 0 && ch >= 2 && !(ok = wait_w(B_ACCE + a, ch / 2 - 1, 0x511))) break;
+                    const int kf = ks & (p.fold - 1);      // stage within the TMEM sum
+                    if (kf == 0 && ch >= 2 && !(ok = wait_w(B_ACCE + a, ch / 2 - 1, 0x511))) break;
                     const int st = g % kStages;
                     if (!(ok = wait_w(B_SPLIT + st, g / kStages, 0x512))) break;
                     tc_fence_after();
@@ -311,11 +449,11 @@ qkv_tf32_kernel(const __grid_constant__ CUtensorMap tx, const __grid_constant__ 
 #pragma unroll
                             for (int kk = 0; kk < BK / 8; kk++)
                                 mma_tf32_ts(tmem + BN * a, xa + 8 * kk, sw128_desc(wb + 32 * kk, 16, 1024), idD,
-                                            (ks % kFold > 0 || part > 0 || kk > 0));
+                                            (kf > 0 || part > 0 || kk > 0));
                         }
                         mma_commit(BAR(B_EMPTY + st));
                     }
-                    const bool last = ks % kFold == kFold - 1 || ks == nk - 1;
+                    const bool last = kf == p.fold - 1 || ks == nk - 1;
                     if (last) {
                         if (leader) mma_commit(BAR(B_ACCF + a));
                         ch++;
@@ -377,7 +515,7 @@ qkv_tf32_kernel(const __grid_constant__ CUtensorMap tx, const __grid_constant__ 
         for (int item = blockIdx.x; ok && item < p.n_items; item += gridDim.x) {
             int m0, w, n0;
             item_coords(p, item, m0, w, n0);
-            const int nchunks = (item_nk(p, m0) + kFold - 1) / kFold;
+            const int nchunks = (item_nk(p, m0) + p.fold - 1) / p.fold;
 #pragma unroll
             for (int c = 0; c < BN; c++) acc[c] = 0.f;
             for (int c = 0; c < nchunks; c++, ch++) {
@@ -397,8 +535,8 @@ qkv_tf32_kernel(const __grid_constant__ CUtensorMap tx, const __grid_constant__ 
             }
             if (!ok) break;
             // bias, then 32 x 32 blocks through shared memory (128-byte swizzle) to TMA stores
-            const float *bias = p.mode == 1 ? nullptr : p.bias[w];
-            const CUtensorMap *mo = p.mode == 1 || w == 0 ? &to0 : w == 1 ? &to1 : &to2;
+            const float *bias = p.mode != 0 ? nullptr : p.bias[w];
+            const CUtensorMap *mo = p.mode != 0 || w == 0 ? &to0 : w == 1 ? &to1 : &to2;
             const bool rows_in = m0 + 32 * quad < p.M;       // TMA clips partial boxes; skip empty ones
 #pragma unroll
             for (int q = 0; q < BN / 32; q++) {
@@ -420,8 +558,10 @@ qkv_tf32_kernel(const __grid_constant__ CUtensorMap tx, const __grid_constant__ 
                 fence_async_smem();
                 __syncwarp();
                 if (leader) {
-                    if (p.mode == 1)                  // dQ rows b*T + i, columns h*d + n
+                    if (p.mode == 1 || p.mode == 2)   // dQ / dK / dV rows b*T + i, columns h*d + n
                         tma_store_3d(mo, smem_u32(buf), (w % p.H) * p.N + col0, m0 + 32 * quad, w / p.H);
+                    else if (p.mode == 3)             // the score tile of the [bh][T][T] buffer
+                        tma_store_3d(mo, smem_u32(buf), col0, m0 + 32 * quad, w);
                     else
                         tma_store_2d(mo, smem_u32(buf), col0, m0 + 32 * quad);
                     bulk_commit_group();
@@ -541,6 +681,8 @@ int launch_qkv_tf32_sm100(const attn_qkv_shape *s, const float *x, const float *
     p.K = s->in_features;
     p.mode = 0;
     p.H = 0;
+    p.D = 0;
+    p.fold = kFoldQKV;
     p.mt = (p.M + BM - 1) / BM;
     p.nt = (p.N + BN - 1) / BN;
     p.n_items = 3 * p.mt * p.nt;
@@ -583,56 +725,144 @@ static bool map_3d(CUtensorMap *m, const void *ptr, long long cols, long long ro
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// Bytes of the split K the dQ GEMM needs (K^T high, then low).
-size_t dq_gemm_ws_bytes(int B, int H, int T, int D) {
-    const long long Tp = ((long long)T + 3) / 4 * 4;
-    return 2 * (((size_t)B * H * D * Tp * 4 + 255) / 256 * 256);
-}
+// ---------------------------------------------------------------------------
+// fp32 backward at d 96 / 128 with every product on the tensor cores
+// ---------------------------------------------------------------------------
+int launch_bwd_rowdot(int dtype, int D, const void *o, const void *dout, const float *lse, float *ws,
+                      long long in_stride, long long out_stride, int B, int H, int T, cudaStream_t s);
 
-// dQ = dS K per (batch, head) on the tensor cores (3xTF32), SET: dS is
-// [B*H][T][ds_ld] fp32 with zeros above the diagonal for every 128 x 128
-// block the GEMM reads (bwd_dkdv_kernel<.., true> writes it); ws holds
-// dq_gemm_ws_bytes.  Needs ds_ld % 4 == 0 and 16-byte aligned tensors.
-int launch_dq_gemm_sm100(const float *ds, long long ds_ld, const float *k, long long in_stride, float *dq,
-                         long long out_stride, int B, int H, int T, int D, void *ws, int *err, cudaStream_t stream) {
+namespace {
+struct BwdTcLayout {
+    size_t off[14];
+    size_t total;
+    BwdTcLayout(int B, int H, int T, int D) {
+        const size_t BH = (size_t)B * H, Tp = ((size_t)T + 3) / 4 * 4;
+        const size_t sz[14] = {2 * BH * T,                                   // lse2, D
+                               BH * T * D, BH * T * D, BH * T * D, BH * T * D, // K, V rows: high, low
+                               BH * D * Tp, BH * D * Tp, BH * D * Tp,          // K^T, Q^T, dO^T high
+                               BH * D * Tp, BH * D * Tp, BH * D * Tp,          //              low
+                               BH * T * T, BH * T * T, 0};                     // buf1, buf2
+        size_t o = 0;
+        for (int i = 0; i < 14; i++) {
+            off[i] = o;
+            o += (sz[i] * 4 + 255) / 256 * 256;
+        }
+        total = o;
+    }
+};
+}  // namespace
+
+size_t bwd_tc_ws_bytes(int B, int H, int T, int D) { return BwdTcLayout(B, H, T, D).total; }
+
+static int launch_gemm_mode(int mode, const CUtensorMap &a, const CUtensorMap &bh, const CUtensorMap &bl,
+                            const CUtensorMap &out, int T, int H, int D, long long BH, int *err, cudaStream_t stream) {
     using namespace attn::qkv;
-    const long long Tp = ((long long)T + 3) / 4 * 4;
-    const size_t half = dq_gemm_ws_bytes(B, H, T, D) / 2;
-    float *kth = static_cast<float *>(ws);
-    float *ktl = reinterpret_cast<float *>(static_cast<char *>(ws) + half);
-    const long long BH = (long long)B * H;
-    CUtensorMap mx, mwh, mwl, mo;
-    if (!map_3d(&mx, ds, T, T, BH, ds_ld, (long long)T * ds_ld, BK, BM) ||
-        !map_3d(&mwh, kth, T, D, BH, Tp, (long long)D * Tp, BK, BN) ||
-        !map_3d(&mwl, ktl, T, D, BH, Tp, (long long)D * Tp, BK, BN) ||
-        !map_3d(&mo, dq, (long long)H * D, T, B, out_stride, (long long)T * out_stride, 32, 32))
-        return set_error(ATTN_ERR_CUDA, "dQ GEMM: cuTensorMapEncodeTiled failed");
     Params p;
     for (int i = 0; i < 3; i++) p.bias[i] = nullptr;
-    p.M = T;
-    p.N = D;
-    p.K = T;
-    p.mode = 1;
+    p.mode = mode;
     p.H = H;
+    p.D = D;
+    p.fold = kFoldBwd;
+    p.M = T;
     p.mt = (T + BM - 1) / BM;
-    p.nt = 1;
-    p.n_items = (int)(BH * p.mt);
-    p.nk = (T + BK - 1) / BK;
+    if (mode == 3) {
+        p.N = T;
+        p.K = D;
+        p.nt = p.mt;
+        p.n_items = (int)(BH * p.mt * (p.mt + 1) / 2);
+        p.nk = (D + BK - 1) / BK;
+    } else {
+        p.N = D;
+        p.K = T;
+        p.nt = 1;
+        p.n_items = (int)(BH * p.mt);
+        p.nk = (T + BK - 1) / BK;
+    }
     p.err = err;
     p.stall = 0;
     p.stall_limit = 0;
-    const dim3 sgrid((D + 31) / 32, (T + 31) / 32, (unsigned)BH);
-    int st = check_pdl(launch_pdl(split_kt_kernel, sgrid, dim3(256), 0, stream, k, kth, ktl, in_stride, T, H, D, Tp),
-                       "dQ GEMM: K split kernel");
-    if (st != ATTN_OK) return st;
     const int ctas = std::max(1, std::min(sm_count_here(), p.n_items));
-    if (!ensure_smem_attr((const void *)qkv_tf32_kernel, SMEM))
-        return set_error(ATTN_ERR_CUDA, "dQ GEMM: cannot set shared-memory size");
-    if (!ensure_carveout((const void *)qkv_tf32_kernel, 100))
-        return set_error(ATTN_ERR_CUDA, "dQ GEMM: cannot set the shared-memory carveout");
-    return check_pdl(launch_pdl(qkv_tf32_kernel, dim3(ctas), dim3(kThreads), (size_t)SMEM, stream, mx, mwh, mwl, mo,
-                                mo, mo, p),
-                     "dQ GEMM kernel");
+    if (!ensure_smem_attr((const void *)qkv_tf32_kernel, SMEM) || !ensure_carveout((const void *)qkv_tf32_kernel, 100))
+        return set_error(ATTN_ERR_CUDA, "tensor-core backward: cannot set the GEMM kernel's shared memory");
+    return check_pdl(launch_pdl(qkv_tf32_kernel, dim3(ctas), dim3(kThreads), (size_t)SMEM, stream, a, bh, bl, out, out,
+                                out, p),
+                     "tensor-core backward GEMM");
+}
+
+// dQ, dK, dV (SET) from dO, Q, K, V, O and lse at d 96 / 128 with every product
+// on the tensor cores (3xTF32): the scores X = Q K^T and Y = dO V^T as GEMM
+// tiles at or below the diagonal, P and dS from them, then dQ = dS K,
+// dV = P^T dO and dK = dS^T Q as GEMMs that read only their causal k range.
+// `ds` is a [B*H][T][T] fp32 buffer (the reference trainer's scratch); ws holds
+// bwd_tc_ws_bytes (256-byte aligned).  Needs T % 4 == 0, the strides % 4 == 0,
+// 16-byte aligned tensors and B*H <= 65535.
+int launch_bwd_tc(int D, const float *dout, const float *q, const float *k, const float *v, const float *o,
+                  const float *lse, float *dq, float *dk, float *dv, float *ds, void *ws, long long in_stride,
+                  long long out_stride, int B, int H, int T, int *err, cudaStream_t s) {
+    using namespace attn::qkv;
+    const BwdTcLayout L(B, H, T, D);
+    char *w = static_cast<char *>(ws);
+    auto F = [&](int i) { return reinterpret_cast<float *>(w + L.off[i]); };
+    float *stats = F(0), *krh = F(1), *krl = F(2), *vrh = F(3), *vrl = F(4);
+    float *kth = F(5), *qth = F(6), *oth = F(7), *ktl = F(8), *qtl = F(9), *otl = F(10);
+    float *buf1 = F(11), *buf2 = F(12);
+    const long long BH = (long long)B * H, Tp = ((long long)T + 3) / 4 * 4;
+    const float qk_scale = attn::kLog2e / sqrtf((float)D), ds_scale = 1.0f / sqrtf((float)D);
+    int st = launch_bwd_rowdot(ATTN_F32, D, o, dout, lse, stats, in_stride, out_stride, B, H, T, s);
+    if (st) return st;
+    const long long total4 = BH * T * D / 4;
+    const int rgrid = (int)std::min<long long>((total4 + 255) / 256, 4L * sm_count_here());
+    if ((st = check_pdl(launch_pdl(split_rows_kernel, dim3(rgrid), dim3(256), 0, s, k, krh, krl, in_stride, T, H, D,
+                                   total4), "split K rows")) ||
+        (st = check_pdl(launch_pdl(split_rows_kernel, dim3(rgrid), dim3(256), 0, s, v, vrh, vrl, in_stride, T, H, D,
+                                   total4), "split V rows")))
+        return st;
+    const dim3 tgrid((D + 31) / 32, (T + 31) / 32, (unsigned)BH);
+    const float *srcs[3] = {k, q, dout};
+    float *his[3] = {kth, qth, oth}, *los[3] = {ktl, qtl, otl};
+    for (int i = 0; i < 3; i++)
+        if ((st = check_pdl(launch_pdl(split_kt_kernel, tgrid, dim3(256), 0, s, srcs[i], his[i], los[i], in_stride, T,
+                                       H, D, Tp), "split and transpose")))
+            return st;
+    CUtensorMap mq, mo_, mkh, mkl, mvh, mvl, mb1, mb2, mds, mkth, mktl, mqth, mqtl, moth, motl, ydq, ydk, ydv;
+    bool okm = map_3d(&mq, q, (long long)H * D, T, B, in_stride, (long long)T * in_stride, BK, BM) &&
+               map_3d(&mo_, dout, (long long)H * D, T, B, in_stride, (long long)T * in_stride, BK, BM) &&
+               map_3d(&mkh, krh, D, T, BH, D, (long long)T * D, BK, BN) &&
+               map_3d(&mkl, krl, D, T, BH, D, (long long)T * D, BK, BN) &&
+               map_3d(&mvh, vrh, D, T, BH, D, (long long)T * D, BK, BN) &&
+               map_3d(&mvl, vrl, D, T, BH, D, (long long)T * D, BK, BN) &&
+               map_3d(&mkth, kth, T, D, BH, Tp, (long long)D * Tp, BK, BN) &&
+               map_3d(&mktl, ktl, T, D, BH, Tp, (long long)D * Tp, BK, BN) &&
+               map_3d(&mqth, qth, T, D, BH, Tp, (long long)D * Tp, BK, BN) &&
+               map_3d(&mqtl, qtl, T, D, BH, Tp, (long long)D * Tp, BK, BN) &&
+               map_3d(&moth, oth, T, D, BH, Tp, (long long)D * Tp, BK, BN) &&
+               map_3d(&motl, otl, T, D, BH, Tp, (long long)D * Tp, BK, BN) &&
+               map_3d(&ydq, dq, (long long)H * D, T, B, out_stride, (long long)T * out_stride, 32, 32) &&
+               map_3d(&ydk, dk, (long long)H * D, T, B, out_stride, (long long)T * out_stride, 32, 32) &&
+               map_3d(&ydv, dv, (long long)H * D, T, B, out_stride, (long long)T * out_stride, 32, 32);
+    // the [bh][T][T] buffers: read as GEMM A operands (128-row boxes), written as score tiles (32-row boxes)
+    CUtensorMap mb1s, mb2s;
+    okm = okm && map_3d(&mb1, buf1, T, T, BH, T, (long long)T * T, BK, BM) &&
+          map_3d(&mb2, buf2, T, T, BH, T, (long long)T * T, BK, BM) &&
+          map_3d(&mds, ds, T, T, BH, T, (long long)T * T, BK, BM) &&
+          map_3d(&mb1s, buf1, T, T, BH, T, (long long)T * T, 32, 32) &&
+          map_3d(&mb2s, buf2, T, T, BH, T, (long long)T * T, 32, 32);
+    if (!okm) return set_error(ATTN_ERR_CUDA, "tensor-core backward: cuTensorMapEncodeTiled failed");
+    if ((st = launch_gemm_mode(3, mq, mkh, mkl, mb1s, T, H, D, BH, err, s)) ||       // X = Q K^T
+        (st = launch_gemm_mode(3, mo_, mvh, mvl, mb2s, T, H, D, BH, err, s)))        // Y = dO V^T
+        return st;
+    const int mt = (T + BM - 1) / BM;
+    const size_t sg_smem = (size_t)2 * BM * kSgLd * sizeof(float);
+    if (!ensure_smem_attr((const void *)scores_to_grads_kernel, sg_smem))
+        return set_error(ATTN_ERR_CUDA, "tensor-core backward: cannot set shared-memory size");
+    if ((st = check_pdl(launch_pdl(scores_to_grads_kernel, dim3(mt * (mt + 1) / 2, (unsigned)BH), dim3(kSgThreads), sg_smem,
+                                   s, buf1, buf2, (const float *)stats, (const float *)(stats + BH * T), ds, T, mt,
+                                   qk_scale, ds_scale), "scores to P and dS")))
+        return st;
+    if ((st = launch_gemm_mode(1, mds, mkth, mktl, ydq, T, H, D, BH, err, s)) ||      // dQ = dS K
+        (st = launch_gemm_mode(2, mb1, moth, motl, ydv, T, H, D, BH, err, s)))        // dV = P^T dO
+        return st;
+    return launch_gemm_mode(2, mb2, mqth, mqtl, ydk, T, H, D, BH, err, s);            // dK = dS^T Q
 }
 
 }  // namespace attn_host

@@ -97,6 +97,44 @@ def test_backward_full_size_c5(A, dtype):
             assert rel_err(unit(dv, b, h0 + h, T, d), rv[:, cols]) < tol, (b, h0 + h)
 
 
+def test_drop_ins_at_trainer_shape(A):
+    """attn_fwd / attn_bwd at the reference GPU trainer's own shape (B4 H12
+    T1024 d128, gpu_kernels.h:17-31) with the trainer's buffer sizes, the
+    backward's products all on the tensor cores: every head of batch 1 against
+    the reference's own train.c attention (the restatement where the reference
+    objects are absent)."""
+    import ctypes
+    import torch
+    B, H, T, d = 4, 12, 1024, 128
+    A.check(A.lib.attn_set_macro_shape(B, H, T, d))
+    q, k, v = (gen((B * T, H * d), s, 0.5, torch.float32) for s in (21, 22, 23))
+    do = gen((B * T, H * d), 24, 1.0, torch.float32)
+    att = torch.empty_like(q)
+    probs = torch.empty(B * H * T * T, device="cuda")
+    scratch = torch.empty(B * H * T * T, device="cuda")
+    dq, dk, dv = (torch.empty_like(q) for _ in range(3))
+    torch.cuda.synchronize()
+    P = ctypes.c_void_p
+    A.lib.attn_fwd(P(q.data_ptr()), P(k.data_ptr()), P(v.data_ptr()), P(att.data_ptr()), P(probs.data_ptr()))
+    A.lib.attn_bwd(P(dq.data_ptr()), P(dk.data_ptr()), P(dv.data_ptr()), P(scratch.data_ptr()), P(do.data_ptr()),
+                   P(q.data_ptr()), P(k.data_ptr()), P(v.data_ptr()), P(probs.data_ptr()))
+    torch.cuda.synchronize()
+    b = 1
+    qu, ku, vu, gu = (slab(x, b, 0, H, T, d) for x in (q, k, v, do))
+    if O.ref_available():
+        ra, probs_r = O.ref_attention_forward(qu, ku, vu, 1, T, H, d)
+        rq, rk, rv = O.ref_attention_backward(gu, qu, ku, vu, probs_r, 1, T, H, d)
+    else:
+        ra, probs_r, _ = O.attn_forward(qu, ku, vu, 1, T, H, d, want_probs=True)
+        rq, rk, rv = O.attn_backward(gu, qu, ku, vu, probs_r, 1, T, H, d)
+    for h in range(H):
+        cols = slice(h * d, (h + 1) * d)
+        assert rel_err(unit(att, b, h, T, d), ra[:, cols]) < F32_TOL, h
+        assert rel_err(unit(dq, b, h, T, d), rq[:, cols]) < F32_TOL, h
+        assert rel_err(unit(dk, b, h, T, d), rk[:, cols]) < F32_TOL, h
+        assert rel_err(unit(dv, b, h, T, d), rv[:, cols]) < F32_TOL, h
+
+
 def test_c1_layer_decode_full_run(A):
     """16 layers x 128 steps at d_model 512 = 16 x 32, caches of 512 prior rows."""
     import ctypes
