@@ -93,11 +93,12 @@ ATTN_API void attn_fwd(const float *Q, const float *K, const float *V, float *at
  * cuBLAS path, beta = 0).  `scratch` is the caller's workspace (B*H*T*T
  * floats in train_kaggle.cu:138).  In the default ATTN_PROBS_LSE_OUT mode at
  * head_dim 96 and 128 with T a multiple of 4, this library fills all of it
- * with dS (as the reference's own softmax backward does) and computes dQ from
- * it on the tensor cores, keeping its row statistics and a split copy of K in
- * a library-owned device buffer (2*B*H*T*(1+d) floats; calls that use it must
- * not overlap on the GPU); otherwise it uses 2*B*H*T floats of `scratch`.
- * Exits(1) with a message on failure. */
+ * with dS (as the reference's own softmax backward does) and runs the
+ * backward as tensor-core GEMMs over explicit score tiles, keeping the scores,
+ * P^T, dS^T, the row statistics and split operands in a library-owned device
+ * buffer (2*B*H*T*(T+5d+1) floats, 654 MB at the trainer's shape; calls that
+ * use it must not overlap on the GPU); otherwise it uses 2*B*H*T floats of
+ * `scratch`.  Exits(1) with a message on failure. */
 ATTN_API void attn_bwd(float *dQ, float *dK, float *dV, float *scratch,
               const float *dAtt, const float *Q, const float *K, const float *V,
               const float *probs);
