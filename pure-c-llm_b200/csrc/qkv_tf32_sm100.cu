@@ -259,15 +259,19 @@ split_rows_kernel(const float *__restrict__ src, float *__restrict__ dh, float *
     }
 }
 
-// One 128 x 128 tile (query tile qt, key tile kt <= qt) of one (batch, head):
-// from the scores X = Q K^T (buf1) and Y = dO V^T (buf2), both [bh][T][T] with
-// rows i, keys j, forms P = 2^(X log2(e)/sqrt(d) - lse2_i) and
-// dS = P (Y - D_i) / sqrt(d) (0 for j > i, train.c:385-400 restated on the
-// saved row statistics), and writes dS (rows i) into `ds`, and P^T and dS^T
-// (rows j) into the tile (kt, qt) of buf1 and buf2 -- above the diagonal,
-// where no score tile lives; the diagonal tile is read whole before it is
-// overwritten.
-constexpr int kSgLd = 129;                         // padded row of the shared tiles (odd: conflict-free columns)
+// From the score tiles X = Q K^T (buf1) and Y = dO V^T (buf2), both [bh][T][T]
+// with rows i and keys j: P = 2^(X log2(e)/sqrt(d) - lse2_i) and
+// dS = P (Y - D_i) / sqrt(d), 0 for j > i (train.c:385-400 restated on the
+// saved row statistics).  dS (rows i) goes to `ds`; P^T and dS^T (rows j) to
+// the mirror tile (kt, qt) of buf1 and buf2 -- above the diagonal, where no
+// score tile lives.  A CTA takes the 64-key half h of an off-diagonal tile
+// (the halves read and write disjoint regions), or both halves of a diagonal
+// tile one after the other: there half 0's mirror writes land on rows 0-63,
+// which half 1 only has masked entries in, and half 1's on rows 64-127 after
+// half 0 has read them.  Units of a (batch, head): qt^2 + 2 kt + h for the
+// halves of tile (qt, kt < qt), qt^2 + 2 qt for the diagonal tile qt.
+constexpr int kSgCols = 64;                        // keys per half tile
+constexpr int kSgLd = kSgCols + 1;                 // padded shared row (odd: conflict-free columns)
 constexpr int kSgThreads = 512;
 __global__ void __launch_bounds__(kSgThreads)
 scores_to_grads_kernel(float *__restrict__ buf1, float *__restrict__ buf2, const float *__restrict__ lse2,
@@ -280,58 +284,64 @@ scores_to_grads_kernel(float *__restrict__ buf1, float *__restrict__ buf2, const
     __shared__ float rl[BM], rd[BM];
     const int bh = blockIdx.y;
     const int r = blockIdx.x;
-    int qt = (int)((sqrtf(8.f * (float)r + 1.f) - 1.f) * 0.5f);
-    while (qt * (qt + 1) / 2 > r) qt--;
-    while ((qt + 1) * (qt + 2) / 2 <= r) qt++;
-    const int kt = r - qt * (qt + 1) / 2;
-    const int i0 = qt * BM, j0 = kt * BN;
+    int qt = (int)sqrtf((float)r);
+    while (qt * qt > r) qt--;
+    while ((qt + 1) * (qt + 1) <= r) qt++;
+    const int rem = r - qt * qt;
+    const bool diag = rem == 2 * qt;
+    const int kt = diag ? qt : rem >> 1;
+    const int i0 = qt * BM;
     const long long base = (long long)bh * T * T;
     if (threadIdx.x < BM) {
         const int i = i0 + threadIdx.x;
         rl[threadIdx.x] = i < T ? lse2[(long long)bh * T + i] : 0.f;
         rd[threadIdx.x] = i < T ? dvec[(long long)bh * T + i] : 0.f;
     }
-    // rows of 128 floats as 32 float4 (T % 4 == 0, so a float4 is all in or all out)
-    for (int idx = threadIdx.x; idx < BM * (BN / 4); idx += kSgThreads) {
-        const int a = idx >> 5, c = (idx & 31) * 4, i = i0 + a, j = j0 + c;
-        float4 x = make_float4(0.f, 0.f, 0.f, 0.f), y = x;
-        if (i < T && j < T) {
-            x = *reinterpret_cast<const float4 *>(buf1 + base + (long long)i * T + j);
-            y = *reinterpret_cast<const float4 *>(buf2 + base + (long long)i * T + j);
+    for (int hh = diag ? 0 : (rem & 1); hh < (diag ? 2 : (rem & 1) + 1); hh++) {
+        const int j0 = kt * BN + hh * kSgCols;
+        __syncthreads();                               // (the previous half's shared tiles are free)
+        // 128 rows x 64 keys as 16 float4 per row (T % 4 == 0: a float4 is all in or all out)
+        for (int idx = threadIdx.x; idx < BM * (kSgCols / 4); idx += kSgThreads) {
+            const int a = idx >> 4, c = (idx & 15) * 4, i = i0 + a, j = j0 + c;
+            float4 x = make_float4(0.f, 0.f, 0.f, 0.f), y = x;
+            if (i < T && j < T && j <= i + 3) {        // (a float4 wholly above the diagonal is not read)
+                x = *reinterpret_cast<const float4 *>(buf1 + base + (long long)i * T + j);
+                y = *reinterpret_cast<const float4 *>(buf2 + base + (long long)i * T + j);
+            }
+            float *px = sx + a * kSgLd + c, *py = sy + a * kSgLd + c;
+            px[0] = x.x; px[1] = x.y; px[2] = x.z; px[3] = x.w;
+            py[0] = y.x; py[1] = y.y; py[2] = y.z; py[3] = y.w;
         }
-        float *px = sx + a * kSgLd + c, *py = sy + a * kSgLd + c;
-        px[0] = x.x; px[1] = x.y; px[2] = x.z; px[3] = x.w;
-        py[0] = y.x; py[1] = y.y; py[2] = y.z; py[3] = y.w;
-    }
-    __syncthreads();
-    for (int idx = threadIdx.x; idx < BM * BN; idx += kSgThreads) {
-        const int a = idx >> 7, c = idx & 127, i = i0 + a, j = j0 + c;
-        float pv = 0.f, dv = 0.f;
-        if (i < T && j < T && j <= i) {
-            pv = exp2f(sx[a * kSgLd + c] * qk_scale - rl[a]);
-            dv = pv * (sy[a * kSgLd + c] - rd[a]) * ds_scale;
+        __syncthreads();
+        for (int idx = threadIdx.x; idx < BM * kSgCols; idx += kSgThreads) {
+            const int a = idx >> 6, c = idx & 63, i = i0 + a, j = j0 + c;
+            float pv = 0.f, dv = 0.f;
+            if (i < T && j < T && j <= i) {
+                pv = exp2f(sx[a * kSgLd + c] * qk_scale - rl[a]);
+                dv = pv * (sy[a * kSgLd + c] - rd[a]) * ds_scale;
+            }
+            sx[a * kSgLd + c] = pv;
+            sy[a * kSgLd + c] = dv;
         }
-        sx[a * kSgLd + c] = pv;
-        sy[a * kSgLd + c] = dv;
-    }
-    __syncthreads();
-    for (int idx = threadIdx.x; idx < BM * (BN / 4); idx += kSgThreads) {
-        const int a = idx >> 5, c = (idx & 31) * 4;          // dS, rows i
-        const int i = i0 + a, j = j0 + c;
-        if (i < T && j < T) {
-            const float *py = sy + a * kSgLd + c;
-            *reinterpret_cast<float4 *>(ds + base + (long long)i * T + j) = make_float4(py[0], py[1], py[2], py[3]);
+        __syncthreads();
+        for (int idx = threadIdx.x; idx < BM * (kSgCols / 4); idx += kSgThreads) {
+            const int a = idx >> 4, c = (idx & 15) * 4;   // dS, rows i
+            const int i = i0 + a, j = j0 + c;
+            if (i < T && j < T) {
+                const float *py = sy + a * kSgLd + c;
+                *reinterpret_cast<float4 *>(ds + base + (long long)i * T + j) = make_float4(py[0], py[1], py[2], py[3]);
+            }
         }
-    }
-    for (int idx = threadIdx.x; idx < BN * (BM / 4); idx += kSgThreads) {
-        const int c = idx >> 5, a = (idx & 31) * 4;          // P^T and dS^T, rows j: column c of the tiles
-        const int i = i0 + a, j = j0 + c;
-        if (i < T && j < T) {
-            const float *px = sx + a * kSgLd + c, *py = sy + a * kSgLd + c;
-            *reinterpret_cast<float4 *>(buf1 + base + (long long)j * T + i) =
-                make_float4(px[0], px[kSgLd], px[2 * kSgLd], px[3 * kSgLd]);
-            *reinterpret_cast<float4 *>(buf2 + base + (long long)j * T + i) =
-                make_float4(py[0], py[kSgLd], py[2 * kSgLd], py[3 * kSgLd]);
+        for (int idx = threadIdx.x; idx < kSgCols * (BM / 4); idx += kSgThreads) {
+            const int c = idx >> 5, a = (idx & 31) * 4;   // P^T and dS^T, rows j: column c of the tiles
+            const int i = i0 + a, j = j0 + c;
+            if (i < T && j < T) {
+                const float *px = sx + a * kSgLd + c, *py = sy + a * kSgLd + c;
+                *reinterpret_cast<float4 *>(buf1 + base + (long long)j * T + i) =
+                    make_float4(px[0], px[kSgLd], px[2 * kSgLd], px[3 * kSgLd]);
+                *reinterpret_cast<float4 *>(buf2 + base + (long long)j * T + i) =
+                    make_float4(py[0], py[kSgLd], py[2 * kSgLd], py[3 * kSgLd]);
+            }
         }
     }
 }
@@ -852,10 +862,10 @@ int launch_bwd_tc(int D, const float *dout, const float *q, const float *k, cons
         (st = launch_gemm_mode(3, mo_, mvh, mvl, mb2s, T, H, D, BH, err, s)))        // Y = dO V^T
         return st;
     const int mt = (T + BM - 1) / BM;
-    const size_t sg_smem = (size_t)2 * BM * kSgLd * sizeof(float);
+    const size_t sg_smem = (size_t)2 * BM * kSgLd * sizeof(float);     // 65 KB: three CTAs per SM
     if (!ensure_smem_attr((const void *)scores_to_grads_kernel, sg_smem))
         return set_error(ATTN_ERR_CUDA, "tensor-core backward: cannot set shared-memory size");
-    if ((st = check_pdl(launch_pdl(scores_to_grads_kernel, dim3(mt * (mt + 1) / 2, (unsigned)BH), dim3(kSgThreads), sg_smem,
+    if ((st = check_pdl(launch_pdl(scores_to_grads_kernel, dim3(mt * mt, (unsigned)BH), dim3(kSgThreads), sg_smem,
                                    s, buf1, buf2, (const float *)stats, (const float *)(stats + BH * T), ds, T, mt,
                                    qk_scale, ds_scale), "scores to P and dS")))
         return st;
