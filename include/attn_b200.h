@@ -97,7 +97,8 @@ ATTN_API void attn_fwd(const float *Q, const float *K, const float *V, float *at
  * backward as tensor-core GEMMs over explicit score tiles, keeping the scores,
  * P^T, dS^T, the row statistics and split operands in a library-owned device
  * buffer (2*B*H*T*(T+5d+1) floats, 654 MB at the trainer's shape; calls that
- * use it must not overlap on the GPU); otherwise it uses 2*B*H*T floats of
+ * use it must not overlap on the GPU); otherwise, or when that buffer cannot
+ * be allocated, it runs the CUDA-core kernels and uses 2*B*H*T floats of
  * `scratch`.  Exits(1) with a message on failure. */
 ATTN_API void attn_bwd(float *dQ, float *dK, float *dV, float *scratch,
               const float *dAtt, const float *Q, const float *K, const float *V,
