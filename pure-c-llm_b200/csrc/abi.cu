@@ -44,7 +44,10 @@ int launch_fwd_bf16_sm100(int D, const void *q, const void *k, const void *v, vo
 bool fwd_bf16_sm100_supported(int D, long long in_stride, long long out_stride);
 int launch_fwd_tf32_sm100(int D, const void *q, const void *k, const void *v, void *o, float *lse,
                           long long in_stride, long long out_stride, int B, int H, int T, int *err,
-                          cudaStream_t s);
+                          cudaStream_t s, int parts);
+int launch_fwd_bf16_via_tf32(int D, const void *q, const void *k, const void *v, void *o, float *lse,
+                             long long in_stride, long long out_stride, int B, int H, int T, int *err,
+                             cudaStream_t s);
 bool fwd_tf32_sm100_supported(int D, long long in_stride, long long out_stride);
 int launch_bwd_f32(int dtype, int D, const void *dout, const void *q, const void *k,
                    const void *v, const void *o, const float *lse, void *dq, void *dk, void *dv,
@@ -269,7 +272,15 @@ int attn_fwd_ex(const attn_shape *s, int dtype, const void *Q, const void *K, co
                                      s->heads, s->seq_len, device_error_ptr(), cs);
     if (dtype == ATTN_F32 && fwd_tf32_sm100_supported(s->head_dim, in_st, out_st))
         return launch_fwd_tf32_sm100(s->head_dim, Q, K, V, O, lse, in_st, out_st, s->batch,
-                                     s->heads, s->seq_len, device_error_ptr(), cs);
+                                     s->heads, s->seq_len, device_error_ptr(), cs, 3);
+    // bf16 at the other head dims: the tf32 kernel over exact fp32 copies, one product per product
+    if (dtype == ATTN_BF16 && fwd_tf32_sm100_supported(s->head_dim, s->heads * (long long)s->head_dim,
+                                                       s->heads * (long long)s->head_dim) &&
+        in_st % 4 == 0 && out_st % 4 == 0) {
+        const int st = launch_fwd_bf16_via_tf32(s->head_dim, Q, K, V, O, lse, in_st, out_st, s->batch, s->heads,
+                                                s->seq_len, device_error_ptr(), cs);
+        if (st != ATTN_ERR_NOMEM) return st;
+    }
     return launch_fwd_f32(dtype, s->head_dim, Q, K, V, O, lse, in_st, out_st, s->batch, s->heads,
                           s->seq_len, cs);
 }

@@ -200,7 +200,10 @@ __device__ __forceinline__ float f4_at(const float4 &v, int c) {
     return c == 0 ? v.x : c == 1 ? v.y : c == 2 ? v.z : v.w;
 }
 
-template <int D>
+// PARTS = 3: every product formed as xh yh + xh yl + xl yh; PARTS = 1: xh yh
+// alone, for fp32 copies of bf16 inputs (exact in tf32, so their low parts are
+// zero; P's low part is dropped, ~2^-11, far inside the bf16 tolerance).
+template <int D, int PARTS = 3>
 __global__ void __launch_bounds__(kThreads, Cfg<D>::CTAS)
 fwd_tf32_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                 const __grid_constant__ CUtensorMap tv, const __grid_constant__ Params p)
@@ -326,6 +329,7 @@ fwd_tf32_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
                         // K-step kk: chunk kk/4 (128-byte columns), +32 bytes within it
 #pragma unroll
                         for (int part = 0; part < 3; part++) {       // hh, hl, lh
+                            if (part >= PARTS) break;
                             const uint32_t qa = base + (part == 2 ? C::OFF_QL : C::OFF_QH);
                             const uint32_t qt = tmem + (part == 2 ? C::TM_QL : C::TM_QH);
                             const uint32_t kb = part == 1 ? kl : kh;
@@ -368,6 +372,7 @@ fwd_tf32_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
                         // bytes apart), +32 bytes per 8-key step within it
 #pragma unroll
                         for (int part = 0; part < 3; part++) {       // hh, hl, lh
+                            if (part >= PARTS) break;
                             const uint32_t pa = part == 2 ? pl : ph;
                             const uint32_t vb = part == 1 ? vl : vh;
 #pragma unroll
@@ -774,7 +779,9 @@ static void lpt_schedule_tf32(const attn::ftf::Params &p, int ctas, std::vector<
 
 template <int D>
 static int launch_tf32_t(const void *q, const void *k, const void *v, void *o, float *lse, long long in_stride,
-                         long long out_stride, int B, int H, int T, int *err, cudaStream_t s) {
+                         long long out_stride, int B, int H, int T, int *err, cudaStream_t s, int parts) {
+    void (*kern)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const attn::ftf::Params) =
+        parts == 1 ? attn::ftf::fwd_tf32_kernel<D, 1> : attn::ftf::fwd_tf32_kernel<D, 3>;
     using namespace attn::ftf;
     using Cg = Cfg<D>;
     CUtensorMap mq, mk, mv;
@@ -805,26 +812,93 @@ static int launch_tf32_t(const void *q, const void *k, const void *v, void *o, f
         p.use_list = p.sched != nullptr;            // a full cache: the list-free static schedule
     }
     const size_t smem = Cg::SMEM;
-    if (!ensure_smem_attr((const void *)fwd_tf32_kernel<D>, smem))
+    if (!ensure_smem_attr((const void *)kern, smem))
         return set_error(ATTN_ERR_CUDA, "3xTF32 forward: cannot set shared-memory size");
-    if (!ensure_carveout((const void *)fwd_tf32_kernel<D>, 100))
+    if (!ensure_carveout((const void *)kern, 100))
         return set_error(ATTN_ERR_CUDA, "3xTF32 forward: cannot set the shared-memory carveout");
-    return check_pdl(launch_pdl(fwd_tf32_kernel<D>, dim3(ctas), dim3(kThreads), smem, s, mq, mk, mv, p),
+    return check_pdl(launch_pdl(kern, dim3(ctas), dim3(kThreads), smem, s, mq, mk, mv, p),
                      "3xTF32 forward kernel");
 }
 
+// parts = 3 for fp32 inputs; 1 for fp32 copies of bf16 inputs (see Params::parts).
 int launch_fwd_tf32_sm100(int D, const void *q, const void *k, const void *v, void *o, float *lse,
                           long long in_stride, long long out_stride, int B, int H, int T, int *err,
-                          cudaStream_t s) {
+                          cudaStream_t s, int parts) {
     if (((uintptr_t)q | (uintptr_t)k | (uintptr_t)v | (uintptr_t)o) & 15)
         return set_error(ATTN_ERR_INVALID, "3xTF32 forward: tensors must be 16-byte aligned");
     switch (D) {
-        case 32: return launch_tf32_t<32>(q, k, v, o, lse, in_stride, out_stride, B, H, T, err, s);
-        case 64: return launch_tf32_t<64>(q, k, v, o, lse, in_stride, out_stride, B, H, T, err, s);
-        case 96: return launch_tf32_t<96>(q, k, v, o, lse, in_stride, out_stride, B, H, T, err, s);
-        case 128: return launch_tf32_t<128>(q, k, v, o, lse, in_stride, out_stride, B, H, T, err, s);
+        case 32: return launch_tf32_t<32>(q, k, v, o, lse, in_stride, out_stride, B, H, T, err, s, parts);
+        case 64: return launch_tf32_t<64>(q, k, v, o, lse, in_stride, out_stride, B, H, T, err, s, parts);
+        case 96: return launch_tf32_t<96>(q, k, v, o, lse, in_stride, out_stride, B, H, T, err, s, parts);
+        case 128: return launch_tf32_t<128>(q, k, v, o, lse, in_stride, out_stride, B, H, T, err, s, parts);
         default: return set_error(ATTN_ERR_UNSUPPORTED, "3xTF32 forward: head_dim %d", D);
     }
+}
+
+// bf16 <-> fp32 copies of (rows x cols) activations with row strides (elements);
+// cols % 4 == 0, 8-byte aligned bf16 rows and 16-byte aligned fp32 rows.
+__global__ void __launch_bounds__(256)
+bf16_to_f32_kernel(const __nv_bfloat16 *__restrict__ src, long long sst, float *__restrict__ dst, long long dstr,
+                   long long rows, int cols)
+{
+    attn::pdl_begin();   // launched by launch_pdl
+    const int c4 = cols / 4;
+    for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < rows * c4;
+         e += (long long)gridDim.x * blockDim.x) {
+        const long long r = e / c4;
+        const int c = (int)(e % c4) * 4;
+        *reinterpret_cast<float4 *>(dst + r * dstr + c) = attn::load4(src + r * sst + c);
+    }
+}
+__global__ void __launch_bounds__(256)
+f32_to_bf16_kernel(const float *__restrict__ src, long long sst, __nv_bfloat16 *__restrict__ dst, long long dstr,
+                   long long rows, int cols)
+{
+    attn::pdl_begin();   // launched by launch_pdl
+    const int c4 = cols / 4;
+    for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < rows * c4;
+         e += (long long)gridDim.x * blockDim.x) {
+        const long long r = e / c4;
+        const int c = (int)(e % c4) * 4;
+        attn::store4(dst + r * dstr + c, *reinterpret_cast<const float4 *>(src + r * sst + c));
+    }
+}
+
+void *library_workspace(int which, size_t bytes, cudaStream_t s);
+
+// bf16 causal forward at head dims without a bf16 tensor-core kernel (32, 96,
+// 128): Q, K, V are widened to fp32 (exactly: bf16 is a subset of tf32), the
+// tf32 forward runs with one product per product (xh yh; the low parts are
+// zero), and O is rounded back to bf16.  The fp32 copies (4 * B*T*H*d floats)
+// live in a library-owned buffer; calls that use it must not overlap on the
+// GPU.  Returns ATTN_ERR_NOMEM when that buffer cannot be had (the caller then
+// takes the CUDA-core kernel).
+int launch_fwd_bf16_via_tf32(int D, const void *q, const void *k, const void *v, void *o, float *lse,
+                             long long in_stride, long long out_stride, int B, int H, int T, int *err,
+                             cudaStream_t s) {
+    const long long rows = (long long)B * T, hd = (long long)H * D;
+    const size_t one = ((size_t)rows * hd * 4 + 255) / 256 * 256;
+    char *ws = static_cast<char *>(library_workspace(3, 4 * one, s));
+    if (!ws) {
+        (void)cudaGetLastError();
+        return set_error(ATTN_ERR_NOMEM, "bf16 forward: no room for the fp32 copies");
+    }
+    float *qf = reinterpret_cast<float *>(ws), *kf = reinterpret_cast<float *>(ws + one);
+    float *vf = reinterpret_cast<float *>(ws + 2 * one), *of = reinterpret_cast<float *>(ws + 3 * one);
+    const long long n4 = rows * (hd / 4);
+    const int grid = (int)std::min<long long>((n4 + 255) / 256, 8LL * sm_count_here());
+    const void *src[3] = {q, k, v};
+    float *dst[3] = {qf, kf, vf};
+    int st;
+    for (int i = 0; i < 3; i++)
+        if ((st = check_pdl(launch_pdl(bf16_to_f32_kernel, dim3(grid), dim3(256), 0, s,
+                                       static_cast<const __nv_bfloat16 *>(src[i]), in_stride, dst[i], hd, rows, (int)hd),
+                            "bf16 forward: widening")))
+            return st;
+    if ((st = launch_fwd_tf32_sm100(D, qf, kf, vf, of, lse, hd, hd, B, H, T, err, s, 1))) return st;
+    return check_pdl(launch_pdl(f32_to_bf16_kernel, dim3(grid), dim3(256), 0, s, (const float *)of, hd,
+                                static_cast<__nv_bfloat16 *>(o), out_stride, rows, (int)hd),
+                     "bf16 forward: rounding the output");
 }
 
 }  // namespace attn_host

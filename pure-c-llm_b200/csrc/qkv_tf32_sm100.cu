@@ -643,7 +643,8 @@ static size_t qkv_ws_bytes(const attn_qkv_shape *s) { return 2 * qkv_ws_half(s);
 
 // Library-owned workspaces, one per (device, slot), grown on demand; calls that
 // use one must not overlap on the GPU.  Slot 0: the QKV projection's split
-// weights; slot 1: the drop-in backward's row statistics and split K.
+// weights; slot 1: the drop-in backward's score buffers, splits and row
+// statistics; slot 3: fp32 copies for the bf16 forward at d 32/96/128.
 void *library_workspace(int which, size_t bytes, cudaStream_t s) {
     static std::mutex mu;
     static std::map<std::pair<int, int>, std::pair<void *, size_t>> pool;
