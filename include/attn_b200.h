@@ -91,15 +91,17 @@ ATTN_API void attn_fwd(const float *Q, const float *K, const float *V, float *at
 
 /* Replaces gpu_kernels.h:70 attn_bwd.  SETS dQ, dK, dV (like the reference's
  * cuBLAS path, beta = 0).  `scratch` is the caller's workspace (B*H*T*T
- * floats in train_kaggle.cu:138).  In the default ATTN_PROBS_LSE_OUT mode at
- * head_dim 96 and 128 with T a multiple of 4, this library fills all of it
- * with dS (as the reference's own softmax backward does) and runs the
- * backward as tensor-core GEMMs over explicit score tiles, keeping the scores,
- * P^T, dS^T, the row statistics and split operands in a library-owned device
- * buffer (2*B*H*T*(T+5d+1) floats, 654 MB at the trainer's shape; calls that
- * use it must not overlap on the GPU); otherwise, or when that buffer cannot
- * be allocated, it runs the CUDA-core kernels and uses 2*B*H*T floats of
- * `scratch`.  Exits(1) with a message on failure. */
+ * floats in train_kaggle.cu:138).  At head_dim 96 and 128 with T a multiple
+ * of 4 the backward runs as tensor-core GEMMs over explicit score tiles: in
+ * the default ATTN_PROBS_LSE_OUT mode this library fills all of `scratch`
+ * with dS (as the reference's own softmax backward does) and keeps the
+ * scores, P^T, dS^T, the row statistics and split operands in a library-owned
+ * device buffer (2*B*H*T*(T+5d+1) floats, 654 MB at the trainer's shape); in
+ * ATTN_PROBS_LSE mode dS goes to that buffer as well (B*H*T*T floats more,
+ * one buffer for every layer).  Calls that use the buffer must not overlap on
+ * the GPU.  Otherwise, or when the buffer cannot be allocated, it runs the
+ * CUDA-core kernels and uses 2*B*H*T floats of `scratch`.  Exits(1) with a
+ * message on failure. */
 ATTN_API void attn_bwd(float *dQ, float *dK, float *dV, float *scratch,
               const float *dAtt, const float *Q, const float *K, const float *V,
               const float *probs);

@@ -420,17 +420,23 @@ void dropin_bwd(float *dQ, float *dK, float *dV, float *scratch, const float *dA
     // dS), so the backward runs as tensor-core GEMMs over explicit score
     // tiles: dS goes to scratch, the scores, P^T, dS^T, the row statistics and
     // the split operands to a library-owned buffer.
-    if (g_probs_mode == ATTN_PROBS_LSE_OUT && (s.head_dim == 96 || s.head_dim == 128) && s.seq_len % 4 == 0 &&
+    // In ATTN_PROBS_LSE mode the trainer's scratch is shrunk to 2*B*H*T floats,
+    // so dS goes to the library-owned buffer too (one B*H*T*T buffer for all
+    // layers, where the reference keeps one per layer).
+    const bool lse_mode = g_probs_mode == ATTN_PROBS_LSE;
+    if ((s.head_dim == 96 || s.head_dim == 128) && s.seq_len % 4 == 0 &&
         (long long)s.batch * s.heads <= 65535 &&
         ((reinterpret_cast<uintptr_t>(scratch) | reinterpret_cast<uintptr_t>(dQ) | reinterpret_cast<uintptr_t>(dK) |
           reinterpret_cast<uintptr_t>(dV) | reinterpret_cast<uintptr_t>(Q) | reinterpret_cast<uintptr_t>(K) |
           reinterpret_cast<uintptr_t>(V) | reinterpret_cast<uintptr_t>(dAtt) | reinterpret_cast<uintptr_t>(out)) &
          15) == 0) {
         const long long hd = (long long)s.heads * s.head_dim;
-        const size_t need = bwd_tc_ws_bytes(s.batch, s.heads, s.seq_len, s.head_dim);
-        if (void *ws = library_workspace(1, need, nullptr)) {
+        const size_t tc = bwd_tc_ws_bytes(s.batch, s.heads, s.seq_len, s.head_dim);
+        const size_t ds_bytes = lse_mode ? (size_t)s.batch * s.heads * s.seq_len * s.seq_len * sizeof(float) : 0;
+        if (void *ws = library_workspace(1, tc + ds_bytes, nullptr)) {
+            float *ds = lse_mode ? reinterpret_cast<float *>(static_cast<char *>(ws) + tc) : scratch;
             die_on(launch_bwd_tc(s.head_dim, static_cast<const float *>(dAtt), Q, K, V, static_cast<const float *>(out),
-                                 lse, dQ, dK, dV, scratch, ws, hd, hd, s.batch, s.heads, s.seq_len, device_error_ptr(),
+                                 lse, dQ, dK, dV, ds, ws, hd, hd, s.batch, s.heads, s.seq_len, device_error_ptr(),
                                  nullptr),
                    "attn_bwd");
             return;
