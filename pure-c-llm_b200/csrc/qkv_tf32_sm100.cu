@@ -1,6 +1,9 @@
-// qkv_tf32_sm100.cu -- the fused QKV projection: a layer's Q, K and V from its
-// layer-normed input in ONE launch on the Blackwell tensor cores (sm_100a),
-// fp32 in and out with 3xTF32 products.
+// qkv_tf32_sm100.cu -- fp32 GEMMs on the Blackwell tensor cores (sm_100a) with
+// 3xTF32 products: the fused QKV projection (a layer's Q, K and V from its
+// layer-normed input in ONE launch), and -- the same kernel in three more
+// modes (see Params) -- the causal attention backward at head dims 96 and 128
+// as GEMMs over explicit score tiles (launch_bwd_tc, the attn_bwd drop-in's
+// path; attention_backward, train.c:373-407).
 //
 // Semantics: the three gemm_nn calls of train_kaggle.cu:152-154,
 //     Q = X Wq + bq,   K = X Wk + bk,   V = X Wv + bv
@@ -33,13 +36,13 @@
 //   warps 2-3   idle
 //   warps 4-7   splitters: X's high and low parts into the stage's TMEM slot (a
 //               warp per 32 rows, its TMEM lane quadrant)
+//   warps 8-11  epilogue: a thread owns one output row (one TMEM lane), adds
+//               each partial sum into 128 fp32 registers, adds the bias and
+//               writes the tile through shared memory with TMA stores
 // Shared memory's 128 bytes per clock bound this kernel: with both operands
 // in shared memory and both split there, a 32-k stage moved 224 KB through it
 // against ~770 cycles of tensor work.  Now a stage moves 112 KB: TMA's 48 KB,
 // the splitters' 16 KB read of X, and the MMAs' 48 KB read of W's parts.
-//   warps 8-11  epilogue: a thread owns one output row (one TMEM lane), adds
-//               each partial sum into 128 fp32 registers, adds the bias and
-//               writes the tile through shared memory with TMA stores
 // Every mbarrier wait is bounded; a timeout records a code in the device
 // error word, raises a CTA-wide abort flag, and all roles fall through to the
 // teardown, which frees TMEM.
