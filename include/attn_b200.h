@@ -152,6 +152,15 @@ ATTN_API int attn_fwd_ex(const attn_shape *s, int dtype,
 /* Bytes of device workspace attn_bwd_ex needs for this shape. */
 ATTN_API size_t attn_bwd_workspace_bytes(const attn_shape *s, int dtype);
 
+/* Bytes of workspace that let attn_bwd_ex run an fp32 backward at head_dim 96
+ * or 128 (T a multiple of 4, accumulate = 0) on the tensor cores, as GEMMs
+ * over explicit score tiles: 2*B*H*T*(T+5d+1) + B*H*T*T floats (the scores,
+ * P^T, dS^T, dS, split operands and row statistics; 855 MB at B4 H12 T1024
+ * d128), rounded to 256-byte pieces.  0 for shapes without that path.  A
+ * smaller workspace (at least attn_bwd_workspace_bytes) selects the CUDA-core
+ * kernels. */
+ATTN_API size_t attn_bwd_tc_workspace_bytes(const attn_shape *s);
+
 /* Analytic backward (train.c:373-407): dQ, dK, dV from dO, the forward's
  * inputs, its output O and its lse.  accumulate = 1 adds into dQ/dK/dV as
  * train.c does; 0 overwrites them as gpu_kernels.cu's attn_bwd does. */

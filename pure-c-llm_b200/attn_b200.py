@@ -77,6 +77,7 @@ SIGNATURES = {
     "attn_fwd_ex": (I, [ctypes.POINTER(Shape), I, P, P, P, P, P, P]),
     "attn_bwd_workspace_bytes": (SZ, [ctypes.POINTER(Shape), I]),
     "attn_bwd_ex": (I, [ctypes.POINTER(Shape), I, P, P, P, P, P, P, P, P, P, I, P, SZ, P]),
+    "attn_bwd_tc_workspace_bytes": (SZ, [ctypes.POINTER(Shape)]),
     "attn_qkv_workspace_bytes": (SZ, [ctypes.POINTER(QKVShape)]),
     "attn_qkv_proj_ex": (I, [ctypes.POINTER(QKVShape), P, P, P, P, P, P, P, P, P, P, P, SZ, P]),
     "attn_qkv_proj": (None, [P, P, P, P, P, P, P, P, P, P, I, I, I]),

@@ -291,6 +291,14 @@ size_t attn_bwd_workspace_bytes(const attn_shape *s, int dtype) {
     return bwd_f32_workspace_bytes(s->batch, s->heads, s->seq_len);
 }
 
+size_t attn_bwd_tc_workspace_bytes(const attn_shape *s) {
+    if (!s || (s->head_dim != 96 && s->head_dim != 128) || s->batch < 1 || s->heads < 1 || s->seq_len < 1 ||
+        s->seq_len % 4 || (long long)s->batch * s->heads > 65535)
+        return 0;
+    return bwd_tc_ws_bytes(s->batch, s->heads, s->seq_len, s->head_dim) +
+           ((size_t)s->batch * s->heads * s->seq_len * s->seq_len * sizeof(float) + 255) / 256 * 256;
+}
+
 int attn_bwd_ex(const attn_shape *s, int dtype, const void *dO, const void *Q, const void *K,
                 const void *V, const void *O, const float *lse, void *dQ, void *dK, void *dV,
                 int accumulate, void *workspace, size_t workspace_bytes, attn_stream_t stream) {
@@ -316,6 +324,18 @@ int attn_bwd_ex(const attn_shape *s, int dtype, const void *dO, const void *Q, c
         return launch_bwd_tf32_sm100(s->head_dim, dO, Q, K, V, O, lse, dQ, dK, dV, accumulate ? 1 : 0, workspace,
                                      in_st, out_st, s->batch, s->heads, s->seq_len, device_error_ptr(),
                                      reinterpret_cast<cudaStream_t>(stream));
+    // d 96 / 128 with the larger workspace: the tensor-core GEMMs over score tiles
+    const size_t tc_need = attn_bwd_tc_workspace_bytes(s);
+    if (dtype == ATTN_F32 && !accumulate && tc_need && workspace_bytes >= tc_need && aligned(workspace, 256) &&
+        in_st % 4 == 0 && out_st % 4 == 0) {
+        const size_t tc = bwd_tc_ws_bytes(s->batch, s->heads, s->seq_len, s->head_dim);
+        return launch_bwd_tc(s->head_dim, static_cast<const float *>(dO), static_cast<const float *>(Q),
+                             static_cast<const float *>(K), static_cast<const float *>(V),
+                             static_cast<const float *>(O), lse, static_cast<float *>(dQ), static_cast<float *>(dK),
+                             static_cast<float *>(dV), reinterpret_cast<float *>(static_cast<char *>(workspace) + tc),
+                             workspace, in_st, out_st, s->batch, s->heads, s->seq_len, device_error_ptr(),
+                             reinterpret_cast<cudaStream_t>(stream));
+    }
     return launch_bwd_f32(dtype, s->head_dim, dO, Q, K, V, O, lse, dQ, dK, dV, accumulate ? 1 : 0,
                           workspace, in_st, out_st, s->batch, s->heads, s->seq_len,
                           reinterpret_cast<cudaStream_t>(stream));

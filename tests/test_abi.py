@@ -148,3 +148,13 @@ def test_qkv_workspace_size_and_check():
     st = A.lib.attn_qkv_proj_ex(ctypes.byref(shape), P16, P16, P16, P16, None, None, None, P16, P16, P16,
                                 P16, 1024, None)   # a caller workspace that is too small
     assert st == A.ERR_WORKSPACE
+
+
+def test_bwd_tc_workspace_size():
+    """The optional workspace for the tensor-core backward at d 96 / 128."""
+    tr = A.Shape(4, 12, 1024, 128, 0, 0)
+    big = A.lib.attn_bwd_tc_workspace_bytes(ctypes.byref(tr))
+    floats = 2 * 48 * 1024 * (1024 + 5 * 128 + 1) + 48 * 1024 * 1024
+    assert floats * 4 <= big < floats * 4 + 16 * 256
+    for shape in (A.Shape(4, 12, 1024, 64, 0, 0), A.Shape(1, 2, 130, 128, 0, 0), A.Shape(1, 2, 128, 32, 0, 0)):
+        assert A.lib.attn_bwd_tc_workspace_bytes(ctypes.byref(shape)) == 0     # d 64 / 32, or T % 4 != 0

@@ -334,6 +334,45 @@ def test_drop_in_bwd_on_tensor_cores(A, B, H, T, d):
         A.lib.attn_set_macro_shape(4, 12, 1024, 128)
 
 
+@pytest.mark.parametrize("B,H,T,d", [(2, 2, 260, 128), (1, 3, 128, 96)])
+def test_backward_ex_tensor_core_workspace(A, B, H, T, d):
+    """attn_bwd_ex at d 96 / 128 with a workspace of attn_bwd_tc_workspace_bytes:
+    the tensor-core GEMMs over score tiles, against the oracle and against the
+    CUDA-core kernels that the minimum workspace selects; accumulate = 1 keeps
+    the CUDA-core kernels (the GEMMs set their outputs)."""
+    import torch
+    q, k, v = qkv(13 * T + d, B, T, H, d)
+    do = synth.normal(14 * T + d, q.shape)
+    _, probs, _ = O.attn_forward(q, k, v, B, T, H, d, want_probs=True)
+    rq, rk, rv = O.attn_backward(do, q, k, v, probs, B, T, H, d)
+    qd, kd, vd, gd = dev(q), dev(k), dev(v), dev(do)
+    o, lse = A.forward_t(qd, kd, vd, H, B)
+    shape = A.Shape(B, H, T, d, 0, 0)
+    big = A.lib.attn_bwd_tc_workspace_bytes(ctypes.byref(shape))
+    small = A.bwd_workspace_bytes(shape, A.F32)
+    assert big > small
+    outs = {}
+    for name, nbytes in (("tc", big), ("ffma", small)):
+        ws = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+        r = [torch.full_like(qd, 7.0) for _ in range(3)]
+        A.bwd_ex(shape, A.F32, gd.data_ptr(), qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), o.data_ptr(),
+                 lse.data_ptr(), r[0].data_ptr(), r[1].data_ptr(), r[2].data_ptr(), 0, ws.data_ptr(), nbytes, 0)
+        torch.cuda.synchronize()
+        outs[name] = [host(t) for t in r]
+        for got, want in zip(outs[name], (rq, rk, rv)):
+            assert rel_err(got, want) < F32_TOL, name
+    for a, b in zip(outs["tc"], outs["ffma"]):
+        assert rel_err(a, b) < F32_TOL
+    # accumulate = 1 with the large workspace adds, like train.c:372
+    ws = torch.empty(big, dtype=torch.uint8, device="cuda")
+    acc = [torch.ones_like(qd) for _ in range(3)]
+    A.bwd_ex(shape, A.F32, gd.data_ptr(), qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), o.data_ptr(), lse.data_ptr(),
+             acc[0].data_ptr(), acc[1].data_ptr(), acc[2].data_ptr(), 1, ws.data_ptr(), big, 0)
+    torch.cuda.synchronize()
+    for got, want in zip(acc, (rq, rk, rv)):
+        assert rel_err(host(got) - 1.0, want) < F32_TOL
+
+
 @pytest.mark.parametrize("B,H,T,d", [(1, 2, 1536, 128), (2, 3, 100, 128), (1, 2, 40, 64)])
 def test_drop_in_lse_only_probs(A, B, H, T, d):
     """ATTN_PROBS_LSE: `probs` shrinks to B*H*T floats and `scratch` to the
