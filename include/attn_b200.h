@@ -142,7 +142,10 @@ typedef struct {
 
 /* Causal forward O = softmax(Q K^T / sqrt(d)) V per (b, h), rows j <= i.
  * dtype ATTN_F32: fp32 in/out, fp32 arithmetic (train.c:339-370 semantics).
- * dtype ATTN_BF16: bf16 in/out, tensor-core products, fp32 softmax.
+ * dtype ATTN_BF16: bf16 in/out, tensor-core products, fp32 softmax.  At head
+ * dims 32, 96 and 128 a bf16 call keeps fp32 copies of its tensors (4*B*T*H*d
+ * floats) in a library-owned device buffer, grown on demand; such calls must
+ * not overlap on the GPU.
  * lse (may be NULL): B*H*T floats, [b][h][t] = max + log(sum) of the scaled
  * scores of row t -- the statistic the backward recomputes P from. */
 ATTN_API int attn_fwd_ex(const attn_shape *s, int dtype,
