@@ -276,7 +276,13 @@ split_rows_kernel(const float *__restrict__ src, float *__restrict__ dh, float *
 constexpr int kSgCols = 64;                        // keys per half tile
 constexpr int kSgLd = kSgCols + 1;                 // padded shared row (odd: conflict-free columns)
 constexpr int kSgThreads = 512;
-__global__ void __launch_bounds__(kSgThreads)
+constexpr int kSgIters = BM * (kSgCols / 4) / kSgThreads;   // float4 of a half tile per thread and operand
+static_assert(kSgThreads == 32 * (kSgCols / 4) && kSgIters * 32 == BM, "thread t: rows t/16 + 32 it, keys 4 (t % 16)");
+static_assert(kSgThreads / 32 * 4 == kSgCols && BM == 4 * 32, "mirror: warp w columns 4w..4w+3, lane rows l + 32 m");
+// Two CTAs per SM at 64 registers: at the trainer shape this ran faster than three CTAs
+// at 40 registers with spills, and than rows of 4 x 128 bytes (conflict-free shared stores)
+// in place of 2 x 256.
+__global__ void __launch_bounds__(kSgThreads, 2)
 scores_to_grads_kernel(float *__restrict__ buf1, float *__restrict__ buf2, const float *__restrict__ lse2,
                        const float *__restrict__ dvec, float *__restrict__ ds, int T, int mt, float qk_scale,
                        float ds_scale)
@@ -302,48 +308,59 @@ scores_to_grads_kernel(float *__restrict__ buf1, float *__restrict__ buf2, const
     }
     for (int hh = diag ? 0 : (rem & 1); hh < (diag ? 2 : (rem & 1) + 1); hh++) {
         const int j0 = kt * BN + hh * kSgCols;
-        __syncthreads();                               // (the previous half's shared tiles are free)
-        // 128 rows x 64 keys as 16 float4 per row (T % 4 == 0: a float4 is all in or all out)
-        for (int idx = threadIdx.x; idx < BM * (kSgCols / 4); idx += kSgThreads) {
-            const int a = idx >> 4, c = (idx & 15) * 4, i = i0 + a, j = j0 + c;
-            float4 x = make_float4(0.f, 0.f, 0.f, 0.f), y = x;
+        // 128 rows x 64 keys as 16 float4 per row (T % 4 == 0: a float4 is all in or all out);
+        // thread t takes rows t/16 + 32 it, keys 4 (t % 16) .. +3, and issues all its loads of
+        // the half before it uses any
+        const int a0 = threadIdx.x >> 4, c = (threadIdx.x & 15) * 4, j = j0 + c;
+        const long long off0 = base + (long long)(i0 + a0) * T + j;
+        float4 xr[kSgIters], yr[kSgIters];
+#pragma unroll
+        for (int it = 0; it < kSgIters; it++) {
+            const int i = i0 + a0 + 32 * it;
+            const long long off = off0 + (long long)(32 * it) * T;
+            xr[it] = make_float4(0.f, 0.f, 0.f, 0.f);
+            yr[it] = xr[it];
             if (i < T && j < T && j <= i + 3) {        // (a float4 wholly above the diagonal is not read)
-                x = *reinterpret_cast<const float4 *>(buf1 + base + (long long)i * T + j);
-                y = *reinterpret_cast<const float4 *>(buf2 + base + (long long)i * T + j);
+                xr[it] = *reinterpret_cast<const float4 *>(buf1 + off);
+                yr[it] = *reinterpret_cast<const float4 *>(buf2 + off);
             }
+        }
+        __syncthreads();                               // (row statistics loaded; the previous half's tiles free)
+        // P and dS in registers (over the loaded values); dS (rows i) straight to `ds`, both into
+        // shared memory for the mirror
+#pragma unroll
+        for (int it = 0; it < kSgIters; it++) {
+            const int a = a0 + 32 * it, i = i0 + a;
+            const float la = rl[a], da = rd[a];
             float *px = sx + a * kSgLd + c, *py = sy + a * kSgLd + c;
-            px[0] = x.x; px[1] = x.y; px[2] = x.z; px[3] = x.w;
-            py[0] = y.x; py[1] = y.y; py[2] = y.z; py[3] = y.w;
+            auto grad = [&](float &x, float &y, int e) {
+                const bool live = i < T && j + e <= i;
+                x = live ? exp2f(x * qk_scale - la) : 0.f;
+                y = live ? x * (y - da) * ds_scale : 0.f;
+                px[e] = x;
+                py[e] = y;
+            };
+            grad(xr[it].x, yr[it].x, 0);
+            grad(xr[it].y, yr[it].y, 1);
+            grad(xr[it].z, yr[it].z, 2);
+            grad(xr[it].w, yr[it].w, 3);
+            if (i < T && j < T)
+                *reinterpret_cast<float4 *>(ds + off0 + (long long)(32 * it) * T) = yr[it];
         }
         __syncthreads();
-        for (int idx = threadIdx.x; idx < BM * kSgCols; idx += kSgThreads) {
-            const int a = idx >> 6, c = idx & 63, i = i0 + a, j = j0 + c;
-            float pv = 0.f, dv = 0.f;
-            if (i < T && j < T && j <= i) {
-                pv = exp2f(sx[a * kSgLd + c] * qk_scale - rl[a]);
-                dv = pv * (sy[a * kSgLd + c] - rd[a]) * ds_scale;
-            }
-            sx[a * kSgLd + c] = pv;
-            sy[a * kSgLd + c] = dv;
-        }
-        __syncthreads();
-        for (int idx = threadIdx.x; idx < BM * (kSgCols / 4); idx += kSgThreads) {
-            const int a = idx >> 4, c = (idx & 15) * 4;   // dS, rows i
-            const int i = i0 + a, j = j0 + c;
-            if (i < T && j < T) {
-                const float *py = sy + a * kSgLd + c;
-                *reinterpret_cast<float4 *>(ds + base + (long long)i * T + j) = make_float4(py[0], py[1], py[2], py[3]);
-            }
-        }
-        for (int idx = threadIdx.x; idx < kSgCols * (BM / 4); idx += kSgThreads) {
-            const int c = idx >> 5, a = (idx & 31) * 4;   // P^T and dS^T, rows j: column c of the tiles
-            const int i = i0 + a, j = j0 + c;
-            if (i < T && j < T) {
-                const float *px = sx + a * kSgLd + c, *py = sy + a * kSgLd + c;
-                *reinterpret_cast<float4 *>(buf1 + base + (long long)j * T + i) =
-                    make_float4(px[0], px[kSgLd], px[2 * kSgLd], px[3 * kSgLd]);
-                *reinterpret_cast<float4 *>(buf2 + base + (long long)j * T + i) =
-                    make_float4(py[0], py[kSgLd], py[2 * kSgLd], py[3 * kSgLd]);
+        // P^T and dS^T (rows j): warp w writes columns 4w .. 4w+3 of the tiles, lane l rows
+        // l + 32 m (conflict-free shared reads, 128-byte rows of the mirror per instruction)
+        {
+            const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+#pragma unroll
+            for (int k = 0; k < 16; k++) {
+                const int cc = 4 * w + (k >> 2), a = l + 32 * (k & 3);
+                const int i = i0 + a, jj = j0 + cc;
+                if (i < T && jj < T) {
+                    const long long o = base + (long long)jj * T + i;
+                    buf1[o] = sx[a * kSgLd + cc];
+                    buf2[o] = sy[a * kSgLd + cc];
+                }
             }
         }
     }
@@ -866,7 +883,7 @@ int launch_bwd_tc(int D, const float *dout, const float *q, const float *k, cons
         (st = launch_gemm_mode(3, mo_, mvh, mvl, mb2s, T, H, D, BH, err, s)))        // Y = dO V^T
         return st;
     const int mt = (T + BM - 1) / BM;
-    const size_t sg_smem = (size_t)2 * BM * kSgLd * sizeof(float);     // 65 KB: three CTAs per SM
+    const size_t sg_smem = (size_t)2 * BM * kSgLd * sizeof(float);     // 65 KB (two CTAs per SM)
     if (!ensure_smem_attr((const void *)scores_to_grads_kernel, sg_smem))
         return set_error(ATTN_ERR_CUDA, "tensor-core backward: cannot set shared-memory size");
     if ((st = check_pdl(launch_pdl(scores_to_grads_kernel, dim3(mt * mt, (unsigned)BH), dim3(kSgThreads), sg_smem,
