@@ -358,9 +358,9 @@ class Workload:
                 self.scratch = torch.empty(Bl * Hl * T * T, device=dev)
                 self.work *= 3
                 self.total_work *= 3
-                # forward; backward at d 96/128 on the tensor cores: row statistics, 2 row
-                # splits, 3 transposed splits, 2 score GEMMs, P/dS, dQ/dV/dK GEMMs
-                self.launches = 13 if d in (96, 128) and T % 4 == 0 else 4
+                # forward; backward at d 96/128 on the tensor cores: row statistics, the
+                # operand splits, 2 score GEMMs, P/dS, dQ/dV/dK GEMMs
+                self.launches = 9 if d in (96, 128) and T % 4 == 0 else 4
                 self.in_names = ["q", "k", "v", "do"]
                 self.out_names = ["o", "dq", "dk", "dv"]
             if kind == "bwd":

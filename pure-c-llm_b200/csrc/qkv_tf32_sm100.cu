@@ -210,24 +210,42 @@ qkv_split_w_kernel(const float *__restrict__ w0, const float *__restrict__ w1, c
     }
 }
 
-// K of every (batch, head) -> rows [bh*D, (bh+1)*D) of K^T high and low
-// (B*H*D x Tp), the B operand of dQ = dS K.  K is in the activation layout:
-// row b*T + j, columns h*D .. h*D + D - 1, rows in_stride floats apart.
+// The operand splits of the backward GEMMs in one launch, over 32 x 32 tiles
+// (rows j, head columns n) of every (batch, head) of a tensor in the activation
+// layout (row b*T + j, columns h*D .. h*D + D - 1, rows in_stride floats
+// apart).  Tensor z is written split by rows, [bh][T][D] high and low (the
+// K-major B operands of the score GEMMs), where rh[z] is set, and transposed and
+// split, [bh][D][Tp] (the B operands of dQ = dS K, dV = P^T dO, dK = dS^T Q),
+// where th[z] is set: K both ways, Q and dO transposed, V by rows.
+struct SplitOperands {
+    const float *src[4];
+    float *rh[4], *rl[4], *th[4], *tl[4];
+};
 __global__ void __launch_bounds__(256)
-split_kt_kernel(const float *__restrict__ k, float *__restrict__ kth, float *__restrict__ ktl, long long in_stride,
-                int T, int H, int D, long long Tp)
+split_operands_kernel(const __grid_constant__ SplitOperands a, long long in_stride, int T, int H, int D, long long Tp)
 {
     pdl_begin();   // launched by launch_pdl
     __shared__ float tile[32][33];
-    const int bh = blockIdx.z;
-    const float *src = k + (long long)(bh / H) * T * in_stride + (long long)(bh % H) * D;
-    const int n0 = blockIdx.x * 32, j0 = blockIdx.y * 32;
+    const int z = blockIdx.z, bh = blockIdx.y;
+    const int ntn = (D + 31) / 32;
+    const int n0 = (int)(blockIdx.x % ntn) * 32, j0 = (int)(blockIdx.x / ntn) * 32;
+    const float *src = a.src[z] + (long long)(bh / H) * T * in_stride + (long long)(bh % H) * D;
+    float *rh = a.rh[z], *rl = a.rl[z], *th = a.th[z], *tl = a.tl[z];
     const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
 #pragma unroll
     for (int i = 0; i < 4; i++) {
         const int j = j0 + ty + 8 * i, n = n0 + tx;
-        tile[ty + 8 * i][tx] = (j < T && n < D) ? __ldg(src + (long long)j * in_stride + n) : 0.f;
+        const bool in = j < T && n < D;
+        const float x = in ? __ldg(src + (long long)j * in_stride + n) : 0.f;
+        tile[ty + 8 * i][tx] = x;
+        if (rh != nullptr && in) {
+            const float hh = hi_part(x);
+            const long long o = ((long long)bh * T + j) * D + n;
+            rh[o] = hh;
+            rl[o] = x - hh;
+        }
     }
+    if (th == nullptr) return;                       // (the whole block: z is uniform)
     __syncthreads();
 #pragma unroll
     for (int i = 0; i < 4; i++) {
@@ -235,30 +253,9 @@ split_kt_kernel(const float *__restrict__ k, float *__restrict__ kth, float *__r
         if (n < D && j < T) {
             const float x = tile[tx][ty + 8 * i], hh = hi_part(x);
             const long long o = ((long long)bh * D + n) * Tp + j;
-            kth[o] = hh;
-            ktl[o] = x - hh;
+            th[o] = hh;
+            tl[o] = x - hh;
         }
-    }
-}
-
-// K or V of every (batch, head), split by rows: [bh][T][D] high and low (the
-// B operand of the score GEMMs, K-major along d as it is in memory).
-__global__ void __launch_bounds__(256)
-split_rows_kernel(const float *__restrict__ src, float *__restrict__ dh, float *__restrict__ dl, long long in_stride,
-                  int T, int H, int D, long long total4)
-{
-    pdl_begin();   // launched by launch_pdl
-    const int d4 = D / 4;
-    for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < total4;
-         e += (long long)gridDim.x * blockDim.x) {
-        const long long row = e / d4;              // bh * T + j
-        const int c = (int)(e % d4) * 4;
-        const int bh = (int)(row / T), j = (int)(row % T);
-        const float4 x = __ldg(reinterpret_cast<const float4 *>(
-            src + ((long long)(bh / H) * T + j) * in_stride + (long long)(bh % H) * D + c));
-        const float4 h = make_float4(hi_part(x.x), hi_part(x.y), hi_part(x.z), hi_part(x.w));
-        *reinterpret_cast<float4 *>(dh + row * D + c) = h;
-        *reinterpret_cast<float4 *>(dl + row * D + c) = make_float4(x.x - h.x, x.y - h.y, x.z - h.z, x.w - h.w);
     }
 }
 
@@ -841,20 +838,15 @@ int launch_bwd_tc(int D, const float *dout, const float *q, const float *k, cons
     const float qk_scale = attn::kLog2e / sqrtf((float)D), ds_scale = 1.0f / sqrtf((float)D);
     int st = launch_bwd_rowdot(ATTN_F32, D, o, dout, lse, stats, in_stride, out_stride, B, H, T, s);
     if (st) return st;
-    const long long total4 = BH * T * D / 4;
-    const int rgrid = (int)std::min<long long>((total4 + 255) / 256, 4L * sm_count_here());
-    if ((st = check_pdl(launch_pdl(split_rows_kernel, dim3(rgrid), dim3(256), 0, s, k, krh, krl, in_stride, T, H, D,
-                                   total4), "split K rows")) ||
-        (st = check_pdl(launch_pdl(split_rows_kernel, dim3(rgrid), dim3(256), 0, s, v, vrh, vrl, in_stride, T, H, D,
-                                   total4), "split V rows")))
+    SplitOperands so = {};
+    so.src[0] = k, so.rh[0] = krh, so.rl[0] = krl, so.th[0] = kth, so.tl[0] = ktl;
+    so.src[1] = q, so.th[1] = qth, so.tl[1] = qtl;
+    so.src[2] = dout, so.th[2] = oth, so.tl[2] = otl;
+    so.src[3] = v, so.rh[3] = vrh, so.rl[3] = vrl;
+    const dim3 sgrid((unsigned)(((D + 31) / 32) * ((T + 31) / 32)), (unsigned)BH, 4);
+    if ((st = check_pdl(launch_pdl(split_operands_kernel, sgrid, dim3(256), 0, s, so, in_stride, T, H, D, Tp),
+                        "split the operands")))
         return st;
-    const dim3 tgrid((D + 31) / 32, (T + 31) / 32, (unsigned)BH);
-    const float *srcs[3] = {k, q, dout};
-    float *his[3] = {kth, qth, oth}, *los[3] = {ktl, qtl, otl};
-    for (int i = 0; i < 3; i++)
-        if ((st = check_pdl(launch_pdl(split_kt_kernel, tgrid, dim3(256), 0, s, srcs[i], his[i], los[i], in_stride, T,
-                                       H, D, Tp), "split and transpose")))
-            return st;
     CUtensorMap mq, mo_, mkh, mkl, mvh, mvl, mb1, mb2, mds, mkth, mktl, mqth, mqtl, moth, motl, ydq, ydk, ydv;
     bool okm = map_3d(&mq, q, (long long)H * D, T, B, in_stride, (long long)T * in_stride, BK, BM) &&
                map_3d(&mo_, dout, (long long)H * D, T, B, in_stride, (long long)T * in_stride, BK, BM) &&
